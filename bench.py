@@ -1,0 +1,318 @@
+"""Benchmark of the sparse decode hot path (select + attend per layer) at 32K.
+
+Contract: ``python bench.py --gpus N --steps K --warmup W`` prints ONE JSON line
+on rank 0.  A step is one decode token through L=36 independent layer states
+(Qwen3-4B attention geometry: 32 query / 8 KV heads, head_dim 128, bf16), each
+holding a 32768-token history (64-token blocks, r=4 reps, Top-32, sink 64,
+recent 512) resident in HBM.  Per layer the step runs kernel (1) (score +
+Top-K) and kernel (2) (fused gather-attend).  The 36 layer states together
+hold ~2.7 GB and a step touches ~540 MB, more than L2 (126 MB), so no L2 flush
+is needed between steps.  Inputs are synthetic (seeded N(0,1)).
+
+Metric: device time per layer decode, whole job: step_time / (L * n_gpus) in
+microseconds (lower is better).  With N GPUs each rank decodes its own
+independent sequence (replicas; weak scaling, no collective on the data path).
+
+``--impl reference`` times the reference algorithm's CPU implementation (the
+oracle port of m12_runtime.py's torch path) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+PKG = "nano-vllm-kv-optimizer_b200"
+
+HQ, HKV, D, B, R_REPS = 32, 8, 128, 64, 4
+TOPK, SINK, RECENT = 32, 64, 512
+CTX = 32768
+LAYERS = 36
+METRIC = "sparse decode attn us/layer @32K ctx"
+UNIT = "us/layer"
+
+# algorithmic bytes per layer decode (unit of the roofline)
+ATTEND_TOKENS = TOPK * B + SINK + RECENT                 # 2624 keys per kv head
+ATTEND_BYTES = ATTEND_TOKENS * HKV * D * 2 * 2 + (HQ * D * 2) * 2 + HKV * D * 2 * 2
+SELECT_BYTES = (CTX // B) * HKV * R_REPS * D * 2 + HQ * D * 2
+STEP_BYTES = ATTEND_BYTES + SELECT_BYTES
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, index):
+        self.proc = None
+        self.index = index
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={index}",
+                 "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 7:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = float(f[1])
+            except ValueError:
+                continue
+            for n, val in zip(names, f[3:7]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def build_layers(nkv, dev, n_layers, seed):
+    """L layer runtimes, each with a 32K-token random history stored by kernel (5)."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    layers = []
+    for li in range(n_layers):
+        rt = nkv.M12LayerRuntime(li, nkv.M12Config(max_model_len=CTX + 4096, device=dev))
+        rt.reserve_blocks(CTX // B)
+        for c in range(CTX // 4096):
+            k = torch.randn(4096, HKV, D, generator=g, device=dev).bfloat16()
+            v = torch.randn(4096, HKV, D, generator=g, device=dev).bfloat16()
+            if c == 0:
+                rt.prefill_first(None, k, v)
+            else:
+                rt._store_kv(k, v)
+        layers.append(rt)
+    torch.cuda.synchronize()
+    return layers
+
+
+def cpu_reference(steps, warmup, threads):
+    """The reference algorithm's CPU path (oracle port) on one 32K layer state."""
+    from oracle import m12_oracle as orc
+
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(7)
+    layer = orc.OracleLayer(orc.OracleConfig())
+    for _ in range(CTX // 4096):
+        k = torch.randn(4096, HKV, D, generator=g).bfloat16()
+        v = torch.randn(4096, HKV, D, generator=g).bfloat16()
+        layer.store(k, v)
+    times = []
+    for i in range(warmup + steps):
+        q = torch.randn(1, HQ, D, generator=g).bfloat16()
+        k = torch.randn(1, HKV, D, generator=g).bfloat16()
+        v = torch.randn(1, HKV, D, generator=g).bfloat16()
+        t = time.perf_counter()
+        layer.decode(q, k, v)
+        dt = time.perf_counter() - t
+        if i >= warmup:
+            times.append(dt)
+    return statistics.median(times) * 1e6, len(times)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="nkv", choices=["nkv", "reference"])
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--cpu-steps", type=int, default=20)
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    threads = os.cpu_count() or 1
+
+    config = {"workload": "single-layer sparse decode (select+attend) @32K history, 36 layer states",
+              "model": "Qwen3-4B attention geometry (32q/8kv, d128)", "context": CTX,
+              "block": B, "reps": R_REPS, "top_k": TOPK, "sink": SINK, "recent": RECENT,
+              "layers_per_step": args.layers, "global_batch": world, "seq_len": CTX,
+              "parallelism": f"replicas{world}",
+              "l2": "step touches ~540 MB of distinct KV/reps (> 126 MB L2); no flush"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        us, n = cpu_reference(max(3, args.steps if args.steps < 30 else 20), max(3, args.warmup),
+                              threads)
+        line = {"impl": "reference", "metric": METRIC, "value": us, "unit": UNIT, "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": us * args.layers / 1000.0,
+                "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic", "config": config,
+                "cpu_baseline": {"value": us, "unit": UNIT, "cores": threads, "kind": "port",
+                                 "sample": f"{n} decode calls of one 32K layer state (median)"},
+                "e2e": {"value": us, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    nkv = __import__("importlib").import_module(PKG)
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120))
+    dev = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(dev)
+    L = args.layers
+    layers = build_layers(nkv, dev, L, seed=1234 + rank)
+
+    gq = torch.Generator(device=dev).manual_seed(99 + rank)
+    qs = torch.randn(L, 1, HQ, D, generator=gq, device=dev).bfloat16()
+    ks = torch.randn(L, 1, HKV, D, generator=gq, device=dev).bfloat16()
+    vs = torch.randn(L, 1, HKV, D, generator=gq, device=dev).bfloat16()
+
+    stream = torch.cuda.Stream(dev)
+    # warm the kernels once eagerly (workspace allocation happens here)
+    with torch.cuda.stream(stream):
+        for li, rt in enumerate(layers):
+            rt.decode(qs[li], ks[li], vs[li], dev)
+    stream.synchronize()
+    attend_cfg = nkv._lib.attend_last_config()
+
+    # whole step (select + attend for every layer) captured in one CUDA graph
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for li, rt in enumerate(layers):
+            rt.decode(qs[li], ks[li], vs[li], dev)
+    # kernel (2) alone over the same ids, for the roofline of the dominant kernel
+    ids_saved = [rt._ids[:TOPK].clone() for rt in layers]
+    g_att = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_att, stream=stream):
+        for li, rt in enumerate(layers):
+            sink_len = min(SINK, rt.valid_len)
+            w, start, n, _ = nkv.m12_runtime.ring_decode_plan(rt._ring_head, rt.valid_len, RECENT)
+            rt._attend(qs[li], ids_saved[li], TOPK, sink_len, start, n, ks[li], vs[li],
+                       ring_write_pos=w)
+
+    def timed(g, iters):
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(iters):
+                g.replay()
+            ev1.record(stream)
+        ev1.synchronize()
+        return ev0.elapsed_time(ev1)
+
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk = Clocks(local) if rank == 0 else None
+    ms = timed(graph, args.steps)
+    torch.cuda.synchronize()
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    clocks = clk.stop() if clk else None
+    ms_per_step = ms / args.steps
+    value = ms_per_step * 1000.0 / (L * world)
+
+    # dominant kernel (attend) timed alone
+    for _ in range(3):
+        g_att.replay()
+    att_ms = timed(g_att, args.steps) / args.steps
+    att_us = att_ms * 1000.0 / L
+    peak, peak_kind = peaks()
+    achieved = ATTEND_BYTES / (att_us * 1e-6) / 1e9
+    step_gbs = STEP_BYTES / (ms_per_step * 1000.0 / L * 1e-6) / 1e9
+
+    # end to end through the public API: pinned host q/k/v -> device, eager
+    # rt.decode per layer, output back to pinned host memory
+    hq = torch.randn(L, 1, HQ, D).bfloat16().pin_memory()
+    hk = torch.randn(L, 1, HKV, D).bfloat16().pin_memory()
+    hv = torch.randn(L, 1, HKV, D).bfloat16().pin_memory()
+    ho = torch.empty(L, 1, HQ, D, dtype=torch.bfloat16).pin_memory()
+    e2e_steps = max(3, min(args.steps, 20))
+    with torch.cuda.stream(stream):
+        def e2e_step():
+            for li, rt in enumerate(layers):
+                q = hq[li].to(dev, non_blocking=True)
+                k = hk[li].to(dev, non_blocking=True)
+                v = hv[li].to(dev, non_blocking=True)
+                o = rt.decode(q, k, v, dev)
+                ho[li].copy_(o, non_blocking=True)
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        e1.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = e2e_ms * 1000.0 / (L * world)
+
+    line = None
+    if rank == 0:
+        cpu_us, n_cpu = cpu_reference(args.cpu_steps, 3, threads)
+        line = {
+            "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) K/V/Q)", "config": config,
+            "step_hbm_gbs": round(step_gbs, 1),
+            "roofline": {"bound": "hbm", "kernel": "nkv attend (kernel 2)",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "us_per_launch": round(att_us, 3), "bytes_per_launch": ATTEND_BYTES,
+                         "traffic": None},
+            "cpu_baseline": {"value": round(cpu_us, 1), "unit": UNIT, "cores": threads,
+                             "kind": "port",
+                             "sample": f"{n_cpu} decode calls of one 32K layer state (median)"},
+            "e2e": {"value": round(e2e_value, 4), "unit": UNIT,
+                    "h2d_bytes_per_step": L * (HQ + 2 * HKV) * D * 2,
+                    "d2h_bytes_per_step": L * HQ * D * 2},
+            "gpu_launches": 2 * L * args.steps,
+            "attend_launch": {"cluster": attend_cfg[0], "splits_per_head": attend_cfg[1],
+                              "keys_per_cta": attend_cfg[2]},
+            "clocks": clocks,
+        }
+        print(json.dumps(line))
+    del graph, g_att
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,234 @@
+/*
+ * nanokv.h — C ABI of the NanoKV block-sparse attention path on B200 (sm_100a).
+ *
+ * Plain pointers and sizes only: every tensor argument is a device pointer (or a
+ * host pointer that is mapped into the device address space, where stated) plus
+ * its shape/stride integers.  Every entry point is asynchronous on the given
+ * CUDA stream, returns NKV_OK or a negative status, and leaves a message for
+ * nkv_last_error() on failure.  No entry point allocates device memory: the
+ * caller passes a workspace sized by the matching *_workspace_bytes() query.
+ *
+ * Geometry supported by the kernels: head_dim 128, bf16 activations, query heads
+ * per KV head G in {1, 2, 4, 8}, block_size in {16, 32, 64, 128}, r <= 8.
+ * Anything else returns NKV_ERR_UNSUPPORTED (there is no fallback path).
+ *
+ * Each declaration names the reference interface it replaces
+ * (Tao20060602/nano-vllm-kv-optimizer, path:line).
+ */
+#ifndef NANOKV_H
+#define NANOKV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NKV_OK 0
+#define NKV_ERR_ARG (-1)         /* bad shape, pointer or size                        */
+#define NKV_ERR_UNSUPPORTED (-2) /* geometry outside what the kernels are built for   */
+#define NKV_ERR_CUDA (-3)        /* a CUDA call or launch failed                      */
+#define NKV_ERR_DEVICE (-4)      /* a kernel recorded an error word (see nkv_check)   */
+
+/* History storage kinds for the selected-block segment. */
+#define NKV_STORE_BF16 0        /* bf16 [max_blocks][Hkv][B][D]                          */
+#define NKV_STORE_INT8_REF 1    /* int8 store, K scale [Hkv][D], V scale [max_blocks][Hkv] */
+#define NKV_STORE_INT8_TOKEN 2  /* int8 store, bf16 scale per (block, head, token) for K and V */
+
+typedef void* nkv_stream_t; /* a cudaStream_t */
+
+const char* nkv_last_error(void);
+int nkv_version(void);
+
+/* Device address of pinned host memory (cudaHostGetDevicePointer); fails unless
+ * the range is mapped.  The offload mode passes such addresses as k_store /
+ * v_store.  Replaces nothing in the reference (whose host history is pageable
+ * and gathered on the CPU, m12_runtime.py:1213-1238). */
+int nkv_map_host(void* host_ptr, void** dev_ptr);
+
+/* Reads the 32-bit error word kernels write into a workspace (bounded waits,
+ * out-of-range ids).  Synchronous: copies 4 bytes device->host on `stream`.
+ * Returns NKV_OK when clear, NKV_ERR_DEVICE (and clears it) otherwise. */
+int nkv_check(nkv_stream_t stream, void* workspace);
+
+/* ------------------------------------------------------------------------ */
+/* (1) Block-representative scoring + protection mask + exact Top-K.
+ *
+ * Replaces M12LayerRuntime._gpu_select (nanovllm/sparse/m12_runtime.py:959-1055)
+ * and the Triton fused_block_scores (nanovllm/sparse/fused_select.py:57-79).
+ *
+ * score[b] = max over query rows n < nq, query heads h < hq, reps j < r of
+ *            fp32(q[n][h]) . fp32(reps[h / G][b][j])          (G = hq / hkv)
+ * Blocks listed in protected_ids (ids >= nblocks are ignored) score -inf.
+ * Writes the k best block ids to out_ids (int64, ordered by score descending,
+ * equal scores by ascending id) and, when non-NULL, their scores to
+ * out_topk_scores and the masked per-block scores to out_block_scores.
+ * q: bf16 rows with the given strides (elements), head_dim contiguous.
+ * reps: bf16 [hkv][max_blocks][r][head_dim].  1 <= k <= min(nblocks, 256).  */
+size_t nkv_select_workspace_bytes(int max_blocks, int nq);
+int nkv_select(nkv_stream_t stream, const void* q, int nq, int64_t q_row_stride,
+               int64_t q_head_stride, int hq, int hkv, int head_dim, const void* reps, int r,
+               int max_blocks, int nblocks, const int32_t* protected_ids, int n_protected, int k,
+               int64_t* out_ids, float* out_topk_scores, float* out_block_scores, void* workspace,
+               size_t workspace_bytes);
+
+/* Lossless-verify selection: a separate Top-K per query row, their sorted
+ * union and the per-row allowed mask.
+ * Replaces M12LayerRuntime._gpu_select_per_query (m12_runtime.py:1057-1087).
+ * out_union: int64 [nq * k] (first *out_count valid, ascending);
+ * out_count: int32 device scalar; out_allowed: uint8 [nq][nq * k]. nq <= 8. */
+int nkv_select_per_query(nkv_stream_t stream, const void* q, int nq, int64_t q_row_stride,
+                         int64_t q_head_stride, int hq, int hkv, int head_dim, const void* reps,
+                         int r, int max_blocks, int nblocks, const int32_t* protected_ids,
+                         int n_protected, int k, int64_t* out_union, int32_t* out_count,
+                         uint8_t* out_allowed, float* out_scores, void* workspace,
+                         size_t workspace_bytes);
+
+/* ------------------------------------------------------------------------ */
+/* (2)+(3) Fused gather-and-attend GQA attention over the sparse key set.
+ *
+ * Replaces the decode gather/pack + packed attention of M12LayerRuntime.decode
+ * (m12_runtime.py:1164-1320, _fused_attention fast path :868-873), the int8
+ * dequant-and-pack (fused_dequant.py:47-63, m12_runtime.py:1243-1278) and the
+ * verify attention of verify_tokens (m12_runtime.py:716-760, masked path
+ * :875-896).  Keys are read in place from four segments, in this order:
+ *   0. selected history blocks  block_ids[0..n_sel) of the block store
+ *   1. sink window              sink[h][0..sink_len)
+ *   2. recent ring slice        ring[h][(ring_start + i) % ring_cap], i < ring_len
+ *   3. current tokens           cur[j], j < n_cur (0 or nq): query n sees j <= n
+ * With allowed != NULL, query n sees block_ids[u] only if allowed[n][u] != 0.
+ * ring_write_pos >= 0 additionally stores current token 0 into that ring slot
+ * (the decode recent-window append).  Works for nq <= 8. */
+typedef struct nkv_attend_args {
+  const void* q; /* bf16 [nq][hq][head_dim] */
+  int64_t q_row_stride, q_head_stride;
+  int nq, hq, hkv, head_dim, block_size;
+  float scale;
+  /* segment 0 */
+  const int64_t* block_ids; /* device int64 [n_sel] */
+  int n_sel;
+  int max_blocks;           /* bound for block ids (store capacity)          */
+  int store_kind;           /* NKV_STORE_*                                   */
+  const void* k_store;      /* [max_blocks][hkv][B][D]; may be host-mapped   */
+  const void* v_store;
+  const float* k_chan_scale;  /* NKV_STORE_INT8_REF: [hkv][D]             */
+  const float* v_block_scale; /* NKV_STORE_INT8_REF: [max_blocks][hkv]    */
+  const void* k_tok_scale;    /* NKV_STORE_INT8_TOKEN: bf16 [max_blocks][hkv][B] */
+  const void* v_tok_scale;
+  const uint8_t* allowed; /* optional [nq][allowed_stride] */
+  int allowed_stride;
+  /* segment 1 */
+  const void* sink_k;
+  const void* sink_v; /* bf16 [hkv][sink_cap][D] */
+  int sink_cap, sink_len;
+  /* segment 2 */
+  void* ring_k;
+  void* ring_v; /* bf16 [hkv][ring_cap][D] */
+  int ring_cap, ring_start, ring_len;
+  /* segment 3 */
+  const void* cur_k;
+  const void* cur_v; /* bf16 rows [n_cur][hkv][D] with strides */
+  int64_t cur_row_stride, cur_head_stride;
+  int n_cur;
+  int ring_write_pos;
+  /* output */
+  void* out; /* bf16 [nq][hq][D] */
+  int64_t out_row_stride, out_head_stride;
+  void* workspace;
+  size_t workspace_bytes;
+  /* 1: the kernel launched just before on this stream is the nkv_select that
+   * writes block_ids, and every other input was complete before that launch.
+   * The attend kernel then starts while the selection runs (programmatic
+   * dependent launch) and waits for it only before reading block_ids. */
+  int overlap_select;
+} nkv_attend_args;
+
+/* max_tokens bounds n_sel * block_size + sink_len + ring_len + n_cur. */
+size_t nkv_attend_workspace_bytes(int hkv, int hq, int nq, int max_tokens);
+int nkv_attend(nkv_stream_t stream, const nkv_attend_args* args);
+/* Launch shape chosen by the last nkv_attend on the calling thread: whether the
+ * splits of a head were merged inside a thread-block cluster, the number of
+ * splits per head and the keys per CTA.  Host only (no GPU work). */
+int nkv_attend_last_config(int* cluster, int* splits, int* keys_per_cta);
+
+/* ------------------------------------------------------------------------ */
+/* (4) Segmented prefill attention on tcgen05/TMEM: the same four segments as
+ * nkv_attend for a whole chunk of nq queries (nq == n_cur, causal in-chunk,
+ * bottom-right aligned), without packing.
+ * Replaces prefill_chunk's pack + _prefill_attention (m12_runtime.py:589-642,
+ * 809-839; FA2 flash_attn_func call :834-839) and the segmented adapter's
+ * prepare/attend contract (nanovllm/sparse/segmented_prefill_adapter.py:95-147).
+ * Requires store_kind == NKV_STORE_BF16 and allowed == NULL. */
+size_t nkv_prefill_workspace_bytes(int hkv, int hq, int nq, int max_tokens);
+int nkv_prefill(nkv_stream_t stream, const nkv_attend_args* args);
+
+/* ------------------------------------------------------------------------ */
+/* (5) KV store + representative refresh for one prefill chunk.
+ *
+ * Replaces M12LayerRuntime._store_kv (m12_runtime.py:420-513: block padding,
+ * history append, sink/recent update) and _build_reps_gpu (:354-395).
+ * Writes ceil(T / B) blocks starting at start_block (zero padded), rebuilds
+ * their r representatives (mean direction, then farthest point with the
+ * reference's clamp-at-zero criterion), copies tokens [0, sink_write) into
+ * the sink and tokens [ring_first, T) into ring slots (ring_pos0 + i) % cap.
+ * k_store == v_store == NULL rebuilds representatives only (the reference's
+ * standalone _build_reps_gpu). */
+typedef struct nkv_store_args {
+  const void* k;
+  const void* v; /* bf16 rows [T][hkv][D] with strides */
+  int64_t k_row_stride, k_head_stride, v_row_stride, v_head_stride;
+  int T, hkv, head_dim, block_size, r;
+  int start_block;
+  int max_blocks;   /* block dimension of reps / rep_index                */
+  int store_blocks; /* capacity (blocks) of the block store and its scales */
+  int store_kind;
+  void* k_store;
+  void* v_store;        /* may be host-mapped (offload)                     */
+  const float* k_chan_scale; /* INT8_REF: [hkv][D] input (see nkv_k_channel_scale) */
+  float* v_block_scale;      /* INT8_REF: [max_blocks][hkv] output             */
+  void* k_tok_scale;
+  void* v_tok_scale;    /* INT8_TOKEN: bf16 [max_blocks][hkv][B] outputs       */
+  void* reps;           /* bf16 [hkv][max_blocks][r][D]                      */
+  int16_t* rep_index;   /* optional [hkv][max_blocks][r]: chosen token       */
+  void* sink_k;
+  void* sink_v;
+  int sink_cap, sink_write;
+  void* ring_k;
+  void* ring_v;
+  int ring_cap, ring_pos0, ring_first;
+} nkv_store_args;
+
+int nkv_store_chunk(nkv_stream_t stream, const nkv_store_args* args);
+
+/* Recent-window append of T tokens: token i (i >= max(0, T - ring_cap)) goes to
+ * ring slot (ring_pos0 + i) % ring_cap of every head.  With ring_pos0 =
+ * head + min(ring_cap, valid_len) this is the reference's left-aligned window
+ * update with carry (m12_runtime.py:488-503) and commit_verified (:777-803). */
+int nkv_ring_append(nkv_stream_t stream, const void* k, const void* v, int T, int64_t k_row_stride,
+                    int64_t k_head_stride, int64_t v_row_stride, int64_t v_head_stride, int hkv,
+                    int head_dim, void* ring_k, void* ring_v, int ring_cap, int ring_pos0);
+
+/* Per-(kv head, channel) K scale of the reference int8 scheme, from one chunk:
+ * scale[h][d] = max(max_t |k[t][h][d]|, 1e-8) / 127   (m12_runtime.py:463-465). */
+int nkv_k_channel_scale(nkv_stream_t stream, const void* k, int T, int64_t row_stride,
+                        int64_t head_stride, int hkv, int head_dim, float* out_scale);
+
+/* Bf16 mean of each of nseg consecutive query segments (torch.tensor_split
+ * sizes).  Replaces prefill_query_summaries (m12_runtime.py:53-67). */
+int nkv_query_summaries(nkv_stream_t stream, const void* q, int T, int64_t row_stride,
+                        int64_t head_stride, int hq, int head_dim, int nseg, void* out);
+
+/* Dense paged-cache row scatter, the twin of the Triton store_kvcache
+ * (nanovllm/layers/attention.py:11-41): for every i with slot[i] != -1,
+ * k_cache[slot[i]][:] = key[i][:], v_cache[slot[i]][:] = value[i][:].
+ * Rows hold row_elems = num_heads * head_dim bf16 values; key/value rows are
+ * key_stride / value_stride elements apart; cache rows are row_elems apart. */
+int nkv_store_kvcache(nkv_stream_t stream, const void* key, int64_t key_stride,
+                      const void* value, int64_t value_stride, void* k_cache, void* v_cache,
+                      const int64_t* slot_mapping, int n, int row_elems);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NANOKV_H */

@@ -1,0 +1,1505 @@
+// Kernels (2)+(3): fused gather-and-attend GQA attention over the sparse key set.
+//
+// Logical keys of one KV head, in the reference's packed order
+// (m12_runtime.py:1240-1308 decode, :716-749 verify):
+//   [ selected blocks (block_ids order) | sink | recent ring slice | current ]
+// They are never packed.  The grid is (splits, hkv); CTA (s, h) owns logical
+// keys [s*tps, (s+1)*tps) of head h and
+//   1. moves them into shared memory: one cp.async.bulk per contiguous piece
+//      (a 16 KiB block-store tile is one piece) for bf16 data, or 128-bit
+//      loads + in-register dequant for an int8 store (which may live in mapped
+//      pinned host memory: the offload mode); K copies are issued before V so
+//      Q.K overlaps the V transfer,
+//   2. scores all its keys for the nq*G query rows of the head (fp32, masked:
+//      causal for current tokens, the per-row allowed mask for selected blocks),
+//   3. exponentiates against the split max and accumulates P.V,
+//   4. merges the splits with the log-sum-exp rule and writes bf16: when the
+//      splits of a head fit one thread-block cluster (<= 16 CTAs) the partials
+//      stay in shared memory and are read by the peers through DSMEM between
+//      two cluster barriers; otherwise they go to the workspace and the last
+//      CTA of the head (atomic ticket, no spinning) merges them.
+#include <cooperative_groups.h>
+#include <stdlib.h>
+
+#include "nkv_common.cuh"
+#include "nkv_host.h"
+
+namespace cg = cooperative_groups;
+
+namespace nkv {
+
+constexpr int AT_THREADS = 256;
+constexpr int AT_WARPS = AT_THREADS / 32;
+// single-query decode kernel: 16 warps hide the Q.K latency chains; G = 8 needs
+// the registers of a 256-thread launch
+template <int G> struct DK { static constexpr int THREADS = 256, WARPS = THREADS / 32; };
+constexpr int AT_TPS_MAX = 256;  // keys per CTA (K+V tiles: 128 KiB)
+constexpr int AT_MIN_TPS = 16;
+constexpr int AT_CLUSTER_MAX = 16;        // splits of one head merged through DSMEM
+constexpr int AT_TPS_MAX_CLUSTER = 384;   // keys per CTA in cluster mode (K+V: 192 KiB)
+constexpr int AT_MAX_SLOTS = 32;          // block slots one CTA can touch (tps / B + 2)
+constexpr int AT_MAX_PIECES = AT_MAX_SLOTS + 8;  // + sink, two ring pieces, current tokens
+constexpr size_t AT_SMEM_ONE_PER_SM = 116 * 1024;  // > half of the SM's 228 KiB
+
+struct AttendParams {
+  const __nv_bfloat16* q;
+  long long q_row, q_head;
+  int nq, hkv, B;
+  float scale;
+  const long long* ids;
+  int n_sel, max_blocks, kind;
+  const void* k_store;
+  const void* v_store;
+  const float* kcs;
+  const float* vbs;
+  const __nv_bfloat16* kts;
+  const __nv_bfloat16* vts;
+  const unsigned char* allowed;
+  int allowed_stride;
+  const __nv_bfloat16* sink_k;
+  const __nv_bfloat16* sink_v;
+  int sink_cap, sink_len;
+  __nv_bfloat16* ring_k;
+  __nv_bfloat16* ring_v;
+  int ring_cap, ring_start, ring_len;
+  const __nv_bfloat16* cur_k;
+  const __nv_bfloat16* cur_v;
+  long long cur_row, cur_head;
+  int n_cur, ring_write_pos;
+  __nv_bfloat16* out;
+  long long out_row, out_head;
+  float* part_o;       // [hkv][splits][nr][D]
+  float* part_ml;      // [hkv][splits][nr][2]
+  unsigned* counters;  // [hkv]
+  int* err;
+  int splits, tps, ntok, nr, nr_pad;
+  // buffer extents in elements (checked builds)
+  long long ext_store, ext_sink, ext_ring, ext_cur, ext_q, ext_out, ext_part_o, ext_part_ml;
+  int* trace;  // checked builds: per-CTA record of parameters and pieces (or null)
+  int overlap;  // 1: wait for the preceding (select) grid before touching ids
+  int cluster;  // 1: the splits of a head form one thread-block cluster (DSMEM merge)
+  int log2B;    // block_size is a power of two
+  int push;     // decode cluster merge: 1 = push to rank 0, 0 = pull by every CTA
+  int stop;     // checked builds only: end the decode kernel after phase `stop` (timing probes)
+};
+
+__device__ __forceinline__ long long clamp_id(const AttendParams& p, int slot, bool* bad) {
+  long long id = __ldg(p.ids + slot);
+  if (id < 0 || id >= p.max_blocks) {
+    *bad = true;
+    if (p.err) atomicExch(p.err, ERR_BAD_INDEX);
+    return 0;
+  }
+  *bad = false;
+  return id;
+}
+
+// Walk the contiguous pieces of logical keys [t0, t1) of head h and issue one
+// bulk copy per piece for K (which==0) or V (which==1).  Selected blocks are
+// skipped when the store is int8 (those are loaded by the threads).
+// With count_only, nothing is issued and the byte total is returned.
+// part: 0 = every piece, 1 = pieces outside the selected segment, 2 = selected only.
+__device__ uint32_t issue_bulk(const AttendParams& p, int h, int t0, int t1, __nv_bfloat16* dst,
+                               int which, uint64_t* bar, bool count_only, int part = 0) {
+  uint32_t total = 0;
+  const int B = p.B;
+  const int selEnd = p.n_sel * B, sinkEnd = selEnd + p.sink_len, ringEnd = sinkEnd + p.ring_len;
+  int pos = t0;
+  if (part == 1 && pos < selEnd) pos = min(selEnd, t1);
+  while (pos < t1) {
+    const __nv_bfloat16* src;
+    int len;
+    if (part == 2 && pos >= selEnd) break;
+    if (pos < selEnd) {
+      const int slot = pos / B, off = pos % B;
+      len = min(B - off, t1 - pos);
+      if (p.kind != NKV_STORE_BF16) { pos += len; continue; }
+      bool bad;
+      const long long id = clamp_id(p, slot, &bad);
+      const __nv_bfloat16* base = reinterpret_cast<const __nv_bfloat16*>(which ? p.v_store : p.k_store);
+      src = base + ((id * p.hkv + h) * B + off) * NKV_D;
+    } else if (pos < sinkEnd) {
+      const int off = pos - selEnd;
+      len = min(sinkEnd - pos, t1 - pos);
+      src = (which ? p.sink_v : p.sink_k) + ((long long)h * p.sink_cap + off) * NKV_D;
+    } else if (pos < ringEnd) {
+      const int i = pos - sinkEnd;
+      int phys = p.ring_start + i;            // ring_start < cap, i < ring_len <= cap
+      if (phys >= p.ring_cap) phys -= p.ring_cap;
+      const int room = p.ring_cap - phys;     // slots before the physical end
+      len = ringEnd - pos;
+      if (t1 - pos < len) len = t1 - pos;
+      if (room < len) len = room;
+      if (len < 1 || phys < 0 || phys + len > p.ring_cap) {  // never taken for valid arguments
+        if (p.err) atomicExch(p.err, ERR_BOUNDS);
+        len = 1;
+        phys = 0;
+      }
+      src = (which ? p.ring_v : p.ring_k) + ((long long)h * p.ring_cap + phys) * NKV_D;
+    } else {
+      const int j = pos - ringEnd;
+      len = 1;
+      src = (which ? p.cur_v : p.cur_k) + j * p.cur_row + h * p.cur_head;
+    }
+#ifdef NKV_CHECKED
+    {
+      long long ext, base_off;
+      if (pos < selEnd) {
+        ext = p.ext_store;
+        base_off = src - reinterpret_cast<const __nv_bfloat16*>(which ? p.v_store : p.k_store);
+      } else if (pos < sinkEnd) {
+        ext = p.ext_sink;
+        base_off = src - (which ? p.sink_v : p.sink_k);
+      } else if (pos < ringEnd) {
+        ext = p.ext_ring;
+        base_off = src - (which ? p.ring_v : p.ring_k);
+      } else {
+        ext = p.ext_cur;
+        base_off = src - (which ? p.cur_v : p.cur_k);
+      }
+      const int site = (pos < selEnd ? 10 : pos < sinkEnd ? 11 : pos < ringEnd ? 12 : 13) + 10 * which;
+      if (!NKV_INB(p.err, site, base_off, (long long)len * NKV_D, ext) ||
+          !NKV_INB(p.err, 30, (long long)(pos - t0) * NKV_D, (long long)len * NKV_D, (long long)p.tps * NKV_D)) {
+        pos += len;  // skipped: not counted, not issued
+        continue;
+      }
+    }
+#endif
+#ifdef NKV_CHECKED
+    if (p.trace && count_only && which == 0) {
+      int* tr = p.trace + (blockIdx.y * gridDim.x + blockIdx.x) * 64;
+      const int k = tr[15];
+      if (k < 12) {
+        tr[16 + 4 * k] = pos;
+        tr[17 + 4 * k] = len;
+        tr[18 + 4 * k] = (int)((src - (pos < selEnd ? reinterpret_cast<const __nv_bfloat16*>(p.k_store)
+                                   : pos < sinkEnd ? p.sink_k : pos < ringEnd ? p.ring_k : p.cur_k)) / NKV_D);
+        tr[19 + 4 * k] = pos < selEnd ? 0 : pos < sinkEnd ? 1 : pos < ringEnd ? 2 : 3;
+        tr[15] = k + 1;
+      }
+    }
+#endif
+    total += (uint32_t)len * NKV_D * 2;
+    if (!count_only) bulk_g2s(dst + (long long)(pos - t0) * NKV_D, src, (uint32_t)len * NKV_D * 2, bar);
+    pos += len;
+  }
+  return total;
+}
+
+// int8 selected keys of [t0, t1): 128-bit loads (16 values), dequant to bf16.
+__device__ void load_int8(const AttendParams& p, int h, int t0, int t1, __nv_bfloat16* ks,
+                          __nv_bfloat16* vs) {
+  const int B = p.B;
+  const int selEnd = min(p.n_sel * B, t1);
+  if (t0 >= selEnd) return;
+  const int nt = selEnd - t0;
+  const signed char* kst = reinterpret_cast<const signed char*>(p.k_store);
+  const signed char* vst = reinterpret_cast<const signed char*>(p.v_store);
+  constexpr int U = 4;
+  for (int base = threadIdx.x; base < nt * 8; base += AT_THREADS * U) {
+    uint4 kr[U], vr[U];
+    long long ids[U];
+    int rows[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * AT_THREADS;
+      rows[u] = -1;
+      if (i < nt * 8) {
+        const int t = i >> 3, c = i & 7;
+        const int pos = t0 + t, slot = pos / B, off = pos % B;
+        bool bad;
+        const long long id = clamp_id(p, slot, &bad);
+        ids[u] = id;
+        rows[u] = t * 8 + c;
+        const long long o = ((id * p.hkv + h) * B + off) * NKV_D + c * 16;
+        kr[u] = ldg_nc_v4(kst + o);
+        vr[u] = ldg_nc_v4(vst + o);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (rows[u] < 0) continue;
+      const int t = rows[u] >> 3, c = rows[u] & 7;
+      const int pos = t0 + t, off = pos % B;
+      const signed char* kb = reinterpret_cast<const signed char*>(&kr[u]);
+      const signed char* vb = reinterpret_cast<const signed char*>(&vr[u]);
+      uint32_t kw[8], vw[8];
+      if (p.kind == NKV_STORE_INT8_REF) {
+        const float vsc = __ldg(p.vbs + ids[u] * p.hkv + h);
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) {
+          const int d = c * 16 + e;
+          const float k0 = (float)kb[e] * __ldg(p.kcs + h * NKV_D + d);
+          const float k1 = (float)kb[e + 1] * __ldg(p.kcs + h * NKV_D + d + 1);
+          kw[e / 2] = (uint32_t)f2bf(k0) | ((uint32_t)f2bf(k1) << 16);
+          vw[e / 2] = (uint32_t)f2bf((float)vb[e] * vsc) | ((uint32_t)f2bf((float)vb[e + 1] * vsc) << 16);
+        }
+      } else {
+        const long long so = (ids[u] * p.hkv + h) * B + off;
+        const float ksc = __bfloat162float(p.kts[so]);
+        const float vsc = __bfloat162float(p.vts[so]);
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) {
+          kw[e / 2] = (uint32_t)f2bf((float)kb[e] * ksc) | ((uint32_t)f2bf((float)kb[e + 1] * ksc) << 16);
+          vw[e / 2] = (uint32_t)f2bf((float)vb[e] * vsc) | ((uint32_t)f2bf((float)vb[e + 1] * vsc) << 16);
+        }
+      }
+      uint4* kd = reinterpret_cast<uint4*>(ks + (long long)t * NKV_D + c * 16);
+      uint4* vd = reinterpret_cast<uint4*>(vs + (long long)t * NKV_D + c * 16);
+      kd[0] = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+      kd[1] = make_uint4(kw[4], kw[5], kw[6], kw[7]);
+      vd[0] = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+      vd[1] = make_uint4(vw[4], vw[5], vw[6], vw[7]);
+    }
+  }
+}
+
+// Same as load_int8 with a shared-memory row pitch (elements).
+__device__ void load_int8_pitched(const AttendParams& p, int h, int t0, int t1, __nv_bfloat16* ks,
+                                  __nv_bfloat16* vs, int pitch) {
+  const int B = p.B;
+  const int selEnd = min(p.n_sel * B, t1);
+  if (t0 >= selEnd) return;
+  const int nt = selEnd - t0;
+  const signed char* kst = reinterpret_cast<const signed char*>(p.k_store);
+  const signed char* vst = reinterpret_cast<const signed char*>(p.v_store);
+  constexpr int U = 4;
+  for (int base = threadIdx.x; base < nt * 8; base += (int)blockDim.x * U) {
+    uint4 kr[U], vr[U];
+    long long ids[U];
+    int rows[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * (int)blockDim.x;
+      rows[u] = -1;
+      if (i < nt * 8) {
+        const int t = i >> 3, c = i & 7;
+        const int pos = t0 + t, slot = pos / B, off = pos % B;
+        bool bad;
+        const long long id = clamp_id(p, slot, &bad);
+        ids[u] = id;
+        rows[u] = t * 8 + c;
+        const long long o = ((id * p.hkv + h) * B + off) * NKV_D + c * 16;
+        kr[u] = ldg_nc_v4(kst + o);
+        vr[u] = ldg_nc_v4(vst + o);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (rows[u] < 0) continue;
+      const int t = rows[u] >> 3, c = rows[u] & 7;
+      const int pos = t0 + t, off = pos % B;
+      const signed char* kb = reinterpret_cast<const signed char*>(&kr[u]);
+      const signed char* vb = reinterpret_cast<const signed char*>(&vr[u]);
+      uint32_t kw[8], vw[8];
+      if (p.kind == NKV_STORE_INT8_REF) {
+        const float vsc = __ldg(p.vbs + ids[u] * p.hkv + h);
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) {
+          const int d = c * 16 + e;
+          const float k0 = (float)kb[e] * __ldg(p.kcs + h * NKV_D + d);
+          const float k1 = (float)kb[e + 1] * __ldg(p.kcs + h * NKV_D + d + 1);
+          kw[e / 2] = (uint32_t)f2bf(k0) | ((uint32_t)f2bf(k1) << 16);
+          vw[e / 2] = (uint32_t)f2bf((float)vb[e] * vsc) | ((uint32_t)f2bf((float)vb[e + 1] * vsc) << 16);
+        }
+      } else {
+        const long long so = (ids[u] * p.hkv + h) * B + off;
+        const float ksc = __bfloat162float(p.kts[so]);
+        const float vsc = __bfloat162float(p.vts[so]);
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) {
+          kw[e / 2] = (uint32_t)f2bf((float)kb[e] * ksc) | ((uint32_t)f2bf((float)kb[e + 1] * ksc) << 16);
+          vw[e / 2] = (uint32_t)f2bf((float)vb[e] * vsc) | ((uint32_t)f2bf((float)vb[e + 1] * vsc) << 16);
+        }
+      }
+      uint4* kd = reinterpret_cast<uint4*>(ks + (long long)t * pitch + c * 16);
+      uint4* vd = reinterpret_cast<uint4*>(vs + (long long)t * pitch + c * 16);
+      kd[0] = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+      kd[1] = make_uint4(kw[4], kw[5], kw[6], kw[7]);
+      vd[0] = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+      vd[1] = make_uint4(vw[4], vw[5], vw[6], vw[7]);
+    }
+  }
+}
+
+// Sum of G per-head partials over the 8 lanes of a token group, transposed:
+// each step keeps half of the remaining heads and ships the other half to the
+// partner lane, so G=4 costs 4 shuffles instead of 12.  Lane c (= lane & 7)
+// ends with the total of head head_of<G>(c); lanes with c < G hold distinct heads.
+template <int G>
+__device__ __forceinline__ int head_of(int c) {
+  int g = 0;
+#pragma unroll
+  for (int s = 0, w = G >> 1; w > 0; ++s, w >>= 1) g += ((c >> s) & 1) * w;
+  return g;
+}
+template <int G>
+__device__ __forceinline__ float reduce8_transposed(float (&v)[G], int c) {
+  float cur[G];
+#pragma unroll
+  for (int i = 0; i < G; ++i) cur[i] = v[i];
+  int len = G;
+#pragma unroll
+  for (int s = 0; s < 3; ++s) {
+    const int m = 1 << s;
+    if (len > 1) {
+      const int half = len >> 1;
+      const bool upper = (c >> s) & 1;
+#pragma unroll
+      for (int i = 0; i < G / 2; ++i) {
+        if (i < half) {
+          const float keep = upper ? cur[half + i] : cur[i];
+          const float give = upper ? cur[i] : cur[half + i];
+          cur[i] = keep + __shfl_xor_sync(FULL, give, m);
+        }
+      }
+      len = half;
+    } else {
+      cur[0] += __shfl_xor_sync(FULL, cur[0], m);
+    }
+  }
+  return cur[0];
+}
+
+// Logical key T visible to query row n?  ids_s: this CTA's block ids (-1 = bad).
+__device__ __forceinline__ bool visible(const AttendParams& p, int T, int n, int selEnd, int ringEnd,
+                                        const long long* ids_s, int slot0) {
+  if (T < selEnd) {
+    const int slot = T >> p.log2B;
+    if (ids_s[slot - slot0] < 0) return false;
+    if (p.allowed && !p.allowed[(long long)n * p.allowed_stride + slot]) return false;
+    return true;
+  }
+  if (T >= ringEnd) return (T - ringEnd) <= n + (p.n_cur - p.nq);
+  return true;
+}
+
+// acc[a][e] = sum over keys t = slice, slice+step, ... of p[t][rg*4+a] * V[t][lane*4+e]
+__device__ __forceinline__ void pv_accumulate(const float* sc, const __nv_bfloat16* vs, int nrp, int rg,
+                                              int slice, int step, int n, int lane, float (&acc)[4][4]) {
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+#pragma unroll 4
+  for (int t = slice; t < n; t += step) {
+    const float4 pr = *reinterpret_cast<const float4*>(sc + t * nrp + rg * 4);
+    const uint2 vw = *reinterpret_cast<const uint2*>(vs + (long long)t * NKV_D + lane * 4);
+    const float v0 = bf_lo(vw.x), v1 = bf_hi(vw.x), v2 = bf_lo(vw.y), v3 = bf_hi(vw.y);
+    const float pp[4] = {pr.x, pr.y, pr.z, pr.w};
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      acc[a][0] = fmaf(pp[a], v0, acc[a][0]);
+      acc[a][1] = fmaf(pp[a], v1, acc[a][1]);
+      acc[a][2] = fmaf(pp[a], v2, acc[a][2]);
+      acc[a][3] = fmaf(pp[a], v3, acc[a][3]);
+    }
+  }
+}
+
+template <int G>
+__device__ void combine_splits(const AttendParams& p, int h, float* wbuf);
+template <int G>
+__device__ void combine_cluster(const AttendParams& p, int h, float* pm, float* pl, float* po);
+template <int G>
+__device__ void push_merge(const AttendParams& p, int h, const float* pm, const float* pl, const float* po,
+                           float* recv);
+
+template <int G, bool Q1>
+__global__ void __launch_bounds__(AT_THREADS) attend_kernel(AttendParams p) {
+  extern __shared__ __align__(128) unsigned char sm[];
+  __shared__ __align__(8) uint64_t bar[2];
+  __shared__ unsigned s_ticket;
+  __shared__ float s_m[64], s_l[64];
+  __shared__ long long s_ids[AT_MAX_SLOTS];
+
+  const int split = blockIdx.x, h = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int t0 = split * p.tps, t1 = min(p.ntok, t0 + p.tps), n = t1 - t0;
+  const int nr = p.nr, nrp = p.nr_pad;
+  const int B = p.B;
+  const int selEnd = p.n_sel * B, sinkEnd = selEnd + p.sink_len, ringEnd = sinkEnd + p.ring_len;
+  const int slot0 = t0 / B;
+  const int nslots = t0 < selEnd ? (min(t1, selEnd) - 1) / B - slot0 + 1 : 0;
+
+  __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(sm);
+  __nv_bfloat16* vs = ks + (long long)p.tps * NKV_D;
+  float* sc = reinterpret_cast<float*>(vs + (long long)p.tps * NKV_D);  // [tps][nrp]
+  float* red = sc + (long long)p.tps * nrp;                              // [8][4][D]
+  float* qs = red + AT_WARPS * 4 * NKV_D;                                // [nr][D] (Q1 == false)
+  float* pm = qs + (Q1 ? 0 : nr * NKV_D);                                // [nr]   (cluster merge)
+  float* pl = pm + 64;                                                   // [nr]
+  float* po = pl + 64;                                                   // [nr][D]
+
+#ifdef NKV_CHECKED
+  int* trc = p.trace ? p.trace + (blockIdx.y * gridDim.x + blockIdx.x) * 64 : nullptr;
+#else
+  int* trc = nullptr;
+#endif
+  NKV_STAMP(trc, 48);
+
+  // ---- 1. data movement ---------------------------------------------------------
+  const int n_int8 = (p.kind != NKV_STORE_BF16) ? max(0, min(selEnd, t1) - t0) : 0;
+  if (tid == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_mbar_init();
+#ifdef NKV_CHECKED
+    if (p.overlap) pdl_wait();  // the checked count pass reads ids
+    if (p.trace) {
+      trc[0] = t0; trc[1] = t1; trc[2] = p.ring_cap; trc[3] = p.ring_start; trc[4] = p.ring_len;
+      trc[5] = p.sink_len; trc[6] = p.n_sel; trc[7] = p.B; trc[8] = p.tps; trc[9] = p.ntok;
+      unsigned smid;
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+      trc[10] = h; trc[11] = p.sink_cap; trc[12] = p.splits; trc[13] = p.n_cur; trc[14] = (int)smid;
+      trc[15] = 0;
+    }
+    mbar_expect_tx(&bar[0], issue_bulk(p, h, t0, t1, ks, 0, &bar[0], true));
+    mbar_expect_tx(&bar[1], issue_bulk(p, h, t0, t1, vs, 1, &bar[1], true));
+#else
+    const uint32_t bytes = (uint32_t)(n - n_int8) * NKV_D * 2;
+    mbar_expect_tx(&bar[0], bytes);
+    mbar_expect_tx(&bar[1], bytes);
+#endif
+    // pieces that do not depend on the selection first
+    issue_bulk(p, h, t0, t1, ks, 0, &bar[0], false, 1);
+    issue_bulk(p, h, t0, t1, vs, 1, &bar[1], false, 1);
+  }
+  // decode: append the current token to the recent ring (a slot no CTA reads)
+  if (split == 0 && p.ring_write_pos >= 0 && tid >= 32 && tid < 64 &&
+      NKV_INB(p.err, 40, ((long long)h * p.ring_cap + p.ring_write_pos) * NKV_D, NKV_D, p.ext_ring) &&
+      NKV_INB(p.err, 41, h * p.cur_head, NKV_D, p.ext_cur)) {
+    const int c = tid & 15;
+    const bool isv = (tid & 16) != 0;
+    const __nv_bfloat16* src = (isv ? p.cur_v : p.cur_k) + h * p.cur_head + c * 8;
+    __nv_bfloat16* dst = (isv ? p.ring_v : p.ring_k) + ((long long)h * p.ring_cap + p.ring_write_pos) * NKV_D + c * 8;
+    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+  }
+  // queries for this head's G heads
+  float qr[Q1 ? G : 1][16];
+  const int c = lane & 7, t4 = lane >> 3;
+  if (Q1) {
+#pragma unroll
+    for (int g = 0; g < (Q1 ? G : 1); ++g) {
+      const __nv_bfloat16* qsrc = p.q + (long long)(h * G + g) * p.q_head;
+      unpack8(__ldg(reinterpret_cast<const uint4*>(qsrc + c * 8)), qr[g]);
+      unpack8(__ldg(reinterpret_cast<const uint4*>(qsrc + 64 + c * 8)), qr[g] + 8);
+    }
+  } else {
+    for (int i = tid; i < nr * (NKV_D / 8); i += blockDim.x) {
+      const int row = i / (NKV_D / 8), cc = i % (NKV_D / 8);
+      const int qn = row / G, g = row % G;
+      float f[8];
+      unpack8(__ldg(reinterpret_cast<const uint4*>(p.q + qn * p.q_row + (long long)(h * G + g) * p.q_head + cc * 8)), f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) qs[row * NKV_D + cc * 8 + e] = f[e];
+    }
+  }
+  NKV_STAMP(trc, 49);
+  if (p.overlap) pdl_wait();  // block ids are complete past this point
+  // selected blocks: lane i of warp 0 owns block slot slot0 + i
+  if (warp == 0) {
+    __syncwarp();
+    if (lane < nslots) {
+      const int slot = slot0 + lane;
+      bool bad;
+      const long long id = clamp_id(p, slot, &bad);
+      s_ids[lane] = bad ? -1 : id;
+      if (p.kind == NKV_STORE_BF16) {
+        const int a0 = max(t0, slot * B), a1 = min(min(t1, selEnd), slot * B + B);
+        const int off = a0 - slot * B, len = a1 - a0;
+        const long long src = ((id * p.hkv + h) * B + off) * NKV_D;
+        if (NKV_INB(p.err, 15, src, (long long)len * NKV_D, p.ext_store)) {
+          bulk_g2s(ks + (long long)(a0 - t0) * NKV_D, reinterpret_cast<const __nv_bfloat16*>(p.k_store) + src,
+                   (uint32_t)len * NKV_D * 2, &bar[0]);
+          bulk_g2s(vs + (long long)(a0 - t0) * NKV_D, reinterpret_cast<const __nv_bfloat16*>(p.v_store) + src,
+                   (uint32_t)len * NKV_D * 2, &bar[1]);
+        }
+      }
+    }
+  }
+  if (n_int8 > 0) load_int8(p, h, t0, t1, ks, vs);
+  __syncthreads();  // barrier init, ids, int8 tiles and qs visible
+  NKV_STAMP(trc, 50);
+  mbar_wait_bounded(&bar[0], 0, p.err);
+  NKV_STAMP(trc, 51);
+
+  // ---- 2. scores: lanes (t4, c) = (token of a group of 4, 16-dim slice); two groups
+  //         per iteration for ILP; every lane keeps the running max of its row ----------
+  float mloc = -INFINITY;
+  if (Q1) {
+    const int gh = head_of<G>(c);
+    for (int tg = warp; tg * 4 < n; tg += 2 * AT_WARPS) {
+      float kf[2][16];
+      int tt[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        tt[u] = (tg + u * AT_WARPS) * 4 + t4;
+        if (tt[u] < n) {
+          unpack8(*reinterpret_cast<const uint4*>(ks + (long long)tt[u] * NKV_D + c * 8), kf[u]);
+          unpack8(*reinterpret_cast<const uint4*>(ks + (long long)tt[u] * NKV_D + 64 + c * 8), kf[u] + 8);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) kf[u][e] = 0.f;
+        }
+      }
+      float part[2][Q1 ? G : 1];
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int g = 0; g < (Q1 ? G : 1); ++g) {
+          float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
+            s0 = fmaf(qr[g][e], kf[u][e], s0);
+            s1 = fmaf(qr[g][e + 1], kf[u][e + 1], s1);
+          }
+          part[u][g] = s0 + s1;
+        }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const float tot = reduce8_transposed<Q1 ? G : 1>(part[u], c);
+        if (tt[u] < n && c < G) {
+          const bool vis = visible(p, t0 + tt[u], 0, selEnd, ringEnd, s_ids, slot0);
+          const float sv = vis ? tot * p.scale : -INFINITY;
+          sc[tt[u] * nrp + gh] = sv;
+          mloc = fmaxf(mloc, sv);
+        }
+      }
+    }
+    // row max: combine lanes holding the same head (other c bits, t4), then warps
+#pragma unroll
+    for (int m = G; m < 32; m <<= 1) mloc = fmaxf(mloc, __shfl_xor_sync(FULL, mloc, m));
+    if (lane < G) red[warp * 64 + gh] = mloc;
+  } else {
+    for (int tg = warp; tg * 4 < n; tg += AT_WARPS) {
+      const int t = tg * 4 + t4;
+      const bool valid = t < n;
+      float kf[16];
+      if (valid) {
+        unpack8(*reinterpret_cast<const uint4*>(ks + (long long)t * NKV_D + c * 8), kf);
+        unpack8(*reinterpret_cast<const uint4*>(ks + (long long)t * NKV_D + 64 + c * 8), kf + 8);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) kf[e] = 0.f;
+      }
+      for (int qn = 0; qn < p.nq; ++qn) {
+        float part[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float* qrow = qs + (qn * G + g) * NKV_D;
+          float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) s0 = fmaf(qrow[c * 8 + e], kf[e], s0);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) s1 = fmaf(qrow[64 + c * 8 + e], kf[8 + e], s1);
+          part[g] = s0 + s1;
+        }
+        const float tot = reduce8_transposed<G>(part, c);
+        if (valid && c < G) {
+          const bool vis = visible(p, t0 + t, qn, selEnd, ringEnd, s_ids, slot0);
+          sc[t * nrp + qn * G + head_of<G>(c)] = vis ? tot * p.scale : -INFINITY;
+        }
+      }
+    }
+  }
+  if (tid < 64) s_l[tid] = 0.f;
+  __syncthreads();
+  NKV_STAMP(trc, 52);
+
+  // ---- 3. split softmax: row max, exponentials and row sums over all threads ----------
+  if (Q1) {
+    if (tid < nr) {
+      float m = -INFINITY;
+      for (int w = 0; w < AT_WARPS; ++w) m = fmaxf(m, red[w * 64 + tid]);
+      s_m[tid] = m;
+    }
+  } else {
+    for (int row = warp; row < nr; row += AT_WARPS) {
+      float m = -INFINITY;
+      for (int t = lane; t < n; t += 32) m = fmaxf(m, sc[t * nrp + row]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(FULL, m, o));
+      if (lane == 0) s_m[row] = m;
+    }
+  }
+  __syncthreads();
+  {
+    // consecutive threads walk consecutive (token, row) entries; each thread's
+    // entries share one row when nrp divides the thread count
+    float lsum = 0.f;
+    int lrow = -1;
+    for (int i = tid; i < n * nrp; i += blockDim.x) {
+      const int row = i % nrp;
+      float e = 0.f;
+      if (row < nr) {
+        const float m = s_m[row];
+        e = (m == -INFINITY) ? 0.f : __expf(sc[i] - m);
+      }
+      sc[i] = e;
+      if (row != lrow) {
+        if (lrow >= 0 && lrow < nr) atomicAdd(&s_l[lrow], lsum);
+        lsum = 0.f;
+        lrow = row;
+      }
+      lsum += e;
+    }
+    if (lrow >= 0 && lrow < nr) atomicAdd(&s_l[lrow], lsum);
+  }
+  __syncthreads();
+  NKV_STAMP(trc, 53);
+  mbar_wait_bounded(&bar[1], 0, p.err);
+  NKV_STAMP(trc, 54);
+
+  // ---- 4. P.V: lane owns 4 dims; a warp owns a group of 4 rows over a token slice --
+  const int nrg = nrp / 4;
+  float* dst_o = p.cluster ? po : p.part_o + (((long long)h * p.splits + split) * nr) * NKV_D;
+  if (!p.cluster &&
+      !NKV_INB(p.err, 44, (((long long)h * p.splits + split) * nr) * NKV_D, (long long)nr * NKV_D, p.ext_part_o))
+    return;
+  if (nrg >= AT_WARPS) {
+    for (int rg = warp; rg < nrg; rg += AT_WARPS) {
+      float acc[4][4];
+      pv_accumulate(sc, vs, nrp, rg, 0, 1, n, lane, acc);
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+        if (rg * 4 + a < nr)
+          *reinterpret_cast<float4*>(dst_o + (rg * 4 + a) * NKV_D + lane * 4) =
+              make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+    }
+  } else {
+    const int ts = AT_WARPS / nrg;  // token slices per row group
+    if (warp < nrg * ts) {
+      float acc[4][4];
+      pv_accumulate(sc, vs, nrp, warp / ts, warp % ts, ts, n, lane, acc);
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+        *reinterpret_cast<float4*>(red + (warp * 4 + a) * NKV_D + lane * 4) =
+            make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+    }
+    __syncthreads();
+    for (int i = tid; i < nr * NKV_D; i += blockDim.x) {
+      const int row = i / NKV_D, d = i % NKV_D;
+      const int rg = row / 4, a = row % 4;
+      float s = 0.f;
+      for (int sl = 0; sl < ts; ++sl) s += red[((rg * ts + sl) * 4 + a) * NKV_D + d];
+      dst_o[row * NKV_D + d] = s;
+    }
+  }
+  if (p.cluster) {
+    if (tid < nr) {
+      pm[tid] = s_m[tid];
+      pl[tid] = s_l[tid];
+    }
+    NKV_STAMP(trc, 55);
+    combine_cluster<G>(p, h, pm, pl, po);
+    NKV_STAMP(trc, 57);
+    return;
+  }
+  if (tid < nr && NKV_INB(p.err, 42, (((long long)h * p.splits + split) * nr + tid) * 2, 2, p.ext_part_ml)) {
+    float* ml = p.part_ml + (((long long)h * p.splits + split) * nr + tid) * 2;
+    ml[0] = s_m[tid];
+    ml[1] = s_l[tid];
+  }
+
+  // ---- 5. last CTA of the head merges the splits -----------------------------------
+  NKV_STAMP(trc, 55);
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_ticket = atomicAdd(p.counters + h, 1u);
+  __syncthreads();
+  NKV_STAMP(trc, 56);
+  if (s_ticket != (unsigned)p.splits - 1) return;
+  __threadfence();
+  if (tid == 0) p.counters[h] = 0u;
+  combine_splits<G>(p, h, reinterpret_cast<float*>(ks));
+  __syncthreads();
+  NKV_STAMP(trc, 57);
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core helpers (mma.sync m16n8k16, bf16 inputs, fp32 accumulate).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  return (uint32_t)f2bf(lo) | ((uint32_t)f2bf(hi) << 16);
+}
+
+constexpr int KPITCH = NKV_D + 8;  // smem row pitch (elements): 272 B keeps ldmatrix conflict-free
+
+// Single-query decode (nq == 1) on the tensor cores.  Every warp owns a slice
+// of up to 48 keys of the CTA's range and fetches that slice itself with
+// 16-byte cp.async copies (K as one commit group, V as a second), into shared
+// memory rows with a 272-byte pitch so that ldmatrix reads are conflict-free.
+// Copies of keys that do not depend on the selection are issued before the
+// programmatic-dependent-launch wait; the selected blocks right after it.
+//   S = Q K^T   : A = the G query rows (rows >= G are zero), B = K via ldmatrix
+//   softmax     : on the accumulator fragments (quad shuffles); keys past the
+//                 slice or invisible are masked to -inf
+//   O += P V    : the score fragments become the A operand (bf16), V via
+//                 ldmatrix.trans
+// The warp partials (m, l, o) are merged through shared memory, then across
+// the splits (cluster DSMEM merge or workspace merge).
+template <int G>
+__device__ __forceinline__ void slice_copy(const AttendParams& p, int h, int t0, int lo, int hi, int lane,
+                                           __nv_bfloat16* ks, __nv_bfloat16* vs, int selEnd, int sinkEnd,
+                                           int ringEnd, const long long* s_ids, int slot0, bool selected,
+                                           bool want_k) {
+  // lane (r2, chunk): rows lo + r2, lo + r2 + 2, ...; 16-byte chunk of 16
+  const int chunk = lane & 15, r2 = lane >> 4;
+  for (int r = lo + r2; r < hi; r += 2) {
+    const int pos = t0 + r;
+    const bool is_sel = pos < selEnd;
+    if (is_sel != selected) continue;
+    const __nv_bfloat16* src;
+    if (is_sel) {
+      long long id = s_ids[(pos >> p.log2B) - slot0];
+      if (id < 0) id = 0;  // masked in the scores
+      const long long o = ((id * p.hkv + h) * p.B + (pos & (p.B - 1))) * NKV_D;
+      src = reinterpret_cast<const __nv_bfloat16*>(want_k ? p.k_store : p.v_store) + o;
+    } else if (pos < sinkEnd) {
+      src = (want_k ? p.sink_k : p.sink_v) + ((long long)h * p.sink_cap + (pos - selEnd)) * NKV_D;
+    } else if (pos < ringEnd) {
+      int phys = p.ring_start + (pos - sinkEnd);
+      if (phys >= p.ring_cap) phys -= p.ring_cap;
+      src = (want_k ? p.ring_k : p.ring_v) + ((long long)h * p.ring_cap + phys) * NKV_D;
+    } else {
+      src = (want_k ? p.cur_k : p.cur_v) + (long long)(pos - ringEnd) * p.cur_row + (long long)h * p.cur_head;
+    }
+    cp_async16((want_k ? ks : vs) + (long long)r * KPITCH + chunk * 8, src + chunk * 8);
+  }
+}
+
+template <int G>
+__global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(AttendParams p) {
+  extern __shared__ __align__(128) unsigned char sm[];
+  __shared__ unsigned s_ticket;
+  __shared__ long long s_ids[AT_MAX_SLOTS];
+  constexpr int NW = DK<G>::WARPS;
+
+  const int split = blockIdx.x, h = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int t0 = split * p.tps, t1 = min(p.ntok, t0 + p.tps), n = t1 - t0;
+  const int selEnd = p.n_sel * p.B, sinkEnd = selEnd + p.sink_len, ringEnd = sinkEnd + p.ring_len;
+  const int slot0 = t0 >> p.log2B;
+  const int nslots = t0 < selEnd ? ((min(t1, selEnd) - 1) >> p.log2B) - slot0 + 1 : 0;
+  const bool int8 = p.kind != NKV_STORE_BF16;
+
+  __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(sm);          // [tps][KPITCH]
+  __nv_bfloat16* vs = ks + (long long)p.tps * KPITCH;                 // [tps][KPITCH]
+  float* wpo = reinterpret_cast<float*>(vs + (long long)p.tps * KPITCH);  // [NW][G][D]
+  float* wml = wpo + NW * G * NKV_D;                                  // [NW][G][2]
+  float* pm = wml + NW * G * 2;                                       // [G] CTA partial
+  float* pl = pm + 64;
+  float* po = pl + 64;                                                // [G][D]
+  float* recv = po + G * NKV_D;                                       // [C][G][D + 2] (cluster)
+
+#ifdef NKV_CHECKED
+  int* trc = p.trace ? p.trace + (blockIdx.y * gridDim.x + blockIdx.x) * 64 : nullptr;
+#else
+  int* trc = nullptr;
+#endif
+  NKV_STAMP(trc, 48);
+
+  // this warp's slice [lo, hi), 8-aligned, at most 48 keys
+  const int tpw = ((n + NW - 1) / NW + 7) / 8 * 8;
+  const int lo = min(n, warp * tpw), hi = min(n, lo + tpw);
+
+  // keys that do not depend on the selection (sink, ring, current)
+  slice_copy<G>(p, h, t0, lo, hi, lane, ks, vs, selEnd, sinkEnd, ringEnd, s_ids, slot0, false, true);
+  slice_copy<G>(p, h, t0, lo, hi, lane, ks, vs, selEnd, sinkEnd, ringEnd, s_ids, slot0, false, false);
+  // decode: append the current token to the recent ring (a slot no CTA reads)
+  if (split == 0 && p.ring_write_pos >= 0 && tid >= 64 && tid < 96 &&
+      NKV_INB(p.err, 40, ((long long)h * p.ring_cap + p.ring_write_pos) * NKV_D, NKV_D, p.ext_ring) &&
+      NKV_INB(p.err, 41, h * p.cur_head, NKV_D, p.ext_cur)) {
+    const int c = tid & 15;
+    const bool isv = (tid & 16) != 0;
+    const __nv_bfloat16* src = (isv ? p.cur_v : p.cur_k) + h * p.cur_head + c * 8;
+    __nv_bfloat16* dst = (isv ? p.ring_v : p.ring_k) + ((long long)h * p.ring_cap + p.ring_write_pos) * NKV_D + c * 8;
+    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+  }
+  // Q as the A operand: rows = query heads g < G (lane quad g), rows >= G zero.
+  const int qg = lane >> 2, qt = lane & 3;
+  uint32_t qa[8][2];
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    if (qg < G) {
+      const __nv_bfloat16* qrow = p.q + (long long)(h * G + qg) * p.q_head + kk * 16 + 2 * qt;
+      qa[kk][0] = __ldg(reinterpret_cast<const uint32_t*>(qrow));
+      qa[kk][1] = __ldg(reinterpret_cast<const uint32_t*>(qrow + 8));
+    } else {
+      qa[kk][0] = qa[kk][1] = 0u;
+    }
+  }
+  if (p.overlap) pdl_wait();  // block ids are complete past this point
+  if (tid < nslots) {
+    bool bad;
+    const long long id = clamp_id(p, slot0 + tid, &bad);
+    s_ids[tid] = bad ? -1 : id;
+  }
+  if (int8) load_int8_pitched(p, h, t0, t1, ks, vs, KPITCH);
+  __syncthreads();  // ids (and int8 tiles) visible
+  NKV_STAMP(trc, 49);
+  if (!int8) {
+    slice_copy<G>(p, h, t0, lo, hi, lane, ks, vs, selEnd, sinkEnd, ringEnd, s_ids, slot0, true, true);
+  }
+  cp_async_commit();  // group: every K row of the slice
+  if (!int8) {
+    slice_copy<G>(p, h, t0, lo, hi, lane, ks, vs, selEnd, sinkEnd, ringEnd, s_ids, slot0, true, false);
+  }
+  cp_async_commit();  // group: selected V rows (the other V rows are in the first group)
+  cp_async_wait<1>();
+  __syncwarp();
+  NKV_STAMP(trc, 51);
+#ifdef NKV_CHECKED
+  if (p.stop == 1) { cp_async_wait<0>(); return; }
+#endif
+
+  constexpr int MAXT = AT_TPS_MAX_CLUSTER / (8 * NW) + 1;  // n-tiles of 8 keys per warp slice
+  float sfr[MAXT][4];
+  const int ntile = (hi - lo + 7) / 8;
+  // ldmatrix row address pattern: lane i feeds row (i & 7) of matrix (i >> 3)
+  const int mrow = lane & 7, msel = lane >> 3;
+#pragma unroll
+  for (int j = 0; j < MAXT; ++j) {
+    sfr[j][0] = sfr[j][1] = sfr[j][2] = sfr[j][3] = 0.f;
+    if (j < ntile) {
+      int row = lo + j * 8 + mrow;
+      if (row >= hi) row = lo;  // only this slice's rows are loaded; masked below
+      const __nv_bfloat16* kr = ks + (long long)row * KPITCH;
+#pragma unroll
+      for (int kk = 0; kk < 8; kk += 2) {
+        // matrices: (kk, lo 8 dims), (kk, hi 8 dims), (kk+1, lo), (kk+1, hi)
+        uint32_t b[4];
+        ldsm_x4(b, kr + (kk + (msel >> 1)) * 16 + (msel & 1) * 8);
+        mma_bf16(sfr[j], qa[kk][0], 0u, qa[kk][1], 0u, b[0], b[1]);
+        mma_bf16(sfr[j], qa[kk + 1][0], 0u, qa[kk + 1][1], 0u, b[2], b[3]);
+      }
+    }
+  }
+  // mask + scale; lane holds row qg keys lo + 8j + 2qt + {0, 1}
+  float mloc = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < MAXT; ++j) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int t = lo + j * 8 + 2 * qt + e;
+      float sv = -INFINITY;
+      if (j < ntile && t < hi && qg < G && visible(p, t0 + t, 0, selEnd, ringEnd, s_ids, slot0))
+        sv = sfr[j][e] * p.scale;
+      sfr[j][e] = sv;
+      mloc = fmaxf(mloc, sv);
+    }
+  }
+  mloc = fmaxf(mloc, __shfl_xor_sync(FULL, mloc, 1));
+  mloc = fmaxf(mloc, __shfl_xor_sync(FULL, mloc, 2));
+  float lloc = 0.f;
+#pragma unroll
+  for (int j = 0; j < MAXT; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float pe = (mloc == -INFINITY || sfr[j][e] == -INFINITY) ? 0.f : __expf(sfr[j][e] - mloc);
+      sfr[j][e] = pe;
+      lloc += pe;
+    }
+  lloc += __shfl_xor_sync(FULL, lloc, 1);
+  lloc += __shfl_xor_sync(FULL, lloc, 2);
+  NKV_STAMP(trc, 52);
+  cp_async_wait<0>();
+  __syncwarp();
+  NKV_STAMP(trc, 53);
+#ifdef NKV_CHECKED
+  if (p.stop == 2) { if (lane == 0 && mloc == 1.2345f) p.out[0] = __float2bfloat16(lloc); return; }
+#endif
+
+  // O += P V: k-steps of 16 keys (two n-tiles of scores), 16 n-tiles of 8 dims
+  float ofr[16][4];
+#pragma unroll
+  for (int d = 0; d < 16; ++d) ofr[d][0] = ofr[d][1] = ofr[d][2] = ofr[d][3] = 0.f;
+#pragma unroll
+  for (int ksx = 0; ksx < (MAXT + 1) / 2; ++ksx) {
+    if (2 * ksx < ntile) {
+      const uint32_t pa0 = pack_bf16x2(sfr[2 * ksx][0], sfr[2 * ksx][1]);
+      const uint32_t pa2 = 2 * ksx + 1 < MAXT ? pack_bf16x2(sfr[2 * ksx + 1][0], sfr[2 * ksx + 1][1]) : 0u;
+      // ldmatrix.trans rows: keys lo + 16 ksx + (msel & 1) * 8 + mrow, dims + (msel >> 1) * 8
+      int row = lo + ksx * 16 + (msel & 1) * 8 + mrow;
+      if (row >= hi) row = lo;  // loaded, finite values times p = 0
+      const __nv_bfloat16* vr = vs + (long long)row * KPITCH + (msel >> 1) * 8;
+#pragma unroll
+      for (int dn = 0; dn < 16; dn += 2) {
+        uint32_t b[4];
+        ldsm_x4_t(b, vr + dn * 8);
+        mma_bf16(ofr[dn], pa0, 0u, pa2, 0u, b[0], b[1]);
+        mma_bf16(ofr[dn + 1], pa0, 0u, pa2, 0u, b[2], b[3]);
+      }
+    }
+  }
+  // warp partial: rows qg < G hold o[qg][8 dn + 2 qt + {0,1}]
+  if (qg < G) {
+#pragma unroll
+    for (int dn = 0; dn < 16; ++dn)
+      *reinterpret_cast<float2*>(wpo + (warp * G + qg) * NKV_D + dn * 8 + 2 * qt) = make_float2(ofr[dn][0], ofr[dn][1]);
+    if (qt == 0) {
+      wml[(warp * G + qg) * 2] = lo < hi ? mloc : -INFINITY;
+      wml[(warp * G + qg) * 2 + 1] = lo < hi ? lloc : 0.f;
+    }
+  }
+  __syncthreads();
+  NKV_STAMP(trc, 54);
+#ifdef NKV_CHECKED
+  if (p.stop == 3) return;
+#endif
+
+  // ---- merge the warp slices into the CTA partial -----------------------------------
+  float* dst_o = p.cluster ? po : p.part_o + (((long long)h * p.splits + split) * G) * NKV_D;
+  for (int it = tid; it < G * (NKV_D / 4); it += DK<G>::THREADS) {
+    const int g = it / (NKV_D / 4), d4 = it % (NKV_D / 4);
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, wml[(w * G + g) * 2]);
+    float L = 0.f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float m = wml[(w * G + g) * 2];
+      if (m == -INFINITY) continue;
+      const float sw = __expf(m - M);
+      L += sw * wml[(w * G + g) * 2 + 1];
+      const float4 v = *reinterpret_cast<const float4*>(wpo + (w * G + g) * NKV_D + d4 * 4);
+      o.x = fmaf(sw, v.x, o.x);
+      o.y = fmaf(sw, v.y, o.y);
+      o.z = fmaf(sw, v.z, o.z);
+      o.w = fmaf(sw, v.w, o.w);
+    }
+    *reinterpret_cast<float4*>(dst_o + g * NKV_D + d4 * 4) = o;
+    if (d4 == 0) {
+      if (p.cluster) {
+        pm[g] = M;
+        pl[g] = L;
+      } else {
+        float* ml = p.part_ml + (((long long)h * p.splits + split) * G + g) * 2;
+        ml[0] = M;
+        ml[1] = L;
+      }
+    }
+  }
+  NKV_STAMP(trc, 55);
+#ifdef NKV_CHECKED
+  if (p.stop == 4) return;
+#endif
+  if (p.cluster) {
+    if (p.push) {
+      __syncthreads();  // CTA partial complete
+      push_merge<G>(p, h, pm, pl, po, recv);
+    } else {
+      combine_cluster<G>(p, h, pm, pl, po);  // begins with a cluster barrier
+    }
+    NKV_STAMP(trc, 57);
+    return;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_ticket = atomicAdd(p.counters + h, 1u);
+  __syncthreads();
+  if (s_ticket != (unsigned)p.splits - 1) return;
+  __threadfence();
+  if (tid == 0) p.counters[h] = 0u;
+  combine_splits<G>(p, h, reinterpret_cast<float*>(ks));
+}
+
+// Push merge for the decode kernel: every CTA of the head's cluster stores its
+// partial (m, l, o) for G rows into slot `rank` of the receive buffer of the
+// cluster's rank-0 CTA (DSMEM stores), then arrives on the cluster barrier with
+// release semantics.  Only rank 0 waits (acquire); it merges the C partials
+// from its own shared memory and writes the bf16 output.  The other CTAs exit
+// after arriving; nothing reads their shared memory.
+template <int G>
+__device__ void push_merge(const AttendParams& p, int h, const float* pm, const float* pl, const float* po,
+                           float* recv /* [C][G][D + 2] in every CTA; rank 0's is used */) {
+  cg::cluster_group cluster = cg::this_cluster();
+  const int C = (int)cluster.num_blocks();
+  const int rank = (int)cluster.block_rank();
+  constexpr int RW = NKV_D + 2;
+  float* dst = cluster.map_shared_rank(recv, 0) + (long long)rank * G * RW;
+  for (int i = threadIdx.x; i < G * (NKV_D / 4); i += blockDim.x) {
+    const int g = i / (NKV_D / 4), d4 = i % (NKV_D / 4);
+    const float4 v = *reinterpret_cast<const float4*>(po + g * NKV_D + d4 * 4);
+    float* row = dst + g * RW;
+    row[d4 * 4 + 0] = v.x;
+    row[d4 * 4 + 1] = v.y;
+    row[d4 * 4 + 2] = v.z;
+    row[d4 * 4 + 3] = v.w;
+    if (d4 == 0) {
+      row[NKV_D] = pm[g];
+      row[NKV_D + 1] = pl[g];
+    }
+  }
+  // arrive (release: the stores above are visible to whoever acquires)
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  if (rank != 0) return;
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+  for (int it = threadIdx.x; it < G * (NKV_D / 4); it += blockDim.x) {
+    const int g = it / (NKV_D / 4), d4 = it % (NKV_D / 4);
+    float M = -INFINITY;
+    for (int q = 0; q < C; ++q) M = fmaxf(M, recv[(q * G + g) * RW + NKV_D]);
+    float L = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q < C; ++q) {
+      const float* row = recv + (q * G + g) * RW;
+      const float m = row[NKV_D];
+      if (m == -INFINITY) continue;
+      const float w = __expf(m - M);
+      L += w * row[NKV_D + 1];
+      acc.x = fmaf(w, row[d4 * 4 + 0], acc.x);
+      acc.y = fmaf(w, row[d4 * 4 + 1], acc.y);
+      acc.z = fmaf(w, row[d4 * 4 + 2], acc.z);
+      acc.w = fmaf(w, row[d4 * 4 + 3], acc.w);
+    }
+    const float inv = 1.f / L;
+    const long long oo = (long long)(h * G + g) * p.out_head + d4 * 4;
+    if (NKV_INB(p.err, 43, oo, 4, p.ext_out)) {
+      uint2 w2;
+      w2.x = (uint32_t)f2bf(acc.x * inv) | ((uint32_t)f2bf(acc.y * inv) << 16);
+      w2.y = (uint32_t)f2bf(acc.z * inv) | ((uint32_t)f2bf(acc.w * inv) << 16);
+      *reinterpret_cast<uint2*>(p.out + oo) = w2;
+    }
+  }
+}
+
+// Cluster merge: the CTAs of one cluster are the splits of one KV head.  After
+// a cluster barrier, CTA r merges output groups r, r + C, ... reading every
+// split's (m, l, o) from the peers' shared memory, then a second barrier keeps
+// that memory alive until all peers are done.
+template <int G>
+__device__ void combine_cluster(const AttendParams& p, int h, float* pm, float* pl, float* po) {
+  cg::cluster_group cluster = cg::this_cluster();
+  const int C = (int)cluster.num_blocks();
+  const int rank = (int)cluster.block_rank();
+  const int nr = p.nr;
+  cluster.sync();
+  const int items = nr * (NKV_D / 4);
+  for (int it = threadIdx.x * C + rank; it < items; it += C * (int)blockDim.x) {
+    const int row = it / (NKV_D / 4), d4 = it % (NKV_D / 4);
+    float m[AT_CLUSTER_MAX], M = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < AT_CLUSTER_MAX; ++q) {
+      m[q] = -INFINITY;
+      if (q < C) {
+        m[q] = *cluster.map_shared_rank(pm + row, q);
+        M = fmaxf(M, m[q]);
+      }
+    }
+    float L = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < AT_CLUSTER_MAX; ++q) {
+      if (q < C && m[q] != -INFINITY) {
+        const float w = __expf(m[q] - M);
+        L += w * *cluster.map_shared_rank(pl + row, q);
+        const float4 v = *reinterpret_cast<const float4*>(cluster.map_shared_rank(po + row * NKV_D + d4 * 4, q));
+        acc.x = fmaf(w, v.x, acc.x);
+        acc.y = fmaf(w, v.y, acc.y);
+        acc.z = fmaf(w, v.z, acc.z);
+        acc.w = fmaf(w, v.w, acc.w);
+      }
+    }
+    const float inv = 1.f / L;
+    const int qn = row / G, g = row % G;
+    const long long oo = qn * p.out_row + (long long)(h * G + g) * p.out_head + d4 * 4;
+    if (NKV_INB(p.err, 43, oo, 4, p.ext_out)) {
+      uint2 w;
+      w.x = (uint32_t)f2bf(acc.x * inv) | ((uint32_t)f2bf(acc.y * inv) << 16);
+      w.y = (uint32_t)f2bf(acc.z * inv) | ((uint32_t)f2bf(acc.w * inv) << 16);
+      *reinterpret_cast<uint2*>(p.out + oo) = w;
+    }
+  }
+  cluster.sync();
+}
+
+// Log-sum-exp merge of the splits of head h, run by the head's last CTA.
+// wbuf (shared, >= 2 * nr * splits floats) first receives every split's (m, l)
+// in one parallel load, then the per-(row, split) weights exp(m - M) / L; the
+// outputs are weighted sums of float4 partial rows, with the splits divided
+// between two threads per output when there are few rows.
+template <int G>
+__device__ void combine_splits(const AttendParams& p, int h, float* wbuf) {
+  const int tid = threadIdx.x;
+  const int nr = p.nr, S = p.splits;
+  float* wm = wbuf;            // [nr][S]
+  float* wl = wbuf + nr * S;   // [nr][S]
+  const float* ml = p.part_ml + (long long)h * S * nr * 2;
+  for (int i = tid; i < nr * S; i += blockDim.x) {
+    const int row = i / S, sp = i % S;
+    const float2 v = __ldcg(reinterpret_cast<const float2*>(ml + ((long long)sp * nr + row) * 2));
+    wm[i] = v.x;
+    wl[i] = v.y;
+  }
+  __syncthreads();
+  for (int row = tid >> 5; row < nr; row += (int)(blockDim.x >> 5)) {
+    const int lane = tid & 31;
+    float M = -INFINITY;
+    for (int sp = lane; sp < S; sp += 32) M = fmaxf(M, wm[row * S + sp]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, o));
+    float L = 0.f;
+    for (int sp = lane; sp < S; sp += 32) {
+      const float m = wm[row * S + sp];
+      L += (m == -INFINITY) ? 0.f : wl[row * S + sp] * __expf(m - M);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(FULL, L, o);
+    __syncwarp();
+    for (int sp = lane; sp < S; sp += 32) {
+      const float m = wm[row * S + sp];
+      wm[row * S + sp] = (m == -INFINITY) ? 0.f : __expf(m - M) / L;
+    }
+  }
+  __syncthreads();
+  const int items = nr * (NKV_D / 4);          // (row, 4-dim group)
+  const int tpi = items >= (int)blockDim.x ? 1 : 2;  // threads per item
+  const float* po = p.part_o + (long long)h * S * nr * NKV_D;
+  for (int base = 0; base < items * tpi; base += blockDim.x) {
+    const int idx = base + tid;
+    const int item = idx / tpi, half = idx % tpi;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (item < items) {
+      const int row = item / (NKV_D / 4), d4 = item % (NKV_D / 4);
+#pragma unroll 4
+      for (int sp = half; sp < S; sp += tpi) {
+        const float w = wm[row * S + sp];
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(po + ((long long)sp * nr + row) * NKV_D) + d4);
+        acc.x = fmaf(w, v.x, acc.x);
+        acc.y = fmaf(w, v.y, acc.y);
+        acc.z = fmaf(w, v.z, acc.z);
+        acc.w = fmaf(w, v.w, acc.w);
+      }
+    }
+    if (tpi == 2) {
+      acc.x += __shfl_xor_sync(FULL, acc.x, 1);
+      acc.y += __shfl_xor_sync(FULL, acc.y, 1);
+      acc.z += __shfl_xor_sync(FULL, acc.z, 1);
+      acc.w += __shfl_xor_sync(FULL, acc.w, 1);
+    }
+    if (item < items && half == 0) {
+      const int row = item / (NKV_D / 4), d4 = item % (NKV_D / 4);
+      const int qn = row / G, g = row % G;
+      const long long oo = qn * p.out_row + (long long)(h * G + g) * p.out_head + d4 * 4;
+      if (NKV_INB(p.err, 43, oo, 4, p.ext_out)) {
+        uint2 w;
+        w.x = (uint32_t)f2bf(acc.x) | ((uint32_t)f2bf(acc.y) << 16);
+        w.y = (uint32_t)f2bf(acc.z) | ((uint32_t)f2bf(acc.w) << 16);
+        *reinterpret_cast<uint2*>(p.out + oo) = w;
+      }
+    }
+  }
+}
+
+// Launch shape of the most recent nkv_attend call on this thread.
+static thread_local int g_last_cluster = -1, g_last_splits = 0, g_last_tps = 0;
+
+static int env_int(const char* name, int dflt) {
+  const char* v = getenv(name);
+  return (v && *v) ? atoi(v) : dflt;
+}
+
+static int splits_for(int ntok, int hkv, int sms) {
+  int s_mem = (ntok + AT_TPS_MAX - 1) / AT_TPS_MAX;
+  int s_par = sms / hkv;
+  int s_cap = (ntok + AT_MIN_TPS - 1) / AT_MIN_TPS;
+  int s = s_par < s_cap ? s_par : s_cap;
+  if (s < s_mem) s = s_mem;
+  if (s < 1) s = 1;
+  return s;
+}
+
+static size_t attend_ws(int hkv, int nr, int max_tokens) {
+  const long long smax = (max_tokens + AT_MIN_TPS - 1) / AT_MIN_TPS + 1;
+  size_t o = 256 + ((hkv * 4 + 255) / 256) * 256;
+  o += (size_t)hkv * smax * nr * NKV_D * 4;
+  o += (size_t)hkv * smax * nr * 2 * 4;
+  return o + 256;
+}
+
+}  // namespace nkv
+
+using namespace nkv;
+
+extern "C" size_t nkv_attend_workspace_bytes(int hkv, int hq, int nq, int max_tokens) {
+  if (hkv < 1) hkv = 1;
+  if (nq < 1) nq = 1;
+  if (max_tokens < 1) max_tokens = 1;
+  return attend_ws(hkv, (hq / hkv) * nq, max_tokens);
+}
+
+extern "C" int nkv_attend(nkv_stream_t stream, const nkv_attend_args* a) {
+  NKV_REQUIRE(a, "attend: null args");
+  NKV_SUPPORTED(a->head_dim == NKV_D, "attend: head_dim %d unsupported (128 only)", a->head_dim);
+  NKV_REQUIRE(a->hkv >= 1 && a->hq % a->hkv == 0, "attend: hq %d not a multiple of hkv %d", a->hq,
+              a->hkv);
+  const int G = a->hq / a->hkv;
+  NKV_SUPPORTED(G == 1 || G == 2 || G == 4 || G == 8, "attend: G=%d unsupported", G);
+  NKV_SUPPORTED(a->nq >= 1 && a->nq <= 8 && a->nq * G <= 64, "attend: nq=%d unsupported", a->nq);
+  NKV_REQUIRE(a->n_cur == a->nq || a->n_cur == 0, "attend: n_cur (%d) must be 0 or nq (%d)",
+              a->n_cur, a->nq);
+  NKV_REQUIRE(a->block_size >= 1 && a->n_sel >= 0 && a->sink_len >= 0 && a->ring_len >= 0,
+              "attend: negative segment length");
+  NKV_SUPPORTED((a->block_size & (a->block_size - 1)) == 0 && a->block_size >= 16 && a->block_size <= 128,
+                "attend: block_size %d unsupported (16, 32, 64 or 128)", a->block_size);
+  NKV_REQUIRE(a->n_sel == 0 || (a->block_ids && a->k_store && a->v_store && a->max_blocks > 0),
+              "attend: selected segment needs block_ids and the block store");
+  NKV_REQUIRE(a->store_kind >= 0 && a->store_kind <= 2, "attend: bad store_kind");
+  NKV_REQUIRE(a->store_kind != NKV_STORE_INT8_REF || a->n_sel == 0 || (a->k_chan_scale && a->v_block_scale),
+              "attend: int8 reference scheme needs its scales");
+  NKV_REQUIRE(a->store_kind != NKV_STORE_INT8_TOKEN || a->n_sel == 0 || (a->k_tok_scale && a->v_tok_scale),
+              "attend: int8 token scheme needs its scales");
+  NKV_REQUIRE(a->sink_len <= a->sink_cap || a->sink_len == 0, "attend: sink_len > sink_cap");
+  NKV_REQUIRE(a->sink_len == 0 || (a->sink_k && a->sink_v), "attend: sink missing");
+  NKV_REQUIRE(a->ring_len == 0 || (a->ring_k && a->ring_v && a->ring_len <= a->ring_cap &&
+                                   a->ring_start >= 0 && a->ring_start < a->ring_cap),
+              "attend: bad ring slice");
+  NKV_REQUIRE(a->ring_write_pos < a->ring_cap && (a->ring_write_pos < 0 || a->ring_k),
+              "attend: bad ring_write_pos");
+  NKV_REQUIRE(a->q && a->out && a->workspace, "attend: null pointer");
+  NKV_REQUIRE(a->n_cur == 0 || (a->cur_k && a->cur_v), "attend: current tokens missing");
+  NKV_REQUIRE(a->ring_write_pos < 0 || a->n_cur >= 1, "attend: ring write needs a current token");
+  NKV_REQUIRE(a->allowed == nullptr || a->allowed_stride >= a->n_sel, "attend: allowed stride");
+  NKV_REQUIRE(((uintptr_t)a->out & 7) == 0 && a->out_head_stride % 4 == 0 && a->out_row_stride % 4 == 0,
+              "attend: out must be 8-byte aligned with strides multiple of 4 elements");
+  NKV_REQUIRE(((uintptr_t)a->q & 15) == 0 && ((uintptr_t)a->cur_k & 15) == 0 &&
+                  ((uintptr_t)a->cur_v & 15) == 0 && a->q_row_stride % 8 == 0 &&
+                  a->q_head_stride % 8 == 0 && a->cur_row_stride % 8 == 0 &&
+                  a->cur_head_stride % 8 == 0,
+              "attend: q/cur must be 16-byte aligned with strides multiple of 8 elements");
+  const long long ntok = (long long)a->n_sel * a->block_size + a->sink_len + a->ring_len + a->n_cur;
+  NKV_REQUIRE(ntok >= 1 && ntok < (1ll << 30), "attend: key count %lld out of range", ntok);
+  const int nr = a->nq * G;
+  NKV_REQUIRE(a->workspace_bytes >= attend_ws(a->hkv, nr, (int)ntok),
+              "attend: workspace too small (%zu < %zu)", a->workspace_bytes,
+              attend_ws(a->hkv, nr, (int)ntok));
+
+  AttendParams p;
+  p.q = (const __nv_bfloat16*)a->q;
+  p.q_row = a->q_row_stride;
+  p.q_head = a->q_head_stride;
+  p.nq = a->nq;
+  p.hkv = a->hkv;
+  p.B = a->block_size;
+  p.log2B = 0;
+  while ((1 << p.log2B) < a->block_size) ++p.log2B;
+  p.scale = a->scale;
+  p.ids = (const long long*)a->block_ids;
+  p.n_sel = a->n_sel;
+  p.max_blocks = a->max_blocks;
+  p.kind = a->store_kind;
+  p.k_store = a->k_store;
+  p.v_store = a->v_store;
+  p.kcs = a->k_chan_scale;
+  p.vbs = a->v_block_scale;
+  p.kts = (const __nv_bfloat16*)a->k_tok_scale;
+  p.vts = (const __nv_bfloat16*)a->v_tok_scale;
+  p.allowed = a->allowed;
+  p.allowed_stride = a->allowed_stride;
+  p.sink_k = (const __nv_bfloat16*)a->sink_k;
+  p.sink_v = (const __nv_bfloat16*)a->sink_v;
+  p.sink_cap = a->sink_cap;
+  p.sink_len = a->sink_len;
+  p.ring_k = (__nv_bfloat16*)a->ring_k;
+  p.ring_v = (__nv_bfloat16*)a->ring_v;
+  p.ring_cap = a->ring_cap;
+  p.ring_start = a->ring_start;
+  p.ring_len = a->ring_len;
+  p.cur_k = (const __nv_bfloat16*)a->cur_k;
+  p.cur_v = (const __nv_bfloat16*)a->cur_v;
+  p.cur_row = a->cur_row_stride;
+  p.cur_head = a->cur_head_stride;
+  p.n_cur = a->n_cur;
+  p.ring_write_pos = a->ring_write_pos;
+  p.out = (__nv_bfloat16*)a->out;
+  p.out_row = a->out_row_stride;
+  p.out_head = a->out_head_stride;
+  p.ntok = (int)ntok;
+  p.nr = nr;
+  p.nr_pad = (nr + 3) / 4 * 4;
+  const int sms = sm_count();
+  // cluster mode: one cluster of C <= 16 CTAs per head, enough heads x C to
+  // cover the SMs, and every split's keys within the cluster tile limit.
+  // NKV_ATTEND_CLUSTER (0 = never, N = cluster size) overrides the choice.
+  const int cl_env = env_int("NKV_ATTEND_CLUSTER", -1);
+  int C = 0;
+  if (cl_env != 0 && (cl_env > 0 || a->hkv * AT_CLUSTER_MAX >= sms / 2 || a->hkv * 8 >= sms / 2)) {
+    C = cl_env > 0 ? (cl_env > AT_CLUSTER_MAX ? AT_CLUSTER_MAX : cl_env) : AT_CLUSTER_MAX;
+    while (cl_env <= 0 && C > 1 && a->hkv * C > sms + sms / 4) C >>= 1;
+    int tps = (p.ntok + C - 1) / C;
+    if (tps < AT_MIN_TPS) {
+      C = (p.ntok + AT_MIN_TPS - 1) / AT_MIN_TPS;
+      tps = (p.ntok + C - 1) / C;
+    }
+    tps = (tps + 7) / 8 * 8;
+    if (tps > AT_TPS_MAX_CLUSTER || (tps / a->block_size + 2) > AT_MAX_SLOTS) C = 0;
+    else {
+      p.tps = tps;
+      p.splits = (p.ntok + tps - 1) / tps;
+      C = p.splits;
+    }
+  }
+  p.cluster = C > 0 ? 1 : 0;
+  // NKV_ATTEND_MERGE: 0 = workspace merge, 1 = cluster pull, 2 = cluster push
+  const int merge_env = env_int("NKV_ATTEND_MERGE", 1);
+  if (merge_env == 0) p.cluster = 0;
+  p.push = merge_env == 2 ? 1 : 0;
+  p.stop = env_int("NKV_DEBUG_STOP", 0);
+  AttendParams pg = p;  // workspace-merge configuration (fallback)
+  pg.cluster = 0;
+  pg.push = 0;
+  {
+    AttendParams& q = pg;
+    q.splits = splits_for(q.ntok, a->hkv, sms);
+    q.tps = (q.ntok + q.splits - 1) / q.splits;
+    q.tps = (q.tps + 3) / 4 * 4;
+    q.splits = (q.ntok + q.tps - 1) / q.tps;
+    while (2 * nr * q.splits > q.tps * 64) {
+      q.tps *= 2;
+      q.splits = (q.ntok + q.tps - 1) / q.tps;
+    }
+  }
+  if (!p.cluster) {
+    p.splits = splits_for(p.ntok, a->hkv, sms);
+    p.tps = (p.ntok + p.splits - 1) / p.splits;
+    p.tps = (p.tps + 3) / 4 * 4;
+    p.splits = (p.ntok + p.tps - 1) / p.tps;
+    // the merge keeps 2 * nr * splits floats in the K tile region (tps * 64 floats)
+    while (2 * nr * p.splits > p.tps * 64) {
+      p.tps *= 2;
+      p.splits = (p.ntok + p.tps - 1) / p.tps;
+    }
+    NKV_SUPPORTED(p.tps <= AT_TPS_MAX && p.tps / a->block_size + 2 <= AT_MAX_SLOTS,
+                  "attend: %d keys per CTA exceed the tile limit", p.tps);
+  }
+  auto finish = [&](AttendParams& p) -> int {
+    char* ws = (char*)a->workspace;
+    p.err = (int*)ws;
+    p.counters = (unsigned*)(ws + 256);
+    size_t off = 256 + ((a->hkv * 4 + 255) / 256) * 256;
+    p.part_o = (float*)(ws + off);
+    off += (size_t)a->hkv * p.splits * nr * NKV_D * 4;
+    p.part_ml = (float*)(ws + off);
+    p.trace = nullptr;
+#ifdef NKV_CHECKED
+    {
+      const size_t need = attend_ws(a->hkv, nr, (int)ntok);
+      const size_t tb = (size_t)p.splits * a->hkv * 64 * 4;
+      if (a->workspace_bytes >= need + tb + 256) p.trace = (int*)(ws + a->workspace_bytes - tb);
+    }
+#endif
+    p.ext_part_o = (long long)a->hkv * p.splits * nr * NKV_D;
+    p.ext_part_ml = (long long)a->hkv * p.splits * nr * 2;
+    p.ext_store = (long long)a->max_blocks * a->hkv * a->block_size * NKV_D;
+    p.ext_sink = (long long)a->hkv * a->sink_cap * NKV_D;
+    p.ext_ring = (long long)a->hkv * a->ring_cap * NKV_D;
+    p.ext_cur = a->n_cur ? (a->n_cur - 1) * a->cur_row_stride + (a->hkv - 1) * a->cur_head_stride + NKV_D : 0;
+    p.ext_q = (a->nq - 1) * a->q_row_stride + (a->hq - 1) * a->q_head_stride + NKV_D;
+    p.ext_out = (a->nq - 1) * a->out_row_stride + (a->hq - 1) * a->out_head_stride + NKV_D;
+
+    return NKV_OK;
+  };
+  finish(p);
+  finish(pg);
+  const int dk_warps = 8;  // DK<G>::WARPS
+  auto smem_need = [&](const AttendParams& q) -> size_t {
+    if (a->nq == 1) {  // decode_kernel layout
+      return (size_t)q.tps * KPITCH * 2 * 2 + (size_t)dk_warps * G * NKV_D * 4 +
+             (size_t)dk_warps * G * 2 * 4 + (size_t)(128 + G * NKV_D) * 4 +
+             (q.cluster && q.push ? (size_t)q.splits * G * (NKV_D + 2) * 4 : 0);
+    }
+    return (size_t)q.tps * NKV_D * 2 * 2 + (size_t)q.tps * q.nr_pad * 4 + AT_WARPS * 4 * NKV_D * 4 +
+           (size_t)nr * NKV_D * 4 + (q.cluster ? (size_t)(128 + nr * NKV_D) * 4 : 0);
+  };  auto smem_of = [&](const AttendParams& q) -> size_t {
+    size_t need = smem_need(q);
+    // a cluster waits for its slowest CTA: claim more than half of an SM's
+    // shared memory so that the scheduler never stacks two CTAs on one SM
+    (void)AT_SMEM_ONE_PER_SM;  // 16-CTA clusters cannot be placed one CTA per SM
+    return need;
+  };
+
+  NKV_SUPPORTED(smem_of(pg) <= 220 * 1024 && pg.tps / a->block_size + 2 <= AT_MAX_SLOTS,
+                "attend: %d keys per CTA exceed the tile limit", pg.tps);
+  if (p.cluster && smem_of(p) > 220 * 1024) p = pg;
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool q1 = a->nq == 1;
+  p.overlap = pg.overlap = a->overlap_select ? 1 : 0;
+  cudaLaunchAttribute attr[2];
+  cudaLaunchConfig_t lc = {};
+  auto config = [&](const AttendParams& q) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = q.overlap;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = q.cluster ? q.splits : 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    lc.gridDim = dim3(q.splits, a->hkv);
+    lc.blockDim = dim3(AT_THREADS);
+    lc.dynamicSmemBytes = smem_of(q);
+    lc.stream = st;
+    lc.attrs = attr;
+    lc.numAttrs = 2;
+  };
+  switch (G * 2 + (q1 ? 1 : 0)) {
+#define NKV_AT_CASE(GG, QQ)                                                               \
+  case GG * 2 + (QQ ? 1 : 0): {                                                           \
+    auto kern = QQ ? decode_kernel<GG> : attend_kernel<GG, false>;                        \
+    if (ensure_smem(kern, smem_of(p) > smem_of(pg) ? smem_of(p) : smem_of(pg), "attend")) \
+      return NKV_ERR_CUDA;                                                                \
+    if (p.cluster) {                                                                      \
+      int ok = p.splits <= 8 || !ensure_nonportable_cluster(kern, "attend");              \
+      int nclusters = 0;                                                                  \
+      config(p);                                                                          \
+      if (ok && cudaOccupancyMaxActiveClusters(&nclusters, kern, &lc) != cudaSuccess)     \
+        ok = 0;                                                                           \
+      cudaGetLastError();                                                                 \
+      if (!ok || nclusters < 1) p = pg;                                                   \
+    }                                                                                     \
+    config(p);                                                                            \
+    g_last_cluster = p.cluster;                                                           \
+    g_last_splits = p.splits;                                                             \
+    g_last_tps = p.tps;                                                                   \
+    if (cudaLaunchKernelEx(&lc, kern, p) != cudaSuccess) return check_launch("attend");   \
+    break;                                                                                \
+  }
+    NKV_AT_CASE(1, true)
+    NKV_AT_CASE(1, false)
+    NKV_AT_CASE(2, true)
+    NKV_AT_CASE(2, false)
+    NKV_AT_CASE(4, true)
+    NKV_AT_CASE(4, false)
+    NKV_AT_CASE(8, true)
+    NKV_AT_CASE(8, false)
+#undef NKV_AT_CASE
+    default:
+      return NKV_ERR_UNSUPPORTED;
+  }
+  return check_launch("attend");
+}
+
+extern "C" int nkv_attend_last_config(int* cluster, int* splits, int* keys_per_cta) {
+  if (cluster) *cluster = g_last_cluster;
+  if (splits) *splits = g_last_splits;
+  if (keys_per_cta) *keys_per_cta = g_last_tps;
+  return NKV_OK;
+}

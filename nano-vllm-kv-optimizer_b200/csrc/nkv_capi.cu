@@ -1,0 +1,52 @@
+// C-ABI plumbing shared by all entry points: error message, version, and the
+// read-back of the error word kernels leave in a workspace.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include "nkv_host.h"
+
+namespace nkv {
+static thread_local char g_err[512] = "";
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+}  // namespace nkv
+
+extern "C" const char* nkv_last_error(void) { return nkv::g_err; }
+
+extern "C" int nkv_version(void) { return 1; }
+
+extern "C" int nkv_check(nkv_stream_t stream, void* workspace) {
+  NKV_REQUIRE(workspace, "check: null workspace");
+  int word = 0;
+  cudaError_t e = cudaMemcpyAsync(&word, workspace, sizeof(int), cudaMemcpyDeviceToHost,
+                                  (cudaStream_t)stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e != cudaSuccess) {
+    nkv::set_error("check: %s", cudaGetErrorString(e));
+    return NKV_ERR_CUDA;
+  }
+  if (word != 0) {
+    const int zero = 0;
+    cudaMemcpyAsync(workspace, &zero, sizeof(int), cudaMemcpyHostToDevice, (cudaStream_t)stream);
+    cudaStreamSynchronize((cudaStream_t)stream);
+    nkv::set_error("check: kernel error word %d (%s)", word,
+                   word == 1 ? "bounded wait timed out" : word == 2 ? "block id out of range" : "?");
+    return NKV_ERR_DEVICE;
+  }
+  return NKV_OK;
+}
+
+extern "C" int nkv_map_host(void* host_ptr, void** dev_ptr) {
+  NKV_REQUIRE(host_ptr && dev_ptr, "map_host: null pointer");
+  cudaError_t e = cudaHostGetDevicePointer(dev_ptr, host_ptr, 0);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    nkv::set_error("map_host: %p is not mapped pinned memory: %s", host_ptr, cudaGetErrorString(e));
+    return NKV_ERR_ARG;
+  }
+  return NKV_OK;
+}

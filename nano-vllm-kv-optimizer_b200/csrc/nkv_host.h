@@ -1,0 +1,98 @@
+// Host-side helpers shared by the C-ABI entry points: status codes, the
+// thread-local error message, launch-shape queries.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "../../include/nanokv.h"
+
+namespace nkv {
+
+void set_error(const char* fmt, ...);
+
+inline int sm_count() {
+  static thread_local int cached_dev = -1, cached = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != cached_dev) {
+    cudaDeviceGetAttribute(&cached, cudaDevAttrMultiProcessorCount, dev);
+    cached_dev = dev;
+  }
+  return cached > 0 ? cached : 148;
+}
+
+inline int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("%s: launch failed: %s", what, cudaGetErrorString(e));
+    return NKV_ERR_CUDA;
+  }
+  return NKV_OK;
+}
+
+// Raise a kernel's dynamic shared-memory limit to `bytes` (cached per kernel,
+// device and size).  Returns NKV_OK or NKV_ERR_CUDA with a message.
+template <typename Kernel>
+inline int ensure_smem(Kernel kernel, size_t bytes, const char* what) {
+  if (bytes <= 48 * 1024) return 0;
+  struct Entry { const void* fn; int dev; size_t bytes; };
+  static thread_local Entry cache[64];
+  static thread_local int used = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const void* fn = reinterpret_cast<const void*>(kernel);
+  int slot = -1;
+  for (int i = 0; i < used; ++i)
+    if (cache[i].fn == fn && cache[i].dev == dev) slot = i;
+  if (slot >= 0 && cache[slot].bytes >= bytes) return 0;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("%s: cannot reserve %zu bytes of shared memory: %s", what, bytes, cudaGetErrorString(e));
+    return -3;
+  }
+  if (slot < 0 && used < 64) slot = used++;
+  if (slot >= 0) cache[slot] = Entry{fn, dev, bytes};
+  return 0;
+}
+
+// Allow clusters above the portable size of 8 for `kernel` (once per device).
+template <typename Kernel>
+inline int ensure_nonportable_cluster(Kernel kernel, const char* what) {
+  struct Entry { const void* fn; int dev; };
+  static thread_local Entry cache[32];
+  static thread_local int used = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const void* fn = reinterpret_cast<const void*>(kernel);
+  for (int i = 0; i < used; ++i)
+    if (cache[i].fn == fn && cache[i].dev == dev) return 0;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("%s: cluster size above 8 not available: %s", what, cudaGetErrorString(e));
+    return -3;
+  }
+  if (used < 32) cache[used++] = Entry{fn, dev};
+  return 0;
+}
+
+}  // namespace nkv
+
+#define NKV_REQUIRE(cond, ...)              \
+  do {                                      \
+    if (!(cond)) {                          \
+      ::nkv::set_error(__VA_ARGS__);        \
+      return NKV_ERR_ARG;                   \
+    }                                       \
+  } while (0)
+
+#define NKV_SUPPORTED(cond, ...)            \
+  do {                                      \
+    if (!(cond)) {                          \
+      ::nkv::set_error(__VA_ARGS__);        \
+      return NKV_ERR_UNSUPPORTED;           \
+    }                                       \
+  } while (0)

@@ -1,0 +1,463 @@
+// Kernel (5): KV store + representative refresh for one prefill chunk, plus the
+// small helpers around it (K channel scale, query-segment means, and the dense
+// paged-cache row scatter that twins the reference's Triton store_kvcache).
+//
+// Store: one CTA per (block, kv head).  The 64 x 128 bf16 key tile is staged in
+// shared memory (16 KiB), written to the block store (bf16 or int8), and the r
+// representatives are chosen in-CTA exactly as the reference does
+// (m12_runtime.py:354-395):
+//   dir_t   = k_t / max(|k_t|, 1e-12)                 (true division, as F.normalize)
+//   mean    = sum_t dir_t / B ;  mdir = mean / max(|mean|, 1e-12)
+//   pick_0  = first argmax_t dir_t . mdir
+//   pick_s  = first argmin_t of (taken ? 2 : max(0, max_{s'<s} dir_t . dir_pick_s'))
+// The stored representative is the raw bf16 key row of each pick.
+#include "nkv_common.cuh"
+#include "nkv_host.h"
+
+namespace nkv {
+
+constexpr int ST_THREADS = 256;
+constexpr int ST_MAXB = 128;
+
+struct StoreParams {
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  long long k_row, k_head, v_row, v_head;
+  int T, hkv, B, r, start_block, max_blocks, store_kind;  // max_blocks: reps block dim
+  void* k_store;
+  void* v_store;
+  const float* k_chan_scale;
+  float* v_block_scale;
+  __nv_bfloat16* k_tok_scale;
+  __nv_bfloat16* v_tok_scale;
+  __nv_bfloat16* reps;
+  short* rep_index;
+  __nv_bfloat16* sink_k;
+  __nv_bfloat16* sink_v;
+  int sink_cap, sink_write;
+  __nv_bfloat16* ring_k;
+  __nv_bfloat16* ring_v;
+  int ring_cap, ring_pos0, ring_first;
+};
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) x += __shfl_xor_sync(FULL, x, m);
+  return x;
+}
+__device__ __forceinline__ float warp_max(float x) {
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) x = fmaxf(x, __shfl_xor_sync(FULL, x, m));
+  return x;
+}
+
+// quantize one float with a given scale, reference rounding (half to even)
+__device__ __forceinline__ signed char q8(float x, float s) {
+  float y = rintf(__fdiv_rn(x, s));
+  y = fminf(fmaxf(y, -127.f), 127.f);
+  return (signed char)(int)y;
+}
+
+__global__ void __launch_bounds__(ST_THREADS) store_kernel(StoreParams p) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int B = p.B;
+  __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(smem);           // [B][D]
+  __nv_bfloat16* vs = ks + B * NKV_D;                                    // [B][D]
+  float* nrm = reinterpret_cast<float*>(vs + B * NKV_D);                 // [B]
+  float* crit = nrm + ST_MAXB;                                           // [B]
+  float* worst = crit + ST_MAXB;                                         // [B]
+  float* mdir = worst + ST_MAXB;                                         // [D]
+  float* red = mdir + NKV_D;                                             // [8 warps]
+  __shared__ int picks[8];
+  __shared__ float s_vscale;
+
+  const int bl = blockIdx.x, h = blockIdx.y;
+  const int blk = p.start_block + bl;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  // ---- stage K and V tiles (zero padding past T) ---------------------------
+  for (int i = tid; i < B * (NKV_D / 8); i += ST_THREADS) {
+    const int t = i / (NKV_D / 8), c = i % (NKV_D / 8);
+    const int gt = bl * B + t;
+    uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+    if (gt < p.T) {
+      kv = *reinterpret_cast<const uint4*>(p.k + gt * p.k_row + h * p.k_head + c * 8);
+      vv = *reinterpret_cast<const uint4*>(p.v + gt * p.v_row + h * p.v_head + c * 8);
+    }
+    reinterpret_cast<uint4*>(ks)[i] = kv;
+    reinterpret_cast<uint4*>(vs)[i] = vv;
+  }
+  __syncthreads();
+
+  const long long tile = ((long long)blk * p.hkv + h) * B;  // row index into the store
+  // ---- block store ---------------------------------------------------------
+  if (p.k_store == nullptr) {
+    // representatives only
+  } else if (p.store_kind == NKV_STORE_BF16) {
+    uint4* ko = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.k_store) + tile * NKV_D);
+    uint4* vo = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.v_store) + tile * NKV_D);
+    for (int i = tid; i < B * (NKV_D / 8); i += ST_THREADS) {
+      ko[i] = reinterpret_cast<uint4*>(ks)[i];
+      vo[i] = reinterpret_cast<uint4*>(vs)[i];
+    }
+  } else if (p.store_kind == NKV_STORE_INT8_REF) {
+    // V block scale: max |v| over the block's tokens and dims
+    float m = 0.f;
+    for (int i = tid; i < B * NKV_D; i += ST_THREADS) m = fmaxf(m, fabsf(__bfloat162float(vs[i])));
+    m = warp_max(m);
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    if (tid == 0) {
+      float mm = 0.f;
+      for (int w = 0; w < ST_THREADS / 32; ++w) mm = fmaxf(mm, red[w]);
+      s_vscale = __fdiv_rn(fmaxf(mm, 1e-8f), 127.f);
+      p.v_block_scale[(long long)blk * p.hkv + h] = s_vscale;
+    }
+    __syncthreads();
+    const float vsc = s_vscale;
+    signed char* ko = reinterpret_cast<signed char*>(p.k_store) + tile * NKV_D;
+    signed char* vo = reinterpret_cast<signed char*>(p.v_store) + tile * NKV_D;
+    for (int i = tid; i < B * NKV_D / 4; i += ST_THREADS) {
+      const int e = i * 4, d = e % NKV_D;
+      char4 kq, vq;
+      kq.x = q8(__bfloat162float(ks[e + 0]), p.k_chan_scale[h * NKV_D + d + 0]);
+      kq.y = q8(__bfloat162float(ks[e + 1]), p.k_chan_scale[h * NKV_D + d + 1]);
+      kq.z = q8(__bfloat162float(ks[e + 2]), p.k_chan_scale[h * NKV_D + d + 2]);
+      kq.w = q8(__bfloat162float(ks[e + 3]), p.k_chan_scale[h * NKV_D + d + 3]);
+      vq.x = q8(__bfloat162float(vs[e + 0]), vsc);
+      vq.y = q8(__bfloat162float(vs[e + 1]), vsc);
+      vq.z = q8(__bfloat162float(vs[e + 2]), vsc);
+      vq.w = q8(__bfloat162float(vs[e + 3]), vsc);
+      reinterpret_cast<char4*>(ko)[i] = kq;
+      reinterpret_cast<char4*>(vo)[i] = vq;
+    }
+  } else {  // NKV_STORE_INT8_TOKEN: bf16 scale per (token) for K and V
+    signed char* ko = reinterpret_cast<signed char*>(p.k_store) + tile * NKV_D;
+    signed char* vo = reinterpret_cast<signed char*>(p.v_store) + tile * NKV_D;
+    for (int t = warp; t < B; t += ST_THREADS / 32) {
+      float kx[4], vx[4], km = 0.f, vm = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        kx[i] = __bfloat162float(ks[t * NKV_D + lane * 4 + i]);
+        vx[i] = __bfloat162float(vs[t * NKV_D + lane * 4 + i]);
+        km = fmaxf(km, fabsf(kx[i]));
+        vm = fmaxf(vm, fabsf(vx[i]));
+      }
+      km = warp_max(km);
+      vm = warp_max(vm);
+      const __nv_bfloat16 kscb = __float2bfloat16_rn(__fdiv_rn(fmaxf(km, 1e-8f), 127.f));
+      const __nv_bfloat16 vscb = __float2bfloat16_rn(__fdiv_rn(fmaxf(vm, 1e-8f), 127.f));
+      const float ksc = __bfloat162float(kscb), vsc = __bfloat162float(vscb);
+      char4 kq, vq;
+      kq.x = q8(kx[0], ksc); kq.y = q8(kx[1], ksc); kq.z = q8(kx[2], ksc); kq.w = q8(kx[3], ksc);
+      vq.x = q8(vx[0], vsc); vq.y = q8(vx[1], vsc); vq.z = q8(vx[2], vsc); vq.w = q8(vx[3], vsc);
+      reinterpret_cast<char4*>(ko + t * NKV_D)[lane] = kq;
+      reinterpret_cast<char4*>(vo + t * NKV_D)[lane] = vq;
+      if (lane == 0) {
+        p.k_tok_scale[tile + t] = kscb;
+        p.v_tok_scale[tile + t] = vscb;
+      }
+    }
+  }
+
+  // ---- sink and recent-ring rows (bf16) --------------------------------------
+  for (int i = tid; i < B * (NKV_D / 8); i += ST_THREADS) {
+    const int t = i / (NKV_D / 8), c = i % (NKV_D / 8);
+    const int gt = bl * B + t;
+    if (gt >= p.T) continue;
+    if (gt < p.sink_write) {
+      const long long o = ((long long)h * p.sink_cap + gt) * NKV_D + c * 8;
+      *reinterpret_cast<uint4*>(p.sink_k + o) = reinterpret_cast<uint4*>(ks)[i];
+      *reinterpret_cast<uint4*>(p.sink_v + o) = reinterpret_cast<uint4*>(vs)[i];
+    }
+    if (gt >= p.ring_first && p.ring_cap > 0) {
+      const int slot = (int)(((long long)p.ring_pos0 + gt) % p.ring_cap);
+      const long long o = ((long long)h * p.ring_cap + slot) * NKV_D + c * 8;
+      *reinterpret_cast<uint4*>(p.ring_k + o) = reinterpret_cast<uint4*>(ks)[i];
+      *reinterpret_cast<uint4*>(p.ring_v + o) = reinterpret_cast<uint4*>(vs)[i];
+    }
+  }
+
+  // ---- representatives ---------------------------------------------------------
+  // token norms: warp w handles tokens w, w+8, ...; lane holds 4 dims
+  for (int t = warp; t < B; t += ST_THREADS / 32) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float x = __bfloat162float(ks[t * NKV_D + lane * 4 + i]);
+      s = fmaf(x, x, s);
+    }
+    s = warp_sum(s);
+    if (lane == 0) nrm[t] = fmaxf(sqrtf(s), 1e-12f);
+  }
+  __syncthreads();
+  // mean direction: thread d sums dir_t[d] over tokens
+  if (tid < NKV_D) {
+    float s = 0.f;
+    for (int t = 0; t < B; ++t) s += __fdiv_rn(__bfloat162float(ks[t * NKV_D + tid]), nrm[t]);
+    mdir[tid] = __fdiv_rn(s, (float)B);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) s = fmaf(mdir[lane * 4 + i], mdir[lane * 4 + i], s);
+    s = warp_sum(s);
+    const float n = fmaxf(sqrtf(s), 1e-12f);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) mdir[lane * 4 + i] = __fdiv_rn(mdir[lane * 4 + i], n);
+  }
+  __syncthreads();
+
+  for (int step = 0; step < p.r; ++step) {
+    // criterion per token
+    for (int t = warp; t < B; t += ST_THREADS / 32) {
+      float s = 0.f;
+      if (step == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int d = lane * 4 + i;
+          s = fmaf(__fdiv_rn(__bfloat162float(ks[t * NKV_D + d]), nrm[t]), mdir[d], s);
+        }
+      } else {
+        const int pk = picks[step - 1];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int d = lane * 4 + i;
+          const float a = __fdiv_rn(__bfloat162float(ks[t * NKV_D + d]), nrm[t]);
+          const float b = __fdiv_rn(__bfloat162float(ks[pk * NKV_D + d]), nrm[pk]);
+          s = fmaf(a, b, s);
+        }
+      }
+      s = warp_sum(s);
+      if (lane == 0) {
+        if (step == 0) {
+          crit[t] = s;
+        } else {
+          const float w = step == 1 ? s : fmaxf(worst[t], s);
+          worst[t] = w;
+          bool taken = false;
+          for (int q = 0; q < step; ++q) taken |= (picks[q] == t);
+          crit[t] = taken ? 2.0f : fmaxf(w, 0.f);
+        }
+      }
+    }
+    __syncthreads();
+    if (warp == 0) {
+      // first index of the max (step 0) / min (later steps)
+      float best = step == 0 ? -INFINITY : INFINITY;
+      int bi = 0x7fffffff;
+      for (int t = lane; t < B; t += 32) {
+        const float c = crit[t];
+        const bool better = step == 0 ? (c > best) : (c < best);
+        if (better) { best = c; bi = t; }
+      }
+#pragma unroll
+      for (int m = 16; m > 0; m >>= 1) {
+        const float ob = __shfl_xor_sync(FULL, best, m);
+        const int oi = __shfl_xor_sync(FULL, bi, m);
+        const bool take = step == 0 ? (ob > best || (ob == best && oi < bi))
+                                    : (ob < best || (ob == best && oi < bi));
+        if (take) { best = ob; bi = oi; }
+      }
+      if (lane == 0) picks[step] = (bi >= 0 && bi < B) ? bi : 0;  // all-NaN guard
+    }
+    __syncthreads();
+  }
+  // write the chosen raw keys
+  for (int i = tid; i < p.r * (NKV_D / 8); i += ST_THREADS) {
+    const int j = i / (NKV_D / 8), c = i % (NKV_D / 8);
+    const long long o = (((long long)h * p.max_blocks + blk) * p.r + j) * NKV_D + c * 8;
+    *reinterpret_cast<uint4*>(p.reps + o) = reinterpret_cast<uint4*>(ks + picks[j] * NKV_D)[c];
+  }
+  if (p.rep_index && tid < p.r)
+    p.rep_index[((long long)h * p.max_blocks + blk) * p.r + tid] = (short)picks[tid];
+}
+
+// K channel scale: one CTA per kv head, thread = channel.
+__global__ void kscale_kernel(const __nv_bfloat16* k, int T, long long row, long long head,
+                              float* out) {
+  __shared__ float part[8][NKV_D];
+  const int h = blockIdx.x;
+  const int d = threadIdx.x & (NKV_D - 1), slice = threadIdx.x / NKV_D;  // 8 slices
+  float m = 0.f;
+  for (int t = slice; t < T; t += 8) m = fmaxf(m, fabsf(__bfloat162float(k[t * row + h * head + d])));
+  part[slice][d] = m;
+  __syncthreads();
+  if (slice == 0) {
+    for (int s = 1; s < 8; ++s) m = fmaxf(m, part[s][d]);
+    out[h * NKV_D + d] = __fdiv_rn(fmaxf(m, 1e-8f), 127.f);
+  }
+}
+
+// Query-segment means: grid (nseg, hq), thread = dim.
+__global__ void qsum_kernel(const __nv_bfloat16* q, int T, long long row, long long head, int nseg,
+                            __nv_bfloat16* out) {
+  const int s = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  // torch.tensor_split: the first T % nseg segments hold one extra row
+  const int base = T / nseg, extra = T % nseg;
+  const int lo = s * base + min(s, extra);
+  const int n = base + (s < extra ? 1 : 0);
+  float acc = 0.f;
+  for (int t = lo; t < lo + n; ++t) acc += __bfloat162float(q[t * row + h * head + d]);
+  out[((long long)s * gridDim.y + h) * NKV_D + d] = __float2bfloat16_rn(__fdiv_rn(acc, (float)n));
+}
+
+// Paged-cache scatter: grid n rows.
+__global__ void kvcache_kernel(const __nv_bfloat16* key, long long ks, const __nv_bfloat16* value,
+                               long long vs, __nv_bfloat16* kc, __nv_bfloat16* vc,
+                               const long long* slot, int row_elems) {
+  const int i = blockIdx.x;
+  const long long s = slot[i];
+  if (s == -1) return;
+  const bool vec = (row_elems % 8) == 0 && (ks % 8) == 0 && (vs % 8) == 0;
+  if (vec) {
+    for (int c = threadIdx.x; c < row_elems / 8; c += blockDim.x) {
+      reinterpret_cast<uint4*>(kc + s * row_elems)[c] = reinterpret_cast<const uint4*>(key + i * ks)[c];
+      reinterpret_cast<uint4*>(vc + s * row_elems)[c] = reinterpret_cast<const uint4*>(value + i * vs)[c];
+    }
+  } else {
+    for (int c = threadIdx.x; c < row_elems; c += blockDim.x) {
+      kc[s * row_elems + c] = key[i * ks + c];
+      vc[s * row_elems + c] = value[i * vs + c];
+    }
+  }
+}
+
+// Recent-ring append: token i (i >= first) of a T-token run goes to slot
+// (pos0 + i) % cap of every head.  grid (T - first), 2*hkv*16 threads max.
+__global__ void ring_append_kernel(const __nv_bfloat16* k, const __nv_bfloat16* v, long long kr,
+                                   long long kh, long long vr, long long vh, int first, int hkv,
+                                   __nv_bfloat16* ring_k, __nv_bfloat16* ring_v, int cap, int pos0) {
+  const int i = first + blockIdx.x;
+  const int slot = (int)(((long long)pos0 + i) % cap);
+  for (int e = threadIdx.x; e < hkv * 16; e += blockDim.x) {
+    const int h = e / 16, c = e % 16;
+    const long long o = ((long long)h * cap + slot) * NKV_D + c * 8;
+    *reinterpret_cast<uint4*>(ring_k + o) = *reinterpret_cast<const uint4*>(k + i * kr + h * kh + c * 8);
+    *reinterpret_cast<uint4*>(ring_v + o) = *reinterpret_cast<const uint4*>(v + i * vr + h * vh + c * 8);
+  }
+}
+
+}  // namespace nkv
+
+using namespace nkv;
+
+extern "C" int nkv_ring_append(nkv_stream_t stream, const void* k, const void* v, int T,
+                               int64_t k_row_stride, int64_t k_head_stride, int64_t v_row_stride,
+                               int64_t v_head_stride, int hkv, int head_dim, void* ring_k,
+                               void* ring_v, int ring_cap, int ring_pos0) {
+  NKV_SUPPORTED(head_dim == NKV_D, "ring_append: head_dim %d unsupported", head_dim);
+  NKV_REQUIRE(ring_cap >= 1 && ring_pos0 >= 0 && hkv >= 1, "ring_append: bad ring");
+  if (T <= 0) return NKV_OK;
+  NKV_REQUIRE(k && v && ring_k && ring_v, "ring_append: null pointer");
+  NKV_REQUIRE(((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0 && k_row_stride % 8 == 0 &&
+                  k_head_stride % 8 == 0 && v_row_stride % 8 == 0 && v_head_stride % 8 == 0,
+              "ring_append: k/v must be 16-byte aligned with strides multiple of 8 elements");
+  const int first = T > ring_cap ? T - ring_cap : 0;
+  ring_append_kernel<<<T - first, 128, 0, (cudaStream_t)stream>>>(
+      (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, k_row_stride, k_head_stride, v_row_stride,
+      v_head_stride, first, hkv, (__nv_bfloat16*)ring_k, (__nv_bfloat16*)ring_v, ring_cap, ring_pos0);
+  return check_launch("ring_append");
+}
+
+extern "C" int nkv_store_chunk(nkv_stream_t stream, const nkv_store_args* a) {
+  NKV_REQUIRE(a, "store: null args");
+  NKV_SUPPORTED(a->head_dim == NKV_D, "store: head_dim %d unsupported (128 only)", a->head_dim);
+  NKV_SUPPORTED(a->block_size == 16 || a->block_size == 32 || a->block_size == 64 ||
+                    a->block_size == 128,
+                "store: block_size %d unsupported", a->block_size);
+  NKV_SUPPORTED(a->r >= 1 && a->r <= 8 && a->r <= a->block_size, "store: r=%d unsupported", a->r);
+  NKV_REQUIRE(a->T >= 1 && a->hkv >= 1, "store: empty chunk");
+  const int nb = (a->T + a->block_size - 1) / a->block_size;
+  NKV_REQUIRE(a->start_block >= 0 && a->start_block + nb <= a->max_blocks,
+              "store: blocks [%d, %d) exceed the representative capacity %d", a->start_block,
+              a->start_block + nb, a->max_blocks);
+  NKV_REQUIRE(!a->k_store || a->start_block + nb <= a->store_blocks,
+              "store: blocks [%d, %d) exceed the block-store capacity %d", a->start_block,
+              a->start_block + nb, a->store_blocks);
+  NKV_REQUIRE(a->k && a->v && a->reps, "store: null k/v/reps");
+  NKV_REQUIRE((a->k_store == nullptr) == (a->v_store == nullptr),
+              "store: k_store and v_store must both be set or both be NULL (reps only)");
+  NKV_REQUIRE(a->store_kind >= 0 && a->store_kind <= 2, "store: bad store_kind");
+  NKV_REQUIRE(!a->k_store || a->store_kind != NKV_STORE_INT8_REF || (a->k_chan_scale && a->v_block_scale),
+              "store: int8 reference scheme needs k_chan_scale and v_block_scale");
+  NKV_REQUIRE(!a->k_store || a->store_kind != NKV_STORE_INT8_TOKEN || (a->k_tok_scale && a->v_tok_scale),
+              "store: int8 token scheme needs k_tok_scale and v_tok_scale");
+  NKV_REQUIRE(a->sink_write <= 0 || (a->sink_k && a->sink_v && a->sink_write <= a->sink_cap),
+              "store: bad sink arguments");
+  NKV_REQUIRE(a->ring_cap <= 0 || (a->ring_k && a->ring_v && a->ring_pos0 >= 0),
+              "store: bad ring arguments");
+  NKV_REQUIRE(((uintptr_t)a->k & 15) == 0 && ((uintptr_t)a->v & 15) == 0 &&
+                  a->k_row_stride % 8 == 0 && a->k_head_stride % 8 == 0 &&
+                  a->v_row_stride % 8 == 0 && a->v_head_stride % 8 == 0,
+              "store: k/v must be 16-byte aligned with strides multiple of 8 elements");
+  StoreParams p;
+  p.k = (const __nv_bfloat16*)a->k;
+  p.v = (const __nv_bfloat16*)a->v;
+  p.k_row = a->k_row_stride;
+  p.k_head = a->k_head_stride;
+  p.v_row = a->v_row_stride;
+  p.v_head = a->v_head_stride;
+  p.T = a->T;
+  p.hkv = a->hkv;
+  p.B = a->block_size;
+  p.r = a->r;
+  p.start_block = a->start_block;
+  p.max_blocks = a->max_blocks;
+  p.store_kind = a->store_kind;
+  p.k_store = a->k_store;
+  p.v_store = a->v_store;
+  p.k_chan_scale = a->k_chan_scale;
+  p.v_block_scale = a->v_block_scale;
+  p.k_tok_scale = (__nv_bfloat16*)a->k_tok_scale;
+  p.v_tok_scale = (__nv_bfloat16*)a->v_tok_scale;
+  p.reps = (__nv_bfloat16*)a->reps;
+  p.rep_index = a->rep_index;
+  p.sink_k = (__nv_bfloat16*)a->sink_k;
+  p.sink_v = (__nv_bfloat16*)a->sink_v;
+  p.sink_cap = a->sink_cap;
+  p.sink_write = a->sink_write > 0 ? a->sink_write : 0;
+  p.ring_k = (__nv_bfloat16*)a->ring_k;
+  p.ring_v = (__nv_bfloat16*)a->ring_v;
+  p.ring_cap = a->ring_cap > 0 ? a->ring_cap : 0;
+  p.ring_pos0 = a->ring_pos0;
+  p.ring_first = a->ring_first;
+  const size_t smem = 2 * (size_t)a->block_size * NKV_D * 2 + (3 * ST_MAXB + NKV_D + 8) * 4;
+  if (ensure_smem(store_kernel, smem, "store_chunk")) return NKV_ERR_CUDA;
+  dim3 grid(nb, a->hkv);
+  store_kernel<<<grid, ST_THREADS, smem, (cudaStream_t)stream>>>(p);
+  return check_launch("store_chunk");
+}
+
+extern "C" int nkv_k_channel_scale(nkv_stream_t stream, const void* k, int T, int64_t row_stride,
+                                   int64_t head_stride, int hkv, int head_dim, float* out_scale) {
+  NKV_REQUIRE(k && out_scale && T >= 1 && hkv >= 1, "k_channel_scale: bad arguments");
+  NKV_SUPPORTED(head_dim == NKV_D, "k_channel_scale: head_dim %d unsupported", head_dim);
+  kscale_kernel<<<hkv, 8 * NKV_D, 0, (cudaStream_t)stream>>>((const __nv_bfloat16*)k, T, row_stride,
+                                                            head_stride, out_scale);
+  return check_launch("k_channel_scale");
+}
+
+extern "C" int nkv_query_summaries(nkv_stream_t stream, const void* q, int T, int64_t row_stride,
+                                   int64_t head_stride, int hq, int head_dim, int nseg, void* out) {
+  NKV_REQUIRE(q && out && T >= 1 && hq >= 1 && nseg >= 1, "query_summaries: bad arguments");
+  NKV_SUPPORTED(head_dim == NKV_D, "query_summaries: head_dim %d unsupported", head_dim);
+  if (nseg > T) nseg = T;
+  dim3 grid(nseg, hq);
+  qsum_kernel<<<grid, NKV_D, 0, (cudaStream_t)stream>>>((const __nv_bfloat16*)q, T, row_stride,
+                                                       head_stride, nseg, (__nv_bfloat16*)out);
+  return check_launch("query_summaries");
+}
+
+extern "C" int nkv_store_kvcache(nkv_stream_t stream, const void* key, int64_t key_stride,
+                                 const void* value, int64_t value_stride, void* k_cache,
+                                 void* v_cache, const int64_t* slot_mapping, int n, int row_elems) {
+  NKV_REQUIRE(row_elems >= 1, "store_kvcache: bad row size");
+  if (n <= 0) return NKV_OK;
+  NKV_REQUIRE(key && value && k_cache && v_cache && slot_mapping, "store_kvcache: null pointer");
+  kvcache_kernel<<<n, 128, 0, (cudaStream_t)stream>>>(
+      (const __nv_bfloat16*)key, key_stride, (const __nv_bfloat16*)value, value_stride,
+      (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, (const long long*)slot_mapping, row_elems);
+  return check_launch("store_kvcache");
+}
