@@ -4,22 +4,27 @@
 // (m12_runtime.py:1240-1308 decode, :716-749 verify):
 //   [ selected blocks (block_ids order) | sink | recent ring slice | current ]
 // They are never packed.  The grid is (splits, hkv); CTA (s, h) owns logical
-// keys [s*tps, (s+1)*tps) of head h and
-//   1. moves them into shared memory: one cp.async.bulk per contiguous piece
-//      (a 16 KiB block-store tile is one piece) for bf16 data, or 128-bit
-//      loads + in-register dequant for an int8 store (which may live in mapped
-//      pinned host memory: the offload mode); K copies are issued before V so
-//      Q.K overlaps the V transfer,
-//   2. scores all its keys for the nq*G query rows of the head (fp32, masked:
-//      causal for current tokens, the per-row allowed mask for selected blocks),
-//   3. exponentiates against the split max and accumulates P.V,
-//   4. merges the splits with the log-sum-exp rule and writes bf16: when the
-//      splits of a head fit one thread-block cluster (<= 16 CTAs) the partials
-//      stay in shared memory and are read by the peers through DSMEM between
-//      two cluster barriers; otherwise they go to the workspace and the last
-//      CTA of the head (atomic ticket, no spinning) merges them.
+// keys [s*tps, (s+1)*tps) of head h.  Two kernels share that structure:
+//
+//  decode_kernel (nq == 1, the hot path): the CTA's keys are fetched by 2D TMA
+//  (64- and 8-row boxes, 128-byte swizzle) into shared memory, one mbarrier per
+//  contiguous piece; int8, host-resident and current-token rows are loaded by
+//  the threads into the same layout.  Q.K and P.V run on the tensor cores
+//  (mma.sync m16n8k16, bf16 in, fp32 accumulate), one slice of <= 48 keys per
+//  warp.  The splits of a head form one thread-block cluster (<= 16 CTAs) and
+//  merge through DSMEM, or go through the workspace.
+//
+//  attend_kernel (nq > 1, verify): one cp.async.bulk per contiguous piece for
+//  bf16 data or 128-bit loads + in-register dequant for an int8 store; scores
+//  all keys for the nq*G query rows (causal for current tokens, the per-row
+//  allowed mask for selected blocks), fp32 softmax and P.V, the same merges.
+//
+// Merges use the log-sum-exp rule and write bf16.  Without a cluster, the last
+// CTA of a head (atomic ticket, no spinning) merges the workspace partials.
 #include <cooperative_groups.h>
+#include <cuda.h>  // CUtensorMap (encoded through the runtime's driver entry point)
 #include <stdlib.h>
+#include <string.h>
 
 #include "nkv_common.cuh"
 #include "nkv_host.h"
@@ -39,7 +44,6 @@ constexpr int AT_CLUSTER_MAX = 16;        // splits of one head merged through D
 constexpr int AT_TPS_MAX_CLUSTER = 384;   // keys per CTA in cluster mode (K+V: 192 KiB)
 constexpr int AT_MAX_SLOTS = 32;          // block slots one CTA can touch (tps / B + 2)
 constexpr int AT_MAX_PIECES = AT_MAX_SLOTS + 8;  // + sink, two ring pieces, current tokens
-constexpr size_t AT_SMEM_ONE_PER_SM = 116 * 1024;  // > half of the SM's 228 KiB
 
 struct AttendParams {
   const __nv_bfloat16* q;
@@ -79,8 +83,17 @@ struct AttendParams {
   int overlap;  // 1: wait for the preceding (select) grid before touching ids
   int cluster;  // 1: the splits of a head form one thread-block cluster (DSMEM merge)
   int log2B;    // block_size is a power of two
-  int push;     // decode cluster merge: 1 = push to rank 0, 0 = pull by every CTA
   int stop;     // checked builds only: end the decode kernel after phase `stop` (timing probes)
+  // decode kernel: tile rows per K (or V) tile, bytes of the K-tile region,
+  // segments TMA may read (1 selected blocks, 2 sink, 4 ring: bf16 in device memory)
+  int tile_rows, region_k, tma_mask;
+};
+
+// 2D tensor maps of the decode kernel over [rows][128] bf16 sources with
+// 64-column boxes and 128-byte swizzle: m[source][K|V][box], source 0 = block
+// store, 1 = sink, 2 = recent ring; box 0 = 8 rows, 1 = 64 rows.
+struct DecodeMaps {
+  CUtensorMap m[3][2][2];
 };
 
 __device__ __forceinline__ long long clamp_id(const AttendParams& p, int slot, bool* bad) {
@@ -254,74 +267,6 @@ __device__ void load_int8(const AttendParams& p, int h, int t0, int t1, __nv_bfl
   }
 }
 
-// Same as load_int8 with a shared-memory row pitch (elements).
-__device__ void load_int8_pitched(const AttendParams& p, int h, int t0, int t1, __nv_bfloat16* ks,
-                                  __nv_bfloat16* vs, int pitch) {
-  const int B = p.B;
-  const int selEnd = min(p.n_sel * B, t1);
-  if (t0 >= selEnd) return;
-  const int nt = selEnd - t0;
-  const signed char* kst = reinterpret_cast<const signed char*>(p.k_store);
-  const signed char* vst = reinterpret_cast<const signed char*>(p.v_store);
-  constexpr int U = 4;
-  for (int base = threadIdx.x; base < nt * 8; base += (int)blockDim.x * U) {
-    uint4 kr[U], vr[U];
-    long long ids[U];
-    int rows[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int i = base + u * (int)blockDim.x;
-      rows[u] = -1;
-      if (i < nt * 8) {
-        const int t = i >> 3, c = i & 7;
-        const int pos = t0 + t, slot = pos / B, off = pos % B;
-        bool bad;
-        const long long id = clamp_id(p, slot, &bad);
-        ids[u] = id;
-        rows[u] = t * 8 + c;
-        const long long o = ((id * p.hkv + h) * B + off) * NKV_D + c * 16;
-        kr[u] = ldg_nc_v4(kst + o);
-        vr[u] = ldg_nc_v4(vst + o);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (rows[u] < 0) continue;
-      const int t = rows[u] >> 3, c = rows[u] & 7;
-      const int pos = t0 + t, off = pos % B;
-      const signed char* kb = reinterpret_cast<const signed char*>(&kr[u]);
-      const signed char* vb = reinterpret_cast<const signed char*>(&vr[u]);
-      uint32_t kw[8], vw[8];
-      if (p.kind == NKV_STORE_INT8_REF) {
-        const float vsc = __ldg(p.vbs + ids[u] * p.hkv + h);
-#pragma unroll
-        for (int e = 0; e < 16; e += 2) {
-          const int d = c * 16 + e;
-          const float k0 = (float)kb[e] * __ldg(p.kcs + h * NKV_D + d);
-          const float k1 = (float)kb[e + 1] * __ldg(p.kcs + h * NKV_D + d + 1);
-          kw[e / 2] = (uint32_t)f2bf(k0) | ((uint32_t)f2bf(k1) << 16);
-          vw[e / 2] = (uint32_t)f2bf((float)vb[e] * vsc) | ((uint32_t)f2bf((float)vb[e + 1] * vsc) << 16);
-        }
-      } else {
-        const long long so = (ids[u] * p.hkv + h) * B + off;
-        const float ksc = __bfloat162float(p.kts[so]);
-        const float vsc = __bfloat162float(p.vts[so]);
-#pragma unroll
-        for (int e = 0; e < 16; e += 2) {
-          kw[e / 2] = (uint32_t)f2bf((float)kb[e] * ksc) | ((uint32_t)f2bf((float)kb[e + 1] * ksc) << 16);
-          vw[e / 2] = (uint32_t)f2bf((float)vb[e] * vsc) | ((uint32_t)f2bf((float)vb[e + 1] * vsc) << 16);
-        }
-      }
-      uint4* kd = reinterpret_cast<uint4*>(ks + (long long)t * pitch + c * 16);
-      uint4* vd = reinterpret_cast<uint4*>(vs + (long long)t * pitch + c * 16);
-      kd[0] = make_uint4(kw[0], kw[1], kw[2], kw[3]);
-      kd[1] = make_uint4(kw[4], kw[5], kw[6], kw[7]);
-      vd[0] = make_uint4(vw[0], vw[1], vw[2], vw[3]);
-      vd[1] = make_uint4(vw[4], vw[5], vw[6], vw[7]);
-    }
-  }
-}
-
 // Sum of G per-head partials over the 8 lanes of a token group, transposed:
 // each step keeps half of the remaining heads and ships the other half to the
 // partner lane, so G=4 costs 4 shuffles instead of 12.  Lane c (= lane & 7)
@@ -401,9 +346,6 @@ template <int G>
 __device__ void combine_splits(const AttendParams& p, int h, float* wbuf);
 template <int G>
 __device__ void combine_cluster(const AttendParams& p, int h, float* pm, float* pl, float* po);
-template <int G>
-__device__ void push_merge(const AttendParams& p, int h, const float* pm, const float* pl, const float* po,
-                           float* recv);
 
 template <int G, bool Q1>
 __global__ void __launch_bounds__(AT_THREADS) attend_kernel(AttendParams p) {
@@ -742,100 +684,251 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return (uint32_t)f2bf(lo) | ((uint32_t)f2bf(hi) << 16);
 }
 
-constexpr int KPITCH = NKV_D + 8;  // smem row pitch (elements): 272 B keeps ldmatrix conflict-free
+// ---------------------------------------------------------------------------
+// Decode tiles.  The K and V keys of a CTA sit in shared memory as
+// [2][rows][128 B] (the two 64-column halves of a key row) in the 128-byte
+// swizzle that TMA writes: 16-byte chunk c of row r is stored at chunk
+// c ^ (r & 7).  The tile base is 1024-byte aligned and every piece starts at a
+// multiple of 8 rows, so rows loaded by TMA and rows loaded by threads share one
+// pattern, and the 8 rows of one ldmatrix matrix fall in 8 different bank groups.
+// ---------------------------------------------------------------------------
+constexpr int DT_PAD_ROWS = 32;  // tile rows beyond tps: padding of <= 4 pieces of ragged length
+enum : int { PT_SEL = 0, PT_SINK = 1, PT_RING = 2, PT_THREADS = 3, PT_SKIP = 4, PT_EMPTY = 5 };
 
-// Single-query decode (nq == 1) on the tensor cores.  Every warp owns a slice
-// of up to 48 keys of the CTA's range and fetches that slice itself with
-// 16-byte cp.async copies (K as one commit group, V as a second), into shared
-// memory rows with a 272-byte pitch so that ldmatrix reads are conflict-free.
-// Copies of keys that do not depend on the selection are issued before the
-// programmatic-dependent-launch wait; the selected blocks right after it.
-//   S = Q K^T   : A = the G query rows (rows >= G are zero), B = K via ldmatrix
-//   softmax     : on the accumulator fragments (quad shuffles); keys past the
-//                 slice or invisible are masked to -inf
-//   O += P V    : the score fragments become the A operand (bf16), V via
-//                 ldmatrix.trans
-// The warp partials (m, l, o) are merged through shared memory, then across
-// the splits (cluster DSMEM merge or workspace merge).
-template <int G>
-__device__ __forceinline__ void slice_copy(const AttendParams& p, int h, int t0, int lo, int hi, int lane,
-                                           __nv_bfloat16* ks, __nv_bfloat16* vs, int selEnd, int sinkEnd,
-                                           int ringEnd, const long long* s_ids, int slot0, bool selected,
-                                           bool want_k) {
-  // lane (r2, chunk): rows lo + r2, lo + r2 + 2, ...; 16-byte chunk of 16
-  const int chunk = lane & 15, r2 = lane >> 4;
-  for (int r = lo + r2; r < hi; r += 2) {
-    const int pos = t0 + r;
-    const bool is_sel = pos < selEnd;
-    if (is_sel != selected) continue;
-    const __nv_bfloat16* src;
-    if (is_sel) {
-      long long id = s_ids[(pos >> p.log2B) - slot0];
-      if (id < 0) id = 0;  // masked in the scores
-      const long long o = ((id * p.hkv + h) * p.B + (pos & (p.B - 1))) * NKV_D;
-      src = reinterpret_cast<const __nv_bfloat16*>(want_k ? p.k_store : p.v_store) + o;
-    } else if (pos < sinkEnd) {
-      src = (want_k ? p.sink_k : p.sink_v) + ((long long)h * p.sink_cap + (pos - selEnd)) * NKV_D;
-    } else if (pos < ringEnd) {
-      int phys = p.ring_start + (pos - sinkEnd);
-      if (phys >= p.ring_cap) phys -= p.ring_cap;
-      src = (want_k ? p.ring_k : p.ring_v) + ((long long)h * p.ring_cap + phys) * NKV_D;
-    } else {
-      src = (want_k ? p.cur_k : p.cur_v) + (long long)(pos - ringEnd) * p.cur_row + (long long)h * p.cur_head;
-    }
-    cp_async16((want_k ? ks : vs) + (long long)r * KPITCH + chunk * 8, src + chunk * 8);
+__device__ __forceinline__ uint32_t swz(int nrows, int row, int col) {
+  return (uint32_t)((((col >> 6) * nrows + row) << 7) + ((((col & 63) >> 3) ^ (row & 7)) << 4) + ((col & 7) << 1));
+}
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+// One box (8 or 64 rows x 64 columns) of a [rows][128] bf16 tensor into swizzled shared memory.
+__device__ __forceinline__ void tma_box(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// TMA boxes of one piece: `len` rows of source `src` from row y0, into tile
+// rows row0...: 64-row boxes while 64 rows remain, then 8-row boxes; the
+// (box, half, K|V) jobs are spread over the lanes of the calling warp.
+__device__ __forceinline__ void issue_piece(const DecodeMaps& tm, int src, int y0, int len, int row0,
+                                            unsigned char* kt, unsigned char* vt, int NR, uint64_t* kb,
+                                            uint64_t* vb, int lane) {
+  const int nbig = len >> 6, nsmall = ((len & 63) + 7) >> 3;
+  const int jobs = (nbig + nsmall) * 4;
+  for (int j = lane; j < jobs; j += 32) {
+    const int b = j >> 2, half = (j >> 1) & 1, isv = j & 1;
+    const bool big = b < nbig;
+    const int r = big ? b * 64 : nbig * 64 + (b - nbig) * 8;
+    unsigned char* dst = (isv ? vt : kt) + ((size_t)half * NR + row0 + r) * 128;
+    tma_box(dst, &tm.m[src][isv][big ? 1 : 0], half * 64, y0 + r, isv ? vb : kb);
   }
 }
 
+// Rows [pos0, pos0 + len) of the logical keys, loaded by the threads of the
+// CTA into tile rows row0... : 16-byte copies for bf16 sources (the current
+// tokens, a host-resident store, any segment TMA cannot address), in-register
+// dequant for an int8 store (reference scheme: per-channel K scale, per-block
+// V scale; token scheme: per-token bf16 scales).
+__device__ void thread_rows(const AttendParams& p, int h, int pos0, int len, int row0, unsigned char* kt,
+                            unsigned char* vt, int NR, const long long* s_ids, int slot0, int selEnd, int sinkEnd,
+                            int ringEnd) {
+  const int B = p.B;
+  if (pos0 < selEnd && p.kind != NKV_STORE_BF16) {
+    const signed char* kst = reinterpret_cast<const signed char*>(p.k_store);
+    const signed char* vst = reinterpret_cast<const signed char*>(p.v_store);
+    for (int i = threadIdx.x; i < len * 8; i += blockDim.x) {
+      const int r = i >> 3, c = i & 7, pos = pos0 + r, off = pos & (B - 1);
+      long long id = s_ids[(pos >> p.log2B) - slot0];
+      if (id < 0) id = 0;  // masked in the scores
+      const long long o = ((id * p.hkv + h) * B + off) * NKV_D + c * 16;
+      if (!NKV_INB(p.err, 14, o, 16, p.ext_store)) continue;
+      const uint4 kr = ldg_nc_v4(kst + o), vr = ldg_nc_v4(vst + o);
+      const signed char* kb = reinterpret_cast<const signed char*>(&kr);
+      const signed char* vb = reinterpret_cast<const signed char*>(&vr);
+      uint32_t kw[8], vw[8];
+      if (p.kind == NKV_STORE_INT8_REF) {
+        const float vsc = __ldg(p.vbs + id * p.hkv + h);
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) {
+          const int d = c * 16 + e;
+          const float k0 = (float)kb[e] * __ldg(p.kcs + h * NKV_D + d);
+          const float k1 = (float)kb[e + 1] * __ldg(p.kcs + h * NKV_D + d + 1);
+          kw[e / 2] = (uint32_t)f2bf(k0) | ((uint32_t)f2bf(k1) << 16);
+          vw[e / 2] = (uint32_t)f2bf((float)vb[e] * vsc) | ((uint32_t)f2bf((float)vb[e + 1] * vsc) << 16);
+        }
+      } else {
+        const long long so = (id * p.hkv + h) * B + off;
+        const float ksc = __bfloat162float(p.kts[so]);
+        const float vsc = __bfloat162float(p.vts[so]);
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) {
+          kw[e / 2] = (uint32_t)f2bf((float)kb[e] * ksc) | ((uint32_t)f2bf((float)kb[e + 1] * ksc) << 16);
+          vw[e / 2] = (uint32_t)f2bf((float)vb[e] * vsc) | ((uint32_t)f2bf((float)vb[e + 1] * vsc) << 16);
+        }
+      }
+      const int row = row0 + r;
+      *reinterpret_cast<uint4*>(kt + swz(NR, row, c * 16)) = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+      *reinterpret_cast<uint4*>(kt + swz(NR, row, c * 16 + 8)) = make_uint4(kw[4], kw[5], kw[6], kw[7]);
+      *reinterpret_cast<uint4*>(vt + swz(NR, row, c * 16)) = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+      *reinterpret_cast<uint4*>(vt + swz(NR, row, c * 16 + 8)) = make_uint4(vw[4], vw[5], vw[6], vw[7]);
+    }
+    return;
+  }
+  for (int i = threadIdx.x; i < len * 16; i += blockDim.x) {
+    const int r = i >> 4, c = i & 15, pos = pos0 + r;
+    const __nv_bfloat16 *ksrc, *vsrc;
+    long long o;
+    [[maybe_unused]] long long ext;
+    if (pos < selEnd) {
+      long long id = s_ids[(pos >> p.log2B) - slot0];
+      if (id < 0) id = 0;
+      o = ((id * p.hkv + h) * B + (pos & (B - 1))) * NKV_D;
+      ksrc = reinterpret_cast<const __nv_bfloat16*>(p.k_store);
+      vsrc = reinterpret_cast<const __nv_bfloat16*>(p.v_store);
+      ext = p.ext_store;
+    } else if (pos < sinkEnd) {
+      o = ((long long)h * p.sink_cap + (pos - selEnd)) * NKV_D;
+      ksrc = p.sink_k;
+      vsrc = p.sink_v;
+      ext = p.ext_sink;
+    } else if (pos < ringEnd) {
+      int phys = p.ring_start + (pos - sinkEnd);
+      if (phys >= p.ring_cap) phys -= p.ring_cap;
+      o = ((long long)h * p.ring_cap + phys) * NKV_D;
+      ksrc = p.ring_k;
+      vsrc = p.ring_v;
+      ext = p.ext_ring;
+    } else {
+      o = (long long)(pos - ringEnd) * p.cur_row + (long long)h * p.cur_head;
+      ksrc = p.cur_k;
+      vsrc = p.cur_v;
+      ext = p.ext_cur;
+    }
+    if (!NKV_INB(p.err, 15, o + c * 8, 8, ext)) continue;
+    const uint4 kv = ldg_nc_v4(ksrc + o + c * 8), vv = ldg_nc_v4(vsrc + o + c * 8);
+    *reinterpret_cast<uint4*>(kt + swz(NR, row0 + r, c * 8)) = kv;
+    *reinterpret_cast<uint4*>(vt + swz(NR, row0 + r, c * 8)) = vv;
+  }
+}
+
+// Single-query decode (nq == 1) on the tensor cores.
+//  data:   the CTA's keys are cut into pieces that are contiguous in one
+//          source (a selected block, the sink, one or two runs of the recent
+//          ring, the current token).  A piece in device memory is fetched by
+//          2D TMA boxes of 8 rows x 64 columns into its own 8-row-aligned rows
+//          of the swizzled tiles, with one mbarrier for its K and one for its
+//          V; the rest (current tokens, int8 or host-resident blocks) is loaded
+//          by the threads.  Copies that do not depend on the selection are
+//          issued before the programmatic-dependent-launch wait, the selected
+//          blocks right after it.
+//  math:   a warp owns a slice of up to 48 keys and starts as soon as the
+//          pieces of its slice have landed.  S = Q K^T with mma.sync m16n8k16
+//          (A = the G query rows, rows >= G zero; B = K via ldmatrix), softmax
+//          on the accumulator fragments, O += P V with P as the bf16 A operand
+//          and V via ldmatrix.trans.
+//  merge:  warp partials through shared memory (over the K tile, after every
+//          warp is done with it), then the splits of a head through the
+//          cluster (DSMEM) or the workspace.
 template <int G>
-__global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(AttendParams p) {
-  extern __shared__ __align__(128) unsigned char sm[];
+__global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendParams p,
+                                                               const __grid_constant__ DecodeMaps tm) {
+  extern __shared__ __align__(16) unsigned char sm_raw[];
+  __shared__ __align__(8) uint64_t kbar[AT_MAX_PIECES], vbar[AT_MAX_PIECES];
+  __shared__ int plo[AT_MAX_PIECES + 1], plen[AT_MAX_PIECES], prow[AT_MAX_PIECES], ptype[AT_MAX_PIECES];
+  __shared__ unsigned s_thr[2];  // pieces the threads load (bit i of the 64-bit pair = piece i)
   __shared__ unsigned s_ticket;
   __shared__ long long s_ids[AT_MAX_SLOTS];
+  __shared__ short srow[AT_TPS_MAX_CLUSTER];
   constexpr int NW = DK<G>::WARPS;
 
   const int split = blockIdx.x, h = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int t0 = split * p.tps, t1 = min(p.ntok, t0 + p.tps), n = t1 - t0;
-  const int selEnd = p.n_sel * p.B, sinkEnd = selEnd + p.sink_len, ringEnd = sinkEnd + p.ring_len;
+  const int B = p.B;
+  const int selEnd = p.n_sel * B, sinkEnd = selEnd + p.sink_len, ringEnd = sinkEnd + p.ring_len;
   const int slot0 = t0 >> p.log2B;
   const int nslots = t0 < selEnd ? ((min(t1, selEnd) - 1) >> p.log2B) - slot0 + 1 : 0;
-  const bool int8 = p.kind != NKV_STORE_BF16;
-
-  __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(sm);          // [tps][KPITCH]
-  __nv_bfloat16* vs = ks + (long long)p.tps * KPITCH;                 // [tps][KPITCH]
-  float* wpo = reinterpret_cast<float*>(vs + (long long)p.tps * KPITCH);  // [NW][G][D]
-  float* wml = wpo + NW * G * NKV_D;                                  // [NW][G][2]
-  float* pm = wml + NW * G * 2;                                       // [G] CTA partial
-  float* pl = pm + 64;
-  float* po = pl + 64;                                                // [G][D]
-  float* recv = po + G * NKV_D;                                       // [C][G][D + 2] (cluster)
+  const int NR = p.tile_rows;
+  unsigned char* sm = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);
+  unsigned char* kt = sm;                          // K tile, later the warp partials
+  unsigned char* vt = sm + (size_t)p.region_k;     // V tile, later the CTA partial
 
 #ifdef NKV_CHECKED
   int* trc = p.trace ? p.trace + (blockIdx.y * gridDim.x + blockIdx.x) * 64 : nullptr;
 #else
-  int* trc = nullptr;
+  [[maybe_unused]] int* trc = nullptr;
 #endif
   NKV_STAMP(trc, 48);
 
-  // this warp's slice [lo, hi), 8-aligned, at most 48 keys
-  const int tpw = ((n + NW - 1) / NW + 7) / 8 * 8;
-  const int lo = min(n, warp * tpw), hi = min(n, lo + tpw);
-
-  // keys that do not depend on the selection (sink, ring, current)
-  slice_copy<G>(p, h, t0, lo, hi, lane, ks, vs, selEnd, sinkEnd, ringEnd, s_ids, slot0, false, true);
-  slice_copy<G>(p, h, t0, lo, hi, lane, ks, vs, selEnd, sinkEnd, ringEnd, s_ids, slot0, false, false);
-  // decode: append the current token to the recent ring (a slot no CTA reads)
-  if (split == 0 && p.ring_write_pos >= 0 && tid >= 64 && tid < 96 &&
-      NKV_INB(p.err, 40, ((long long)h * p.ring_cap + p.ring_write_pos) * NKV_D, NKV_D, p.ext_ring) &&
-      NKV_INB(p.err, 41, h * p.cur_head, NKV_D, p.ext_cur)) {
-    const int c = tid & 15;
-    const bool isv = (tid & 16) != 0;
-    const __nv_bfloat16* src = (isv ? p.cur_v : p.cur_k) + h * p.cur_head + c * 8;
-    __nv_bfloat16* dst = (isv ? p.ring_v : p.ring_k) + ((long long)h * p.ring_cap + p.ring_write_pos) * NKV_D + c * 8;
-    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+  // ---- pieces ------------------------------------------------------------------------
+  // Fixed table: pieces [0, nslots) are the selected blocks the range touches,
+  // then the sink, the ring run up to the physical wrap, the run after it and
+  // the current tokens (each possibly empty).  Piece i is computed by thread i
+  // in O(1).  Selected pieces keep their key offset as tile row (their lengths
+  // are multiples of 8 because tps and block_size are); the others follow,
+  // each rounded up to 8 rows.
+  const int np = nslots + 4;
+  bool by_threads = false;
+  if (tid < np) {
+    auto clampk = [&](int x) { return min(max(x, t0), t1); };
+    int a, b, row = 0, type;
+    if (tid < nslots) {
+      a = max(t0, (slot0 + tid) * B);
+      b = min(min(t1, selEnd), (slot0 + tid + 1) * B);
+      row = a - t0;
+      type = (p.tma_mask & 1) ? PT_SEL : PT_THREADS;
+    } else {
+      const int k = tid - nslots;  // 0 sink, 1 ring before the wrap, 2 ring after it, 3 current
+      const int wrap = min(ringEnd, sinkEnd + (p.ring_cap - p.ring_start));
+      const int e0 = clampk(selEnd), e1 = clampk(sinkEnd), e2 = clampk(wrap), e3 = clampk(ringEnd);
+      row = e0 - t0;
+      if (k >= 1) row += (e1 - e0 + 7) & ~7;
+      if (k >= 2) row += (e2 - e1 + 7) & ~7;
+      if (k >= 3) row += (e3 - e2 + 7) & ~7;
+      a = k == 0 ? e0 : k == 1 ? e1 : k == 2 ? e2 : e3;
+      b = k == 0 ? e1 : k == 1 ? e2 : k == 2 ? e3 : t1;
+      type = k == 0 ? ((p.tma_mask & 2) ? PT_SINK : PT_THREADS)
+                    : k == 3 ? PT_THREADS : ((p.tma_mask & 4) ? PT_RING : PT_THREADS);
+    }
+    const int len = b - a;
+    if (len <= 0) {
+      type = PT_EMPTY;
+    } else if (row + ((len + 7) & ~7) > NR) {  // never taken: tps + 32 rows hold every table
+      if (p.err) atomicExch(p.err, ERR_BOUNDS);
+      type = PT_SKIP;
+      row = 0;
+    }
+    by_threads = type == PT_THREADS;
+    plo[tid] = a - t0;
+    plen[tid] = len > 0 ? len : 0;
+    prow[tid] = row;
+    ptype[tid] = type;
+    if (tid == np - 1) plo[np] = n;
+    if (type <= PT_RING) {
+      const uint32_t bytes = (uint32_t)((len + 7) & ~7) * 256u;  // K (or V): rows x 2 halves x 128 B
+      mbar_init(&kbar[tid], 1);
+      mbar_init(&vbar[tid], 1);
+      fence_mbar_init();
+      mbar_expect_tx(&kbar[tid], bytes);
+      mbar_expect_tx(&vbar[tid], bytes);
+    }
   }
-  // Q as the A operand: rows = query heads g < G (lane quad g), rows >= G zero.
+  // (after the barrier initialisation: its fence would wait for these loads)
+  if (tid >= 64 && tid < 76 && ((p.tma_mask >> ((tid - 64) >> 2)) & 1)) {
+    const int m = tid - 64;
+    prefetch_tmap(&tm.m[m >> 2][(m >> 1) & 1][m & 1]);
+  }
+  // block ids: read now unless they come from the grid this one overlaps
+  long long id_early = 0;
+  if (!p.overlap && tid < nslots) id_early = __ldg(p.ids + slot0 + tid);
+  if (warp < 2) {  // np <= AT_MAX_SLOTS + 4 pieces live in warps 0 and 1
+    const unsigned bits = __ballot_sync(FULL, by_threads);
+    if (lane == 0) s_thr[warp] = bits;
+  }
+  // Q as the A operand (rows >= G are zero), loaded while the table is built
   const int qg = lane >> 2, qt = lane & 3;
   uint32_t qa[8][2];
 #pragma unroll
@@ -848,62 +941,145 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(AttendParams p) 
       qa[kk][0] = qa[kk][1] = 0u;
     }
   }
+  __syncthreads();
+  NKV_STAMP(trc, 61);
+  const unsigned long long thr_pieces = ((unsigned long long)s_thr[1] << 32) | s_thr[0];
+  // token -> tile row, written by the warp that owns the piece (i % NW)
+  for (int i = warp; i < np; i += NW)
+    for (int r = lane; r < plen[i]; r += 32) srow[plo[i] + r] = (short)(ptype[i] == PT_SKIP ? 0 : prow[i] + r);
+  // sink and ring pieces: TMA boxes, piece i issued by warp i % NW
+  for (int i = warp; i < np; i += NW) {
+    const int type = ptype[i];
+    if (type != PT_SINK && type != PT_RING) continue;
+    const int pos0 = t0 + plo[i];
+    int y0;
+    if (type == PT_SINK) {
+      y0 = h * p.sink_cap + (pos0 - selEnd);
+    } else {
+      int phys = p.ring_start + (pos0 - sinkEnd);
+      if (phys >= p.ring_cap) phys -= p.ring_cap;
+      y0 = h * p.ring_cap + phys;
+    }
+    issue_piece(tm, type, y0, plen[i], prow[i], kt, vt, NR, &kbar[i], &vbar[i], lane);
+  }
+  // decode: append the current token to the recent ring (a slot no CTA reads)
+  if (split == 0 && p.ring_write_pos >= 0 && tid >= 64 && tid < 96 &&
+      NKV_INB(p.err, 40, ((long long)h * p.ring_cap + p.ring_write_pos) * NKV_D, NKV_D, p.ext_ring) &&
+      NKV_INB(p.err, 41, h * p.cur_head, NKV_D, p.ext_cur)) {
+    const int c = tid & 15;
+    const bool isv = (tid & 16) != 0;
+    const __nv_bfloat16* src = (isv ? p.cur_v : p.cur_k) + h * p.cur_head + c * 8;
+    __nv_bfloat16* dst = (isv ? p.ring_v : p.ring_k) + ((long long)h * p.ring_cap + p.ring_write_pos) * NKV_D + c * 8;
+    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+  }
+  // thread-loaded pieces outside the selected segment
+  for (unsigned long long m = thr_pieces; m; m &= m - 1) {
+    const int i = __ffsll((long long)m) - 1;
+    if (t0 + plo[i] >= selEnd)
+      thread_rows(p, h, t0 + plo[i], plen[i], prow[i], kt, vt, NR, s_ids, slot0, selEnd, sinkEnd, ringEnd);
+  }
+  NKV_STAMP(trc, 62);
   if (p.overlap) pdl_wait();  // block ids are complete past this point
   if (tid < nslots) {
-    bool bad;
-    const long long id = clamp_id(p, slot0 + tid, &bad);
+    const long long id = p.overlap ? __ldg(p.ids + slot0 + tid) : id_early;
+    const bool bad = id < 0 || id >= p.max_blocks;
+    if (bad && p.err) atomicExch(p.err, ERR_BAD_INDEX);
     s_ids[tid] = bad ? -1 : id;
   }
-  if (int8) load_int8_pitched(p, h, t0, t1, ks, vs, KPITCH);
-  __syncthreads();  // ids (and int8 tiles) visible
+  __syncthreads();
   NKV_STAMP(trc, 49);
-  if (!int8) {
-    slice_copy<G>(p, h, t0, lo, hi, lane, ks, vs, selEnd, sinkEnd, ringEnd, s_ids, slot0, true, true);
+  // selected blocks: TMA boxes (piece i issued by warp i % NW), or the threads
+  // (int8, host-resident)
+  for (int i = warp; i < np; i += NW) {
+    if (ptype[i] != PT_SEL) continue;
+    const int pos0 = t0 + plo[i];
+    long long id = s_ids[(pos0 >> p.log2B) - slot0];
+    if (id < 0) id = 0;  // masked in the scores
+    const int y0 = (int)((id * p.hkv + h) * B + (pos0 & (B - 1)));
+    issue_piece(tm, PT_SEL, y0, plen[i], prow[i], kt, vt, NR, &kbar[i], &vbar[i], lane);
   }
-  cp_async_commit();  // group: every K row of the slice
-  if (!int8) {
-    slice_copy<G>(p, h, t0, lo, hi, lane, ks, vs, selEnd, sinkEnd, ringEnd, s_ids, slot0, true, false);
+  NKV_STAMP(trc, 63);
+  for (unsigned long long m = thr_pieces; m; m &= m - 1) {
+    const int i = __ffsll((long long)m) - 1;
+    if (t0 + plo[i] < selEnd)
+      thread_rows(p, h, t0 + plo[i], plen[i], prow[i], kt, vt, NR, s_ids, slot0, selEnd, sinkEnd, ringEnd);
   }
-  cp_async_commit();  // group: selected V rows (the other V rows are in the first group)
-  cp_async_wait<1>();
-  __syncwarp();
+  __syncthreads();  // thread-loaded rows visible
+  NKV_STAMP(trc, 50);
+
+  // ---- this warp's slice [lo, hi), 8-aligned -----------------------------------------
+  const int tpw = ((n + NW - 1) / NW + 7) / 8 * 8;
+  const int lo = min(n, warp * tpw), hi = min(n, lo + tpw);
+  int pa = 0, pb = -1;
+  if (lo < hi) {
+    while (pa + 1 < np && plo[pa + 1] <= lo) ++pa;
+    pb = pa;
+    while (pb + 1 < np && plo[pb + 1] < hi) ++pb;
+  }
+  for (int i = pa; i <= pb; ++i)
+    if (ptype[i] <= PT_RING) mbar_wait_bounded(&kbar[i], 0, p.err);
   NKV_STAMP(trc, 51);
 #ifdef NKV_CHECKED
-  if (p.stop == 1) { cp_async_wait<0>(); return; }
+  if (p.stop == 1) {
+    for (int i = pa; i <= pb; ++i)
+      if (ptype[i] <= PT_RING) mbar_wait_bounded(&vbar[i], 0, p.err);
+    return;
+  }
 #endif
 
-  constexpr int MAXT = AT_TPS_MAX_CLUSTER / (8 * NW) + 1;  // n-tiles of 8 keys per warp slice
-  float sfr[MAXT][4];
+  // slices hold at most 48 keys (tps <= 384 over 8 warps, rounded to 8)
+  constexpr int MAXT = AT_TPS_MAX_CLUSTER / (8 * NW);  // n-tiles of 8 keys per warp slice
+  float sfr[MAXT][4], sfr2[MAXT][4];
   const int ntile = (hi - lo + 7) / 8;
   // ldmatrix row address pattern: lane i feeds row (i & 7) of matrix (i >> 3)
   const int mrow = lane & 7, msel = lane >> 3;
+  int rowj[MAXT];
 #pragma unroll
   for (int j = 0; j < MAXT; ++j) {
     sfr[j][0] = sfr[j][1] = sfr[j][2] = sfr[j][3] = 0.f;
-    if (j < ntile) {
-      int row = lo + j * 8 + mrow;
-      if (row >= hi) row = lo;  // only this slice's rows are loaded; masked below
-      const __nv_bfloat16* kr = ks + (long long)row * KPITCH;
-#pragma unroll
-      for (int kk = 0; kk < 8; kk += 2) {
-        // matrices: (kk, lo 8 dims), (kk, hi 8 dims), (kk+1, lo), (kk+1, hi)
-        uint32_t b[4];
-        ldsm_x4(b, kr + (kk + (msel >> 1)) * 16 + (msel & 1) * 8);
-        mma_bf16(sfr[j], qa[kk][0], 0u, qa[kk][1], 0u, b[0], b[1]);
-        mma_bf16(sfr[j], qa[kk + 1][0], 0u, qa[kk + 1][1], 0u, b[2], b[3]);
-      }
-    }
+    sfr2[j][0] = sfr2[j][1] = sfr2[j][2] = sfr2[j][3] = 0.f;
+    int t = lo + j * 8 + mrow;
+    if (t >= hi) t = lo;  // only this slice's rows are known to have landed; masked below
+    rowj[j] = j < ntile ? srow[t] : 0;
   }
-  // mask + scale; lane holds row qg keys lo + 8j + 2qt + {0, 1}
+  // k-steps outermost, the ldmatrix of every n-tile issued before the mma
+  // that use them, and two accumulators per n-tile (even / odd k-steps): the
+  // asm statements keep their order, so the order written here is the
+  // schedule; consecutive mma.sync are independent.
+#pragma unroll
+  for (int kk = 0; kk < 8; kk += 2) {
+    // matrices: (kk, lo 8 dims), (kk, hi 8 dims), (kk+1, lo), (kk+1, hi)
+    uint32_t b[MAXT][4];
+#pragma unroll
+    for (int j = 0; j < MAXT; ++j)
+      if (j < ntile) ldsm_x4(b[j], kt + swz(NR, rowj[j], (kk + (msel >> 1)) * 16 + (msel & 1) * 8));
+#pragma unroll
+    for (int j = 0; j < MAXT; ++j)
+      if (j < ntile) mma_bf16(sfr[j], qa[kk][0], 0u, qa[kk][1], 0u, b[j][0], b[j][1]);
+#pragma unroll
+    for (int j = 0; j < MAXT; ++j)
+      if (j < ntile) mma_bf16(sfr2[j], qa[kk + 1][0], 0u, qa[kk + 1][1], 0u, b[j][2], b[j][3]);
+  }
+#pragma unroll
+  for (int j = 0; j < MAXT; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sfr[j][e] += sfr2[j][e];
+  NKV_STAMP(trc, 58);
+  // mask + scale; lane holds row qg keys lo + 8j + 2qt + {0, 1}.  Bit i of
+  // vis = key lo + i of the slice is visible (two keys per lane, one ballot each).
+  const unsigned long long vis =
+      (unsigned long long)__ballot_sync(FULL, lo + lane < hi &&
+                                                  visible(p, t0 + lo + lane, 0, selEnd, ringEnd, s_ids, slot0)) |
+      ((unsigned long long)__ballot_sync(FULL, lo + 32 + lane < hi &&
+                                                   visible(p, t0 + lo + 32 + lane, 0, selEnd, ringEnd, s_ids, slot0))
+       << 32);
+  const unsigned long long visq = qg < G ? vis >> (2 * qt) : 0ull;
   float mloc = -INFINITY;
 #pragma unroll
   for (int j = 0; j < MAXT; ++j) {
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-      const int t = lo + j * 8 + 2 * qt + e;
-      float sv = -INFINITY;
-      if (j < ntile && t < hi && qg < G && visible(p, t0 + t, 0, selEnd, ringEnd, s_ids, slot0))
-        sv = sfr[j][e] * p.scale;
+      const float sv = ((visq >> (j * 8 + e)) & 1ull) ? sfr[j][e] * p.scale : -INFINITY;
       sfr[j][e] = sv;
       mloc = fmaxf(mloc, sv);
     }
@@ -922,8 +1098,8 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(AttendParams p) 
   lloc += __shfl_xor_sync(FULL, lloc, 1);
   lloc += __shfl_xor_sync(FULL, lloc, 2);
   NKV_STAMP(trc, 52);
-  cp_async_wait<0>();
-  __syncwarp();
+  for (int i = pa; i <= pb; ++i)
+    if (ptype[i] <= PT_RING) mbar_wait_bounded(&vbar[i], 0, p.err);
   NKV_STAMP(trc, 53);
 #ifdef NKV_CHECKED
   if (p.stop == 2) { if (lane == 0 && mloc == 1.2345f) p.out[0] = __float2bfloat16(lloc); return; }
@@ -939,18 +1115,26 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(AttendParams p) 
       const uint32_t pa0 = pack_bf16x2(sfr[2 * ksx][0], sfr[2 * ksx][1]);
       const uint32_t pa2 = 2 * ksx + 1 < MAXT ? pack_bf16x2(sfr[2 * ksx + 1][0], sfr[2 * ksx + 1][1]) : 0u;
       // ldmatrix.trans rows: keys lo + 16 ksx + (msel & 1) * 8 + mrow, dims + (msel >> 1) * 8
-      int row = lo + ksx * 16 + (msel & 1) * 8 + mrow;
-      if (row >= hi) row = lo;  // loaded, finite values times p = 0
-      const __nv_bfloat16* vr = vs + (long long)row * KPITCH + (msel >> 1) * 8;
+      int t = lo + ksx * 16 + (msel & 1) * 8 + mrow;
+      if (t >= hi) t = lo;  // landed, finite values times p = 0
+      const int row = srow[t];
+      // the eight ldmatrix of the k-step first, then its sixteen mma
+      uint32_t b[8][4];
+#pragma unroll
+      for (int dn = 0; dn < 16; dn += 2) ldsm_x4_t(b[dn / 2], vt + swz(NR, row, dn * 8 + (msel >> 1) * 8));
 #pragma unroll
       for (int dn = 0; dn < 16; dn += 2) {
-        uint32_t b[4];
-        ldsm_x4_t(b, vr + dn * 8);
-        mma_bf16(ofr[dn], pa0, 0u, pa2, 0u, b[0], b[1]);
-        mma_bf16(ofr[dn + 1], pa0, 0u, pa2, 0u, b[2], b[3]);
+        mma_bf16(ofr[dn], pa0, 0u, pa2, 0u, b[dn / 2][0], b[dn / 2][1]);
+        mma_bf16(ofr[dn + 1], pa0, 0u, pa2, 0u, b[dn / 2][2], b[dn / 2][3]);
       }
     }
   }
+  float* wpo = reinterpret_cast<float*>(kt);  // [NW][G][D] over the K tile
+  float* wml = wpo + NW * G * NKV_D;          // [NW][G][2]
+  float* pm = reinterpret_cast<float*>(vt);   // [G] CTA partial over the V tile
+  float* pl = pm + 64;
+  float* po = pl + 64;                        // [G][D]
+  __syncthreads();  // every warp is done with the K tile
   // warp partial: rows qg < G hold o[qg][8 dn + 2 qt + {0,1}]
   if (qg < G) {
 #pragma unroll
@@ -961,7 +1145,7 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(AttendParams p) 
       wml[(warp * G + qg) * 2 + 1] = lo < hi ? lloc : 0.f;
     }
   }
-  __syncthreads();
+  __syncthreads();  // warp partials complete; every warp is done with the V tile
   NKV_STAMP(trc, 54);
 #ifdef NKV_CHECKED
   if (p.stop == 3) return;
@@ -1005,12 +1189,7 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(AttendParams p) 
   if (p.stop == 4) return;
 #endif
   if (p.cluster) {
-    if (p.push) {
-      __syncthreads();  // CTA partial complete
-      push_merge<G>(p, h, pm, pl, po, recv);
-    } else {
-      combine_cluster<G>(p, h, pm, pl, po);  // begins with a cluster barrier
-    }
+    combine_cluster<G>(p, h, pm, pl, po);  // begins with a cluster barrier
     NKV_STAMP(trc, 57);
     return;
   }
@@ -1021,115 +1200,54 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(AttendParams p) 
   if (s_ticket != (unsigned)p.splits - 1) return;
   __threadfence();
   if (tid == 0) p.counters[h] = 0u;
-  combine_splits<G>(p, h, reinterpret_cast<float*>(ks));
-}
-
-// Push merge for the decode kernel: every CTA of the head's cluster stores its
-// partial (m, l, o) for G rows into slot `rank` of the receive buffer of the
-// cluster's rank-0 CTA (DSMEM stores), then arrives on the cluster barrier with
-// release semantics.  Only rank 0 waits (acquire); it merges the C partials
-// from its own shared memory and writes the bf16 output.  The other CTAs exit
-// after arriving; nothing reads their shared memory.
-template <int G>
-__device__ void push_merge(const AttendParams& p, int h, const float* pm, const float* pl, const float* po,
-                           float* recv /* [C][G][D + 2] in every CTA; rank 0's is used */) {
-  cg::cluster_group cluster = cg::this_cluster();
-  const int C = (int)cluster.num_blocks();
-  const int rank = (int)cluster.block_rank();
-  constexpr int RW = NKV_D + 2;
-  float* dst = cluster.map_shared_rank(recv, 0) + (long long)rank * G * RW;
-  for (int i = threadIdx.x; i < G * (NKV_D / 4); i += blockDim.x) {
-    const int g = i / (NKV_D / 4), d4 = i % (NKV_D / 4);
-    const float4 v = *reinterpret_cast<const float4*>(po + g * NKV_D + d4 * 4);
-    float* row = dst + g * RW;
-    row[d4 * 4 + 0] = v.x;
-    row[d4 * 4 + 1] = v.y;
-    row[d4 * 4 + 2] = v.z;
-    row[d4 * 4 + 3] = v.w;
-    if (d4 == 0) {
-      row[NKV_D] = pm[g];
-      row[NKV_D + 1] = pl[g];
-    }
-  }
-  // arrive (release: the stores above are visible to whoever acquires)
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-  if (rank != 0) return;
-  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-  for (int it = threadIdx.x; it < G * (NKV_D / 4); it += blockDim.x) {
-    const int g = it / (NKV_D / 4), d4 = it % (NKV_D / 4);
-    float M = -INFINITY;
-    for (int q = 0; q < C; ++q) M = fmaxf(M, recv[(q * G + g) * RW + NKV_D]);
-    float L = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int q = 0; q < C; ++q) {
-      const float* row = recv + (q * G + g) * RW;
-      const float m = row[NKV_D];
-      if (m == -INFINITY) continue;
-      const float w = __expf(m - M);
-      L += w * row[NKV_D + 1];
-      acc.x = fmaf(w, row[d4 * 4 + 0], acc.x);
-      acc.y = fmaf(w, row[d4 * 4 + 1], acc.y);
-      acc.z = fmaf(w, row[d4 * 4 + 2], acc.z);
-      acc.w = fmaf(w, row[d4 * 4 + 3], acc.w);
-    }
-    const float inv = 1.f / L;
-    const long long oo = (long long)(h * G + g) * p.out_head + d4 * 4;
-    if (NKV_INB(p.err, 43, oo, 4, p.ext_out)) {
-      uint2 w2;
-      w2.x = (uint32_t)f2bf(acc.x * inv) | ((uint32_t)f2bf(acc.y * inv) << 16);
-      w2.y = (uint32_t)f2bf(acc.z * inv) | ((uint32_t)f2bf(acc.w * inv) << 16);
-      *reinterpret_cast<uint2*>(p.out + oo) = w2;
-    }
-  }
+  combine_splits<G>(p, h, reinterpret_cast<float*>(kt));
 }
 
 // Cluster merge: the CTAs of one cluster are the splits of one KV head.  After
-// a cluster barrier, CTA r merges output groups r, r + C, ... reading every
-// split's (m, l, o) from the peers' shared memory, then a second barrier keeps
-// that memory alive until all peers are done.
+// a cluster barrier, the output is cut into tasks of 32 dims of one query row;
+// task t is done by warp (t / C) % warps of CTA t % C in one DSMEM round trip:
+// lane q < C reads split q's (m, l), every lane reads its dim of all C partial
+// outputs, then the weights exp(m_q - M) travel by shuffle.  A second barrier
+// keeps every CTA's shared memory alive until its peers are done reading.
 template <int G>
 __device__ void combine_cluster(const AttendParams& p, int h, float* pm, float* pl, float* po) {
   cg::cluster_group cluster = cg::this_cluster();
   const int C = (int)cluster.num_blocks();
   const int rank = (int)cluster.block_rank();
-  const int nr = p.nr;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (int)blockDim.x >> 5;
+  const int tasks = p.nr * (NKV_D / 32);
   cluster.sync();
-  const int items = nr * (NKV_D / 4);
-  for (int it = threadIdx.x * C + rank; it < items; it += C * (int)blockDim.x) {
-    const int row = it / (NKV_D / 4), d4 = it % (NKV_D / 4);
-    float m[AT_CLUSTER_MAX], M = -INFINITY;
-#pragma unroll
-    for (int q = 0; q < AT_CLUSTER_MAX; ++q) {
-      m[q] = -INFINITY;
-      if (q < C) {
-        m[q] = *cluster.map_shared_rank(pm + row, q);
-        M = fmaxf(M, m[q]);
-      }
+#ifdef NKV_CHECKED
+  int* trc = p.trace ? p.trace + (blockIdx.y * gridDim.x + blockIdx.x) * 64 : nullptr;
+  NKV_STAMP(trc, 59);
+#endif
+  for (int task = rank + C * warp; task < tasks; task += C * nw) {
+    const int row = task >> 2, d = (task & 3) * 32 + lane;
+    float mq = -INFINITY, lq = 0.f;
+    if (lane < C) {
+      mq = *cluster.map_shared_rank(pm + row, lane);
+      lq = *cluster.map_shared_rank(pl + row, lane);
     }
-    float L = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float v[AT_CLUSTER_MAX];
 #pragma unroll
-    for (int q = 0; q < AT_CLUSTER_MAX; ++q) {
-      if (q < C && m[q] != -INFINITY) {
-        const float w = __expf(m[q] - M);
-        L += w * *cluster.map_shared_rank(pl + row, q);
-        const float4 v = *reinterpret_cast<const float4*>(cluster.map_shared_rank(po + row * NKV_D + d4 * 4, q));
-        acc.x = fmaf(w, v.x, acc.x);
-        acc.y = fmaf(w, v.y, acc.y);
-        acc.z = fmaf(w, v.z, acc.z);
-        acc.w = fmaf(w, v.w, acc.w);
-      }
-    }
-    const float inv = 1.f / L;
+    for (int q = 0; q < AT_CLUSTER_MAX; ++q) v[q] = q < C ? *cluster.map_shared_rank(po + row * NKV_D + d, q) : 0.f;
+    float M = mq;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, o));
+    const float w = mq == -INFINITY ? 0.f : __expf(mq - M);
+    float L = w * lq;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(FULL, L, o);
+    float acc = 0.f;
+#pragma unroll
+    for (int q = 0; q < AT_CLUSTER_MAX; ++q) acc = fmaf(__shfl_sync(FULL, w, q), v[q], acc);
     const int qn = row / G, g = row % G;
-    const long long oo = qn * p.out_row + (long long)(h * G + g) * p.out_head + d4 * 4;
-    if (NKV_INB(p.err, 43, oo, 4, p.ext_out)) {
-      uint2 w;
-      w.x = (uint32_t)f2bf(acc.x * inv) | ((uint32_t)f2bf(acc.y * inv) << 16);
-      w.y = (uint32_t)f2bf(acc.z * inv) | ((uint32_t)f2bf(acc.w * inv) << 16);
-      *reinterpret_cast<uint2*>(p.out + oo) = w;
-    }
+    const long long oo = qn * p.out_row + (long long)(h * G + g) * p.out_head + d;
+    if (NKV_INB(p.err, 43, oo, 1, p.ext_out)) p.out[oo] = __float2bfloat16(acc * (1.f / L));
   }
+#ifdef NKV_CHECKED
+  NKV_STAMP(trc, 60);
+#endif
   cluster.sync();
 }
 
@@ -1227,6 +1345,73 @@ static int splits_for(int ntok, int hkv, int sms) {
   if (s < s_mem) s = s_mem;
   if (s < 1) s = 1;
   return s;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// dependency on libcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    cudaGetLastError();
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  return fn;
+}
+
+// Tensor map over `rows` rows of 128 bf16 at `base` (boxes of `box_rows` x 64
+// columns, 128-byte swizzle, zero fill outside), or false when TMA must not
+// read it: memory that is not device memory (mapped host memory, managed
+// memory), a base that is not 16-byte aligned, or more rows than a coordinate
+// holds.  Maps are cached per thread in a small hash table keyed by
+// (base, rows, box_rows); encoding touches no device state.
+static bool tma_rows_map(CUtensorMap* out, const void* base, long long rows, int box_rows) {
+  struct Entry { const void* base; long long rows; int box; bool ok; CUtensorMap map; };
+  constexpr int N = 512;
+  static thread_local Entry* cache = nullptr;
+  if (!base || rows < 1 || rows >= (1ll << 31) || ((uintptr_t)base & 15)) return false;
+  if (!cache) cache = static_cast<Entry*>(calloc(N, sizeof(Entry)));
+  if (!cache) return false;
+  uint64_t key = (uint64_t)(uintptr_t)base ^ ((uint64_t)rows * 0x9e3779b97f4a7c15ull) ^ (uint64_t)box_rows;
+  key ^= key >> 29;
+  Entry& e = cache[(key * 0xbf58476d1ce4e5b9ull) >> 55];  // 9 bits: N = 512
+  if (e.base == base && e.rows == rows && e.box == box_rows) {
+    if (e.ok) *out = e.map;
+    return e.ok;
+  }
+  e.base = base;
+  e.rows = rows;
+  e.box = box_rows;
+  e.ok = false;
+  cudaPointerAttributes pa;
+  const bool dev = cudaPointerGetAttributes(&pa, base) == cudaSuccess && pa.type == cudaMemoryTypeDevice;
+  cudaGetLastError();
+  EncodeTiledFn fn = encode_tiled();
+  if (dev && fn && box_rows <= rows) {
+    const cuuint64_t dims[2] = {(cuuint64_t)NKV_D, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)NKV_D * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    e.ok = fn(&e.map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  }
+  if (e.ok) *out = e.map;
+  return e.ok;
+}
+
+// The four maps of one source (K and V, 8- and 64-row boxes); a source of
+// fewer than 64 rows never has a piece of 64 rows and gets no 64-row maps.
+static bool source_maps(DecodeMaps* m, int src, const void* k, const void* v, long long rows) {
+  if (!tma_rows_map(&m->m[src][0][0], k, rows, 8) || !tma_rows_map(&m->m[src][1][0], v, rows, 8)) return false;
+  if (rows < 64) return true;
+  return tma_rows_map(&m->m[src][0][1], k, rows, 64) && tma_rows_map(&m->m[src][1][1], v, rows, 64);
 }
 
 static size_t attend_ws(int hkv, int nr, int max_tokens) {
@@ -1360,19 +1545,16 @@ extern "C" int nkv_attend(nkv_stream_t stream, const nkv_attend_args* a) {
     }
   }
   p.cluster = C > 0 ? 1 : 0;
-  // NKV_ATTEND_MERGE: 0 = workspace merge, 1 = cluster pull, 2 = cluster push
-  const int merge_env = env_int("NKV_ATTEND_MERGE", 1);
-  if (merge_env == 0) p.cluster = 0;
-  p.push = merge_env == 2 ? 1 : 0;
+  // NKV_ATTEND_MERGE: 0 = workspace merge, 1 = cluster merge where it fits
+  if (env_int("NKV_ATTEND_MERGE", 1) == 0) p.cluster = 0;
   p.stop = env_int("NKV_DEBUG_STOP", 0);
   AttendParams pg = p;  // workspace-merge configuration (fallback)
   pg.cluster = 0;
-  pg.push = 0;
   {
     AttendParams& q = pg;
     q.splits = splits_for(q.ntok, a->hkv, sms);
     q.tps = (q.ntok + q.splits - 1) / q.splits;
-    q.tps = (q.tps + 3) / 4 * 4;
+    q.tps = (q.tps + 7) / 8 * 8;
     q.splits = (q.ntok + q.tps - 1) / q.tps;
     while (2 * nr * q.splits > q.tps * 64) {
       q.tps *= 2;
@@ -1382,7 +1564,7 @@ extern "C" int nkv_attend(nkv_stream_t stream, const nkv_attend_args* a) {
   if (!p.cluster) {
     p.splits = splits_for(p.ntok, a->hkv, sms);
     p.tps = (p.ntok + p.splits - 1) / p.splits;
-    p.tps = (p.tps + 3) / 4 * 4;
+    p.tps = (p.tps + 7) / 8 * 8;
     p.splits = (p.ntok + p.tps - 1) / p.tps;
     // the merge keeps 2 * nr * splits floats in the K tile region (tps * 64 floats)
     while (2 * nr * p.splits > p.tps * 64) {
@@ -1422,23 +1604,27 @@ extern "C" int nkv_attend(nkv_stream_t stream, const nkv_attend_args* a) {
   finish(p);
   finish(pg);
   const int dk_warps = 8;  // DK<G>::WARPS
-  auto smem_need = [&](const AttendParams& q) -> size_t {
-    if (a->nq == 1) {  // decode_kernel layout
-      return (size_t)q.tps * KPITCH * 2 * 2 + (size_t)dk_warps * G * NKV_D * 4 +
-             (size_t)dk_warps * G * 2 * 4 + (size_t)(128 + G * NKV_D) * 4 +
-             (q.cluster && q.push ? (size_t)q.splits * G * (NKV_D + 2) * 4 : 0);
+  // decode_kernel: 1 KiB alignment slack + K region (tile, then warp partials)
+  // + V region (tile, then the CTA partial)
+  auto decode_regions = [&](AttendParams& q) {
+    q.tile_rows = q.tps + DT_PAD_ROWS;
+    size_t rk = (size_t)q.tile_rows * 256, wp = (size_t)dk_warps * G * (NKV_D + 2) * 4;
+    if (rk < wp) rk = wp;
+    q.region_k = (int)((rk + 1023) / 1024 * 1024);
+  };
+  decode_regions(p);
+  decode_regions(pg);
+  auto smem_of = [&](const AttendParams& q) -> size_t {
+    if (a->nq == 1) {
+      size_t rv = (size_t)q.tile_rows * 256, cp = (size_t)(128 + G * NKV_D) * 4;
+      return 1024 + (size_t)q.region_k + (rv > cp ? rv : cp);
     }
     return (size_t)q.tps * NKV_D * 2 * 2 + (size_t)q.tps * q.nr_pad * 4 + AT_WARPS * 4 * NKV_D * 4 +
            (size_t)nr * NKV_D * 4 + (q.cluster ? (size_t)(128 + nr * NKV_D) * 4 : 0);
-  };  auto smem_of = [&](const AttendParams& q) -> size_t {
-    size_t need = smem_need(q);
-    // a cluster waits for its slowest CTA: claim more than half of an SM's
-    // shared memory so that the scheduler never stacks two CTAs on one SM
-    (void)AT_SMEM_ONE_PER_SM;  // 16-CTA clusters cannot be placed one CTA per SM
-    return need;
   };
 
-  NKV_SUPPORTED(smem_of(pg) <= 220 * 1024 && pg.tps / a->block_size + 2 <= AT_MAX_SLOTS,
+  NKV_SUPPORTED(smem_of(pg) <= 220 * 1024 && pg.tps / a->block_size + 2 <= AT_MAX_SLOTS &&
+                    (a->nq != 1 || pg.tps <= AT_TPS_MAX_CLUSTER),
                 "attend: %d keys per CTA exceed the tile limit", pg.tps);
   if (p.cluster && smem_of(p) > 220 * 1024) p = pg;
   cudaStream_t st = (cudaStream_t)stream;
@@ -1460,27 +1646,45 @@ extern "C" int nkv_attend(nkv_stream_t stream, const nkv_attend_args* a) {
     lc.attrs = attr;
     lc.numAttrs = 2;
   };
+  DecodeMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  if (q1) {
+    int mask = 0;
+    if (a->n_sel > 0 && a->store_kind == NKV_STORE_BF16 &&
+        source_maps(&maps, 0, a->k_store, a->v_store, (long long)a->max_blocks * a->hkv * a->block_size))
+      mask |= 1;
+    if (a->sink_len > 0 && source_maps(&maps, 1, a->sink_k, a->sink_v, (long long)a->hkv * a->sink_cap))
+      mask |= 2;
+    if (a->ring_len > 0 && source_maps(&maps, 2, a->ring_k, a->ring_v, (long long)a->hkv * a->ring_cap))
+      mask |= 4;
+    p.tma_mask = pg.tma_mask = env_int("NKV_ATTEND_TMA", 1) ? mask : 0;
+    NKV_REQUIRE(((uintptr_t)a->k_store & 15) == 0 && ((uintptr_t)a->v_store & 15) == 0 &&
+                    ((uintptr_t)a->sink_k & 15) == 0 && ((uintptr_t)a->sink_v & 15) == 0 &&
+                    ((uintptr_t)a->ring_k & 15) == 0 && ((uintptr_t)a->ring_v & 15) == 0,
+                "attend: store, sink and ring must be 16-byte aligned");
+  }
   switch (G * 2 + (q1 ? 1 : 0)) {
-#define NKV_AT_CASE(GG, QQ)                                                               \
-  case GG * 2 + (QQ ? 1 : 0): {                                                           \
-    auto kern = QQ ? decode_kernel<GG> : attend_kernel<GG, false>;                        \
-    if (ensure_smem(kern, smem_of(p) > smem_of(pg) ? smem_of(p) : smem_of(pg), "attend")) \
-      return NKV_ERR_CUDA;                                                                \
-    if (p.cluster) {                                                                      \
-      int ok = p.splits <= 8 || !ensure_nonportable_cluster(kern, "attend");              \
-      int nclusters = 0;                                                                  \
-      config(p);                                                                          \
-      if (ok && cudaOccupancyMaxActiveClusters(&nclusters, kern, &lc) != cudaSuccess)     \
-        ok = 0;                                                                           \
-      cudaGetLastError();                                                                 \
-      if (!ok || nclusters < 1) p = pg;                                                   \
-    }                                                                                     \
-    config(p);                                                                            \
-    g_last_cluster = p.cluster;                                                           \
-    g_last_splits = p.splits;                                                             \
-    g_last_tps = p.tps;                                                                   \
-    if (cudaLaunchKernelEx(&lc, kern, p) != cudaSuccess) return check_launch("attend");   \
-    break;                                                                                \
+#define NKV_AT_CASE(GG, QQ)                                                                     \
+  case GG * 2 + (QQ ? 1 : 0): {                                                                 \
+    auto kern = QQ ? (const void*)decode_kernel<GG> : (const void*)attend_kernel<GG, false>;    \
+    if (ensure_smem(kern, smem_of(p) > smem_of(pg) ? smem_of(p) : smem_of(pg), "attend"))       \
+      return NKV_ERR_CUDA;                                                                      \
+    if (p.cluster) {                                                                            \
+      int ok = p.splits <= 8 || !ensure_nonportable_cluster(kern, "attend");                    \
+      int nclusters = 0;                                                                        \
+      config(p);                                                                                \
+      if (ok && cudaOccupancyMaxActiveClusters(&nclusters, kern, &lc) != cudaSuccess) ok = 0;   \
+      cudaGetLastError();                                                                       \
+      if (!ok || nclusters < 1) p = pg;                                                         \
+    }                                                                                           \
+    config(p);                                                                                  \
+    g_last_cluster = p.cluster;                                                                 \
+    g_last_splits = p.splits;                                                                   \
+    g_last_tps = p.tps;                                                                         \
+    cudaError_t le = QQ ? cudaLaunchKernelEx(&lc, decode_kernel<GG>, p, maps)                   \
+                        : cudaLaunchKernelEx(&lc, attend_kernel<GG, false>, p);                 \
+    if (le != cudaSuccess) return check_launch("attend");                                       \
+    break;                                                                                      \
   }
     NKV_AT_CASE(1, true)
     NKV_AT_CASE(1, false)
