@@ -152,6 +152,25 @@ int nkv_attend(nkv_stream_t stream, const nkv_attend_args* args);
  * splits per head and the keys per CTA.  Host only (no GPU work). */
 int nkv_attend_last_config(int* cluster, int* splits, int* keys_per_cta);
 
+/* nkv_attend without a caller workspace.  No counterpart in the reference (its
+ * attention has no workspace argument).  It serves callers that cannot
+ * allocate device memory when they call: hosts whose device memory belongs to
+ * another framework's pool, serving loops that forbid allocation after
+ * warm-up, and code that must not synchronise the device (cudaMalloc and
+ * cudaFree may).
+ *
+ * The workspace is a scratch array of NKV_ATTEND_STATIC_SCRATCH_BYTES inside
+ * the library, one per device; args->workspace and workspace_bytes are
+ * ignored, and a call whose nkv_attend_workspace_bytes exceeds the scratch
+ * fails with NKV_ERR_ARG.  The first call on a device looks the scratch up
+ * (cudaGetSymbolAddress, which may load the module there): make it before any
+ * stream capture.  Each call clears the scratch's error word and merge
+ * counters with cudaMemsetAsync on `stream` and ignores overlap_select.
+ * Calls on one device share the scratch, so calls that can overlap in time
+ * (several streams or host threads) race; serialise them. */
+#define NKV_ATTEND_STATIC_SCRATCH_BYTES (8u << 20)
+int nkv_attend_static(nkv_stream_t stream, const nkv_attend_args* args);
+
 /* ------------------------------------------------------------------------ */
 /* (4) Segmented prefill attention on tcgen05/TMEM: the same four segments as
  * nkv_attend for a whole chunk of nq queries (nq == n_cur, causal in-chunk,

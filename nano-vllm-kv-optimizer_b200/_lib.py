@@ -81,6 +81,7 @@ SIGNATURES = {
     "nkv_attend_workspace_bytes": (C.c_size_t, [c_int, c_int, c_int, c_int]),
     "nkv_attend": (c_int, [c_vp, C.POINTER(AttendArgs)]),
     "nkv_attend_last_config": (c_int, [C.POINTER(c_int), C.POINTER(c_int), C.POINTER(c_int)]),
+    "nkv_attend_static": (c_int, [c_vp, C.POINTER(AttendArgs)]),
     "nkv_prefill_workspace_bytes": (C.c_size_t, [c_int, c_int, c_int, c_int]),
     "nkv_prefill": (c_int, [c_vp, C.POINTER(AttendArgs)]),
     "nkv_store_chunk": (c_int, [c_vp, C.POINTER(StoreArgs)]),

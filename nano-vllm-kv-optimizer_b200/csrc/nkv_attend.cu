@@ -26,6 +26,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "nkv_common.cuh"
 #include "nkv_host.h"
 
@@ -1706,4 +1708,76 @@ extern "C" int nkv_attend_last_config(int* cluster, int* splits, int* keys_per_c
   if (splits) *splits = g_last_splits;
   if (keys_per_cta) *keys_per_cta = g_last_tps;
   return NKV_OK;
+}
+
+// ---------------------------------------------------------------------------
+// nkv_attend_static: nkv_attend on a scratch buffer that lives inside this
+// library, for callers that cannot allocate device memory at call time (a
+// host framework owning the device memory pool, serving loops that forbid
+// allocation after warm-up, code that must not synchronise the device, which
+// cudaMalloc and cudaFree may do).
+//
+// The scratch is one file-scope device array (NKV_ATTEND_STATIC_SCRATCH_BYTES),
+// created when the CUDA module is loaded on a device.  The first call with a
+// device current looks its address up once with cudaGetSymbolAddress (which
+// may load the module on that device); make that first call before capturing
+// a stream.  Every call clears the error word and the per-head merge counters
+// (the part of the workspace the kernels expect to start at zero) with
+// cudaMemsetAsync on the caller's stream, then launches the unchanged
+// nkv_attend path with the scratch as its workspace.  Because that memset sits
+// between a preceding selection and the attention, overlap_select is ignored.
+// All calls on one device share the scratch: calls that may run at the same
+// time (other streams, other host threads) race on it.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_attend_scratch[NKV_ATTEND_STATIC_SCRATCH_BYTES];
+static std::mutex g_attend_scratch_mu;
+static void* g_attend_scratch_ptr[64];  // per device ordinal
+
+extern "C" int nkv_attend_static(nkv_stream_t stream, const nkv_attend_args* a) {
+  NKV_REQUIRE(a, "attend_static: null args");
+  NKV_REQUIRE(a->hkv >= 1 && a->hq >= 1 && a->nq >= 1 && a->block_size >= 1 && a->n_sel >= 0 &&
+                  a->sink_len >= 0 && a->ring_len >= 0 && a->n_cur >= 0,
+              "attend_static: bad geometry");
+  const long long ntok = (long long)a->n_sel * a->block_size + a->sink_len + a->ring_len + a->n_cur;
+  NKV_REQUIRE(ntok >= 1 && ntok < (1ll << 30), "attend_static: key count %lld out of range", ntok);
+  const size_t need = nkv_attend_workspace_bytes(a->hkv, a->hq, a->nq, (int)ntok);
+  NKV_REQUIRE(need <= (size_t)NKV_ATTEND_STATIC_SCRATCH_BYTES,
+              "attend_static: this call needs %zu bytes of workspace but the static scratch holds %zu "
+              "(fewer keys, heads or queries per call, or nkv_attend with a caller workspace)",
+              need, (size_t)NKV_ATTEND_STATIC_SCRATCH_BYTES);
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    set_error("attend_static: no usable current device (%s)", cudaGetErrorString(e));
+    return NKV_ERR_CUDA;
+  }
+  void* ws = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_attend_scratch_mu);
+    ws = g_attend_scratch_ptr[dev];
+    if (!ws) {
+      e = cudaGetSymbolAddress(&ws, g_attend_scratch);
+      if (e != cudaSuccess || !ws) {
+        cudaGetLastError();
+        set_error("attend_static: cudaGetSymbolAddress of the scratch failed on device %d: %s", dev,
+                  cudaGetErrorString(e));
+        return NKV_ERR_CUDA;
+      }
+      g_attend_scratch_ptr[dev] = ws;
+    }
+  }
+  // error word (256 B) + per-head counters, as laid out by the attend workspace
+  const size_t zero_bytes = 256 + ((size_t)(a->hkv * 4 + 255) / 256) * 256;
+  e = cudaMemsetAsync(ws, 0, zero_bytes, (cudaStream_t)stream);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("attend_static: clearing the scratch header failed: %s", cudaGetErrorString(e));
+    return NKV_ERR_CUDA;
+  }
+  nkv_attend_args b = *a;
+  b.workspace = ws;
+  b.workspace_bytes = NKV_ATTEND_STATIC_SCRATCH_BYTES;
+  b.overlap_select = 0;
+  return nkv_attend(stream, &b);
 }

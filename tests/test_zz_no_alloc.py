@@ -1,0 +1,115 @@
+"""nkv_attend_static (workspace = scratch inside the library) against nkv_attend
+(workspace from the caller), on the GPU.
+
+Both run the same kernels on the same arguments; the outputs must agree within
+the GPU parity tolerance (max-abs 2e-2 / rel 1e-2) on two calls in a row, for
+the single-query decode kernel with either split merge and for the multi-query
+kernel.  A call whose workspace would not fit the scratch is refused.
+"""
+import ctypes as C
+import os
+
+import pytest
+import torch
+
+from helpers import pkg
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-2, 1e-2
+DEV = "cuda"
+
+
+def _layer(nkv, seed):
+    """A layer runtime with 8192 stored tokens (bf16 block store in HBM)."""
+    rt = nkv.M12LayerRuntime(0, nkv.M12Config(max_model_len=16384, device=DEV))
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    for c in range(4):
+        k = torch.randn(2048, 8, 128, generator=g, device=DEV).bfloat16()
+        v = torch.randn(2048, 8, 128, generator=g, device=DEV).bfloat16()
+        if c == 0:
+            rt.prefill_first(None, k, v)
+        else:
+            rt._store_kv(k, v)
+    torch.cuda.synchronize()
+    return rt
+
+
+def _attend_args(nkv, rt, nq, seed):
+    """Run rt._attend once through nkv_attend; return its output, a copy of its
+    args and the input tensors those args point into (keep them alive)."""
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    q = torch.randn(nq, 32, 128, generator=g, device=DEV).bfloat16()
+    kc = torch.randn(nq, 8, 128, generator=g, device=DEV).bfloat16()
+    vc = torch.randn(nq, 8, 128, generator=g, device=DEV).bfloat16()
+    n_sel = 32
+    ids = torch.randperm(rt.nblocks_filled, generator=torch.Generator().manual_seed(seed))[:n_sel]
+    ids = ids.to(DEV)
+    captured = []
+    orig = nkv.m12_runtime.call
+
+    def spy(name, stream, argp):
+        if name == "nkv_attend":
+            captured.append(nkv._lib.AttendArgs.from_buffer_copy(argp._obj))
+        return orig(name, stream, argp)
+
+    nkv.m12_runtime.call = spy
+    try:
+        out = rt._attend(q, ids, n_sel, 64, 0, 300, kc, vc)  # no ring write: calls are repeatable
+    finally:
+        nkv.m12_runtime.call = orig
+    torch.cuda.synchronize()
+    assert len(captured) == 1
+    return out, captured[0], (q, kc, vc, ids)
+
+
+def _static(nkv, args, like):
+    lib = nkv._lib.load()
+    out = torch.full_like(like, float("nan"))
+    b = nkv._lib.AttendArgs.from_buffer_copy(args)
+    b.out = out.data_ptr()
+    b.workspace, b.workspace_bytes = None, 0
+    rc = lib.nkv_attend_static(torch.cuda.current_stream().cuda_stream, C.byref(b))
+    assert rc == 0, lib.nkv_last_error().decode()
+    return out
+
+
+@pytest.mark.parametrize("nq,merge", [(1, "1"), (1, "0"), (3, "1")])
+def test_static_scratch_matches_caller_workspace(nq, merge):
+    nkv = pkg()
+    old = os.environ.get("NKV_ATTEND_MERGE")
+    os.environ["NKV_ATTEND_MERGE"] = merge
+    try:
+        rt = _layer(nkv, 5)
+        ref, args, _keep = _attend_args(nkv, rt, nq, 11)
+        for _ in range(2):  # two calls in a row: the scratch is reused
+            got = _static(nkv, args, ref)
+            torch.cuda.synchronize()
+            torch.testing.assert_close(got.float().cpu(), ref.float().cpu(), atol=ATOL, rtol=RTOL)
+        # the caller-workspace path is unaffected by the static calls
+        lib = nkv._lib.load()
+        out = torch.full_like(ref, float("nan"))
+        b = nkv._lib.AttendArgs.from_buffer_copy(args)
+        b.out = out.data_ptr()
+        assert lib.nkv_attend(torch.cuda.current_stream().cuda_stream, C.byref(b)) == 0
+        torch.cuda.synchronize()
+        torch.testing.assert_close(out.float().cpu(), ref.float().cpu(), atol=ATOL, rtol=RTOL)
+    finally:
+        if old is None:
+            os.environ.pop("NKV_ATTEND_MERGE", None)
+        else:
+            os.environ["NKV_ATTEND_MERGE"] = old
+
+
+def test_static_scratch_rejects_oversize():
+    nkv = pkg()
+    rt = _layer(nkv, 6)
+    _, args, _keep = _attend_args(nkv, rt, 1, 12)
+    lib = nkv._lib.load()
+    b = nkv._lib.AttendArgs.from_buffer_copy(args)
+    b.n_sel = 1 << 16  # 4M keys: a workspace far beyond the scratch
+    need = lib.nkv_attend_workspace_bytes(8, 32, 1, b.n_sel * 64 + 64 + 300 + 1)
+    assert need > (8 << 20)
+    rc = lib.nkv_attend_static(torch.cuda.current_stream().cuda_stream, C.byref(b))
+    assert rc == nkv._lib.NKV_ERR_ARG
+    assert "static scratch" in lib.nkv_last_error().decode()
