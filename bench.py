@@ -44,6 +44,13 @@ ATTEND_TOKENS = TOPK * B + SINK + RECENT                 # 2624 keys per kv head
 ATTEND_BYTES = ATTEND_TOKENS * HKV * D * 2 * 2 + (HQ * D * 2) * 2 + HKV * D * 2 * 2
 SELECT_BYTES = (CTX // B) * HKV * R_REPS * D * 2 + HQ * D * 2
 STEP_BYTES = ATTEND_BYTES + SELECT_BYTES
+# DRAM bytes of one attend launch measured by ncu (profiles/decode_kernel_l4.md)
+ATTEND_TRAFFIC = 10826240
+# segmented prefill operator: a 4096-token chunk after a
+# 28672-token history; visible (query, key) pairs per head x 32 heads x 4 D
+PF_CHUNK, PF_HIST = 4096, 28672
+PF_PAIRS = PF_CHUNK * (TOPK * B + SINK + RECENT) + PF_CHUNK * (PF_CHUNK + 1) // 2
+PF_FLOP = PF_PAIRS * HQ * 4 * D
 
 
 def peaks():
@@ -52,6 +59,52 @@ def peaks():
         d = json.load(open(p))
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p))["bf16_tflops"]), "measured (burst)"
+    return 1590.0, "fallback"
+
+
+def prefill_measure(nkv, dev, iters=5):
+    """Kernel (4) at BASELINE config 4: one 4096-token chunk at positions
+    28672-32767 over its Top-32 blocks, sink, recent window and causal chunk."""
+    g = torch.Generator(device=dev).manual_seed(4242)
+    rt = nkv.M12LayerRuntime(0, nkv.M12Config(max_model_len=PF_HIST + PF_CHUNK + 4096, device=dev))
+    for c in range(PF_HIST // PF_CHUNK):
+        k = torch.randn(PF_CHUNK, HKV, D, generator=g, device=dev).bfloat16()
+        v = torch.randn(PF_CHUNK, HKV, D, generator=g, device=dev).bfloat16()
+        if c == 0:
+            rt.prefill_first(None, k, v)
+        else:
+            rt._store_kv(k, v)
+    q = torch.randn(PF_CHUNK, HQ, D, generator=g, device=dev).bfloat16()
+    k = torch.randn(PF_CHUNK, HKV, D, generator=g, device=dev).bfloat16()
+    v = torch.randn(PF_CHUNK, HKV, D, generator=g, device=dev).bfloat16()
+    ids = rt._select_dev(nkv.m12_runtime.prefill_query_summaries(q, 1), TOPK)
+    sink_len, ring_start, ring_len = rt._history_segments()
+
+    def run():
+        return rt._attend(q, ids, TOPK, sink_len, ring_start, ring_len, k, v, prefill=True)
+    for _ in range(2):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        run()
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / iters
+    peak, kind = tensor_peak()
+    tf = PF_FLOP / (us * 1e-6) / 1e12
+    del rt
+    return {"workload": "4096-token chunk at 28672 (Top-32, sink 64, recent 512, causal chunk), 32q/8kv d128",
+            "us_per_chunk": round(us, 2), "flop_per_chunk": PF_FLOP,
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(tf / peak, 4), "peak_kind": kind}}
 
 
 class Clocks:
@@ -146,6 +199,7 @@ def main():
     ap.add_argument("--impl", default="nkv", choices=["nkv", "reference"])
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--cpu-steps", type=int, default=20)
+    ap.add_argument("--no-prefill", action="store_true", help="skip the kernel (4) measurement")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -283,6 +337,10 @@ def main():
     e2e_value = e2e_ms * 1000.0 / (L * world)
 
     line = None
+    prefill = None
+    if rank == 0 and not args.no_prefill:
+        with torch.cuda.stream(stream):
+            prefill = prefill_measure(nkv, dev)
     if rank == 0:
         cpu_us, n_cpu = cpu_reference(args.cpu_steps, 3, threads)
         line = {
@@ -295,7 +353,9 @@ def main():
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "us_per_launch": round(att_us, 3), "bytes_per_launch": ATTEND_BYTES,
-                         "traffic": None},
+                         "traffic": ATTEND_TRAFFIC,
+                         "traffic_source": "ncu dram__bytes_read+write of one launch, "
+                                           "profiles/decode_kernel_l4.md"},
             "cpu_baseline": {"value": round(cpu_us, 1), "unit": UNIT, "cores": threads,
                              "kind": "port",
                              "sample": f"{n_cpu} decode calls of one 32K layer state (median)"},
@@ -306,6 +366,7 @@ def main():
             "attend_launch": {"cluster": attend_cfg[0], "splits_per_head": attend_cfg[1],
                               "keys_per_cta": attend_cfg[2]},
             "clocks": clocks,
+            "prefill": prefill,
         }
         print(json.dumps(line))
     del graph, g_att

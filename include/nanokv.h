@@ -172,13 +172,16 @@ int nkv_attend_last_config(int* cluster, int* splits, int* keys_per_cta);
 int nkv_attend_static(nkv_stream_t stream, const nkv_attend_args* args);
 
 /* ------------------------------------------------------------------------ */
-/* (4) Segmented prefill attention on tcgen05/TMEM: the same four segments as
- * nkv_attend for a whole chunk of nq queries (nq == n_cur, causal in-chunk,
- * bottom-right aligned), without packing.
+/* (4) Segmented prefill attention on the tensor cores: the same four segments
+ * as nkv_attend for a whole chunk of nq queries (nq == n_cur, causal in-chunk,
+ * bottom-right aligned), without packing.  With n_sel = sink_len = ring_len = 0
+ * it is the dense causal attention of the first chunk.
  * Replaces prefill_chunk's pack + _prefill_attention (m12_runtime.py:589-642,
- * 809-839; FA2 flash_attn_func call :834-839) and the segmented adapter's
+ * 809-839; FA2 flash_attn_func call :834-839), the first-chunk FA2 call
+ * (nanovllm/layers/attention.py:80-85) and the segmented adapter's
  * prepare/attend contract (nanovllm/sparse/segmented_prefill_adapter.py:95-147).
- * Requires store_kind == NKV_STORE_BF16 and allowed == NULL. */
+ * Any store_kind (int8 selected blocks are dequantised on load); requires
+ * allowed == NULL.  The workspace holds only the error word. */
 size_t nkv_prefill_workspace_bytes(int hkv, int hq, int nq, int max_tokens);
 int nkv_prefill(nkv_stream_t stream, const nkv_attend_args* args);
 

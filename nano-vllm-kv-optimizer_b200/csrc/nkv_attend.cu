@@ -661,30 +661,6 @@ __global__ void __launch_bounds__(AT_THREADS) attend_kernel(AttendParams p) {
   NKV_STAMP(trc, 57);
 }
 
-// ---------------------------------------------------------------------------
-// Tensor-core helpers (mma.sync m16n8k16, bf16 inputs, fp32 accumulate).
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  return (uint32_t)f2bf(lo) | ((uint32_t)f2bf(hi) << 16);
-}
 
 // ---------------------------------------------------------------------------
 // Decode tiles.  The K and V keys of a CTA sit in shared memory as
@@ -697,9 +673,6 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 constexpr int DT_PAD_ROWS = 32;  // tile rows beyond tps: padding of <= 4 pieces of ragged length
 enum : int { PT_SEL = 0, PT_SINK = 1, PT_RING = 2, PT_THREADS = 3, PT_SKIP = 4, PT_EMPTY = 5 };
 
-__device__ __forceinline__ uint32_t swz(int nrows, int row, int col) {
-  return (uint32_t)((((col >> 6) * nrows + row) << 7) + ((((col & 63) >> 3) ^ (row & 7)) << 4) + ((col & 7) << 1));
-}
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -208,4 +208,37 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   return r;
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core helpers (mma.sync m16n8k16, bf16 inputs, fp32 accumulate).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  return (uint32_t)f2bf(lo) | ((uint32_t)f2bf(hi) << 16);
+}
+
+// Swizzled tile addressing: a tile of nrows rows of 128 bf16 is stored as two
+// 64-column halves [2][nrows][128 B]; 16-byte chunk c of row r sits at chunk
+// c ^ (r & 7) (the 128-byte swizzle TMA writes, with 1024-byte aligned tiles).
+// Returns the byte offset of element (row, col).
+__device__ __forceinline__ uint32_t swz(int nrows, int row, int col) {
+  return (uint32_t)((((col >> 6) * nrows + row) << 7) + ((((col & 63) >> 3) ^ (row & 7)) << 4) + ((col & 7) << 1));
+}
+
 }  // namespace nkv

@@ -271,6 +271,63 @@ def test_decode_32k_matches_oracle():
         _close(got, want)
 
 
+def _rows_attention(q, kp, vp, cf, rows, scale):
+    """fp32 oracle attention of the query rows `rows` of a chunk over the packed keys:
+    row t sees history keys [0, cf) and chunk keys [cf, cf + t]."""
+    out = []
+    for t in rows:
+        n = cf + t + 1
+        out.append(orc.attention(q[t:t + 1], kp[:n], vp[:n], scale)[0])
+    return torch.stack(out)
+
+
+def test_prefill_c4_full_size():
+    """Segmented prefill operator at its benchmark geometry: a 4096-token chunk
+    at positions 28672-32767 after 7 stored chunks (Top-32 of 448 blocks, sink
+    64, recent 512, causal chunk), 32 Q / 8 KV heads.  Selection vs the oracle
+    (modulo 1e-3 ties); kernel (4)'s output on 96 rows (first, last, block
+    edges, random) vs the fp32 oracle over the same packed keys."""
+    nkv = pkg()
+    g = torch.Generator().manual_seed(28672)
+    layer = orc.OracleLayer(orc.OracleConfig())
+    rt = nkv.M12LayerRuntime(0, _cfg(max_model_len=36864))
+    for c in range(7):
+        _, k, v = qkv(g, 4096)
+        if c == 0:
+            rt.prefill_first(None, k.to(DEV), v.to(DEV))
+        else:
+            rt._store_kv(k.to(DEV), v.to(DEV))
+        layer.store(k, v)
+        layer.prefill_len = rt.prefill_len
+    layer.valid_len = rt.valid_len
+    assert rt.nblocks_filled == layer.nblocks == 448
+    q, k, v = qkv(g, 4096)
+    got = rt.prefill_chunk(q.to(DEV), k.to(DEV), v.to(DEV), DEV).cpu()
+    ids = rt.last_prefill_block_ids.cpu()
+    cfg = layer.cfg
+    own = layer._select(orc.query_summaries(q, cfg.prefill_query_segments), cfg.prefill_top_k_blocks)
+    ok, why = ids_match_modulo_ties(ids, own, layer.last_scores)
+    assert ok, why
+    kp, vp, cf = layer._history_pack(ids, k, v)
+    assert cf == 32 * 64 + 64 + 512  # selected + sink + recent (no overlap at 28672)
+    gen = torch.Generator().manual_seed(1)
+    rows = sorted(set([0, 1, 63, 64, 127, 128, 4031, 4094, 4095] +
+                      torch.randint(0, 4096, (87,), generator=gen).tolist()))
+    want = _rows_attention(q, kp, vp, cf, rows, cfg.scale)
+    _close(got[rows], want)
+
+
+def test_first_chunk_causal_matches_oracle():
+    """First-chunk dense causal attention through kernel (4) (no history)."""
+    nkv = pkg()
+    g = torch.Generator().manual_seed(7)
+    rt = nkv.M12LayerRuntime(0, _cfg())
+    q, k, v = qkv(g, 1000)
+    got = rt.first_chunk_attention(q.to(DEV), k.to(DEV), v.to(DEV)).cpu()
+    want = orc.attention(q, k, v, rt.cfg.scale, causal_from=0)
+    _close(got, want)
+
+
 @pytest.mark.parametrize("scheme", ["reference", "token"])
 @pytest.mark.parametrize("residency", ["hbm", "host"])
 def test_int8_history_decode(scheme, residency):
