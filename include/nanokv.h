@@ -171,6 +171,28 @@ int nkv_attend_last_config(int* cluster, int* splits, int* keys_per_cta);
 #define NKV_ATTEND_STATIC_SCRATCH_BYTES (8u << 20)
 int nkv_attend_static(nkv_stream_t stream, const nkv_attend_args* args);
 
+/* One decode step of a layer: nkv_select over the layer's representatives
+ * for the single query, then nkv_attend of that query over the selected
+ * blocks, sink, recent ring and the current token (which it appends to the
+ * ring at attend.ring_write_pos), with the attention overlapping the
+ * selection (programmatic dependent launch).  attend.block_ids / n_sel are
+ * replaced by out_ids / k, attend.overlap_select is implied.
+ * Replaces the device work of M12LayerRuntime.decode (m12_runtime.py:1141-1346:
+ * recent shift and append :1166-1172, select :1193-1198, gather and pack
+ * :1213-1309, attention :1316-1320) in one host call. */
+typedef struct {
+  nkv_attend_args attend; /* nq == n_cur == 1 */
+  const void* reps;       /* bf16 [hkv][reps_blocks][r][head_dim] */
+  int r, reps_blocks, nblocks;
+  const int32_t* protected_ids;
+  int n_protected, k;
+  int64_t* out_ids;       /* [k], device */
+  float* out_topk_scores; /* [k] or NULL */
+  void* select_workspace;
+  size_t select_workspace_bytes;
+} nkv_decode_args;
+int nkv_decode_step(nkv_stream_t stream, const nkv_decode_args* args);
+
 /* ------------------------------------------------------------------------ */
 /* (4) Segmented prefill attention on the tensor cores: the same four segments
  * as nkv_attend for a whole chunk of nq queries (nq == n_cur, causal in-chunk,

@@ -49,6 +49,16 @@ class AttendArgs(C.Structure):
     ]
 
 
+class DecodeArgs(C.Structure):
+    _fields_ = [
+        ("attend", AttendArgs),
+        ("reps", c_vp), ("r", c_int), ("reps_blocks", c_int), ("nblocks", c_int),
+        ("protected_ids", c_vp), ("n_protected", c_int), ("k", c_int),
+        ("out_ids", c_vp), ("out_topk_scores", c_vp),
+        ("select_workspace", c_vp), ("select_workspace_bytes", C.c_size_t),
+    ]
+
+
 class StoreArgs(C.Structure):
     _fields_ = [
         ("k", c_vp), ("v", c_vp),
@@ -82,6 +92,7 @@ SIGNATURES = {
     "nkv_attend": (c_int, [c_vp, C.POINTER(AttendArgs)]),
     "nkv_attend_last_config": (c_int, [C.POINTER(c_int), C.POINTER(c_int), C.POINTER(c_int)]),
     "nkv_attend_static": (c_int, [c_vp, C.POINTER(AttendArgs)]),
+    "nkv_decode_step": (c_int, [c_vp, C.POINTER(DecodeArgs)]),
     "nkv_prefill_workspace_bytes": (C.c_size_t, [c_int, c_int, c_int, c_int]),
     "nkv_prefill": (c_int, [c_vp, C.POINTER(AttendArgs)]),
     "nkv_store_chunk": (c_int, [c_vp, C.POINTER(StoreArgs)]),

@@ -1389,6 +1389,36 @@ static bool source_maps(DecodeMaps* m, int src, const void* k, const void* v, lo
   return tma_rows_map(&m->m[src][0][1], k, rows, 64) && tma_rows_map(&m->m[src][1][1], v, rows, 64);
 }
 
+// cudaOccupancyMaxActiveClusters for a launch configuration, cached per
+// thread by (kernel, device, cluster size, block count, shared memory): the
+// query costs microseconds of host time and its answer never changes.
+static bool cluster_occupancy(const void* kern, const cudaLaunchConfig_t& lc, int* nclusters) {
+  struct Entry { const void* fn; int dev, cl, blocks; size_t smem; int n; };
+  static thread_local Entry cache[32];
+  static thread_local int used = 0, next = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int cl = 1;
+  for (unsigned i = 0; i < lc.numAttrs; ++i)
+    if (lc.attrs[i].id == cudaLaunchAttributeClusterDimension) cl = (int)lc.attrs[i].val.clusterDim.x;
+  const int blocks = (int)(lc.gridDim.x * lc.gridDim.y * lc.gridDim.z);
+  for (int i = 0; i < used; ++i) {
+    const Entry& e = cache[i];
+    if (e.fn == kern && e.dev == dev && e.cl == cl && e.blocks == blocks && e.smem == lc.dynamicSmemBytes) {
+      *nclusters = e.n;
+      return true;
+    }
+  }
+  int n = 0;
+  const cudaError_t err = cudaOccupancyMaxActiveClusters(&n, kern, &lc);
+  cudaGetLastError();
+  if (err != cudaSuccess) return false;
+  const int slot = used < 32 ? used++ : (next++ & 31);
+  cache[slot] = Entry{kern, dev, cl, blocks, lc.dynamicSmemBytes, n};
+  *nclusters = n;
+  return true;
+}
+
 static size_t attend_ws(int hkv, int nr, int max_tokens) {
   const long long smax = (max_tokens + AT_MIN_TPS - 1) / AT_MIN_TPS + 1;
   size_t o = 256 + ((hkv * 4 + 255) / 256) * 256;
@@ -1648,8 +1678,7 @@ extern "C" int nkv_attend(nkv_stream_t stream, const nkv_attend_args* a) {
       int ok = p.splits <= 8 || !ensure_nonportable_cluster(kern, "attend");                    \
       int nclusters = 0;                                                                        \
       config(p);                                                                                \
-      if (ok && cudaOccupancyMaxActiveClusters(&nclusters, kern, &lc) != cudaSuccess) ok = 0;   \
-      cudaGetLastError();                                                                       \
+      if (ok && !cluster_occupancy(kern, lc, &nclusters)) ok = 0;                             \
       if (!ok || nclusters < 1) p = pg;                                                         \
     }                                                                                           \
     config(p);                                                                                  \

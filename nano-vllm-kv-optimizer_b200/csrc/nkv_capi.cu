@@ -50,3 +50,18 @@ extern "C" int nkv_map_host(void* host_ptr, void** dev_ptr) {
   }
   return NKV_OK;
 }
+
+extern "C" int nkv_decode_step(nkv_stream_t stream, const nkv_decode_args* a) {
+  NKV_REQUIRE(a, "decode_step: null args");
+  const nkv_attend_args& t = a->attend;
+  NKV_REQUIRE(t.nq == 1 && t.n_cur == 1, "decode_step: needs one query and one current token");
+  int rc = nkv_select(stream, t.q, 1, t.q_row_stride, t.q_head_stride, t.hq, t.hkv, t.head_dim, a->reps, a->r,
+                      a->reps_blocks, a->nblocks, a->protected_ids, a->n_protected, a->k, a->out_ids,
+                      a->out_topk_scores, nullptr, a->select_workspace, a->select_workspace_bytes);
+  if (rc != NKV_OK) return rc;
+  nkv_attend_args b = t;
+  b.block_ids = a->out_ids;
+  b.n_sel = a->k;
+  b.overlap_select = 1;
+  return nkv_attend(stream, &b);
+}

@@ -197,6 +197,16 @@ def _stream(device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _stream_fast(device_index: int) -> int:
+    """The current stream's handle without the device-object round trip."""
+    if _raw_stream is not None:
+        return _raw_stream(device_index)
+    return torch.cuda.current_stream(device_index).cuda_stream
+
+
 def _aligned(t: torch.Tensor) -> torch.Tensor:
     """The kernels read rows with 16-byte vector loads."""
     if (t.stride(-1) == 1 and t.data_ptr() % 16 == 0
@@ -282,6 +292,12 @@ class M12LayerRuntime:
         self._union_count = torch.zeros(1, dtype=torch.int32, **kw)
         self._allowed = torch.zeros(8, 8 * cfg.top_k_blocks, dtype=torch.uint8, **kw)
         self._prot_key = None
+        self._dargs, self._dkey, self._ids_view = None, None, None
+        self._lib_h = _lib.load()
+        # the single-call decode applies when no selection variant is configured
+        self._fast_ok = (cfg.decode_relative_a is None and not cfg.dynamic_top_k and not cfg.gather_sort
+                         and cfg.decode_query_window <= 1)
+        self._decode_requested = cfg.top_k_blocks if cfg.decode_top_k_blocks is None else cfg.decode_top_k_blocks
         self._prot_dev = torch.zeros(1, dtype=torch.int32, **kw)
         self._n_prot_dev = 0
         self._sel_ws = None
@@ -854,12 +870,100 @@ class M12LayerRuntime:
             return self._qwin[0]
         return prefill_query_summaries(self._qwin[:n], 1)[0]
 
+    def _decode_args(self, kk: int):
+        """Persistent nkv_decode_step arguments; the buffer-dependent part is
+        rebuilt only when the store, the history length, the budget or a
+        workspace changed since the previous step."""
+        cfg = self.cfg
+        key = (self.nblocks_filled, self.cpu_blocks_cap, self._store_ptrs, kk, id(self._ids),
+               id(self.k_scale), id(self.v_scale_cpu), id(self._k_tok_scale), id(self._sel_ws),
+               id(self._att_ws))
+        if key == self._dkey:
+            return self._dargs
+        d = _lib.DecodeArgs()
+        a = d.attend
+        a.nq, a.hq, a.hkv, a.head_dim, a.block_size = 1, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.block_size
+        a.scale = cfg.scale
+        a.max_blocks = self.cpu_blocks_cap
+        a.store_kind = self.store_kind
+        a.k_store, a.v_store = self._store_ptrs
+        a.k_chan_scale = _ptr(self.k_scale)
+        a.v_block_scale = _ptr(self.v_scale_cpu) if self.store_kind == _lib.STORE_INT8_REF else 0
+        a.k_tok_scale, a.v_tok_scale = _ptr(self._k_tok_scale), _ptr(self._v_tok_scale)
+        a.sink_k, a.sink_v, a.sink_cap = self._sink_k.data_ptr(), self._sink_v.data_ptr(), cfg.sink_tokens
+        a.ring_k, a.ring_v, a.ring_cap = self._ring_k.data_ptr(), self._ring_v.data_ptr(), cfg.recent_tokens
+        a.n_cur = 1
+        ws = self._attend_ws(1, kk * cfg.block_size + cfg.sink_tokens + cfg.recent_tokens + 1)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+        prot, nprot = self._protected_dev(self.nblocks_filled)
+        d.reps, d.r, d.reps_blocks, d.nblocks = self.reps_gpu.data_ptr(), cfg.r, self.max_blocks, self.nblocks_filled
+        d.protected_ids, d.n_protected, d.k = prot.data_ptr(), nprot, kk
+        d.out_ids, d.out_topk_scores = self._ids.data_ptr(), self._topk_scores.data_ptr()
+        sws = self._select_ws(1)
+        d.select_workspace, d.select_workspace_bytes = sws.data_ptr(), sws.numel()
+        key = (self.nblocks_filled, self.cpu_blocks_cap, self._store_ptrs, kk, id(self._ids),
+               id(self.k_scale), id(self.v_scale_cpu), id(self._k_tok_scale), id(self._sel_ws),
+               id(self._att_ws))
+        self._dargs, self._dkey = d, key
+        self._ids_view = self._ids[:kk]
+        return d
+
+    def _decode_fast(self, q, k, v, kk):
+        """The plain decode step as one native call (nkv_decode_step)."""
+        cfg = self.cfg
+        d = self._decode_args(kk)
+        a = d.attend
+        qs = q.stride()
+        qp = q.data_ptr()
+        if qs[-1] != 1 or qs[1] % 8 or qp % 16:
+            q = q.contiguous()
+            qs, qp = q.stride(), q.data_ptr()
+        ks, vs = k.stride(), v.stride()
+        kp, vp = k.data_ptr(), v.data_ptr()
+        if ks != vs or ks[-1] != 1 or ks[1] % 8 or kp % 16 or vp % 16:
+            k, v = k.contiguous(), v.contiguous()
+            ks, kp, vp = k.stride(), k.data_ptr(), v.data_ptr()
+        out = torch.empty(1, cfg.num_heads, cfg.head_dim, dtype=q.dtype, device=q.device)
+        a.q, a.q_row_stride, a.q_head_stride = qp, qs[0], qs[1]
+        a.cur_k, a.cur_v, a.cur_row_stride, a.cur_head_stride = kp, vp, ks[0], ks[1]
+        a.sink_len = min(cfg.sink_tokens, self.valid_len)
+        w, a.ring_start, a.ring_len, head_new = ring_decode_plan(self._ring_head, self.valid_len,
+                                                                 cfg.recent_tokens)
+        a.ring_write_pos = w
+        a.out, a.out_row_stride, a.out_head_stride = out.data_ptr(), cfg.num_heads * cfg.head_dim, cfg.head_dim
+        rc = self._lib_h.nkv_decode_step(_stream_fast(q.device.index or 0), d)
+        if rc != _lib.NKV_OK:
+            call("nkv_decode_step", _stream(q.device), C.byref(d))  # raises with the message
+        self._ring_head = head_new
+        return out, a.sink_len, a.ring_len
+
     def decode(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                device: torch.device) -> torch.Tensor:
         """One decode step: ring append, select, attend; no host synchronisation."""
         cfg = self.cfg
         R = cfg.recent_tokens
         assert q.shape[0] == 1 and k.shape[0] == 1
+        if (self._fast_ok and not self.record_q and q.dtype == torch.bfloat16
+                and self._k_store is not None):
+            t0 = perf_counter()
+            kk = self._budget(self._decode_requested)
+            o, sink_len, ring_len = self._decode_fast(q, k, v, kk)
+            t2 = perf_counter()
+            if self.record_ids:
+                self.ids_history.append(self._ids_view.cpu().tolist())
+            self.valid_len += 1
+            self._last_ids_dev, self._last_ids_host = self._ids_view, None
+            self.timings = {
+                "selector_ms": 0.0, "selector_enqueue_ms": 0.0,
+                "d2h_ms": 0.0, "cpu_gather_ms": 0.0, "h2d_pack_ms": 0.0,
+                "h2d_event_spans_cpu_gather": False, "recent_ms": 0.0,
+                "packed_attn_ms": (t2 - t0) * 1000.0,
+                "selected_tokens": kk * cfg.block_size,
+                "total_attend_tokens": kk * cfg.block_size + sink_len + ring_len + 1,
+            }
+            if cfg.check_finite_outputs and not bool(torch.isfinite(o).all()):
+                raise RuntimeError("M12 sparse decode output is non-finite")
+            return o
         if self.record_q:
             self.q_history.append(q[0].detach().cpu().clone())
         t0 = perf_counter()
