@@ -89,6 +89,12 @@ struct AttendParams {
   // decode kernel: tile rows per K (or V) tile, bytes of the K-tile region,
   // segments TMA may read (1 selected blocks, 2 sink, 4 ring: bf16 in device memory)
   int tile_rows, region_k, tma_mask;
+  // decode kernel, ranked mode: the CTAs rank these block scores (written by
+  // the preceding scoring grid) themselves instead of reading ids
+  const float* rank_scores;
+  int rank_n;
+  long long* rank_out;     // the ranked ids, written by CTA (0, 0)
+  float* rank_out_scores;  // their scores (optional)
 };
 
 // 2D tensor maps of the decode kernel over [rows][128] bf16 sources with
@@ -702,6 +708,44 @@ __device__ __forceinline__ void issue_piece(const DecodeMaps& tm, int src, int y
   }
 }
 
+// Top 32 of n fp32 block scores, ranked by the keys of nkv_select (score
+// descending, then block id ascending): each of the NW warps sorts its
+// 32-score chunks (bitonic, 64-bit keys) into a running list, skipping chunks
+// that cannot enter it, then the warp lists merge pairwise.  Returns with
+// lists[0..31] = ranks 0..31 (all threads must call).  n <= NW * 32 * MAXC.
+template <int NW, int MAXC>
+__device__ void rank_top32(const float* __restrict__ scores, int n, u64* lists) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float v[MAXC];
+#pragma unroll
+  for (int c = 0; c < MAXC; ++c) {
+    const int i = (warp + c * NW) * 32 + lane;
+    v[c] = i < n ? __ldcg(scores + i) : -INFINITY;
+  }
+  u64 run = 0ull;  // 0 is below every real key
+#pragma unroll 1
+  for (int c = 0; c < MAXC; ++c) {
+    const int base = (warp + c * NW) * 32;
+    if (base >= n) break;
+    const int i = base + lane;
+    float x = v[0];
+#pragma unroll
+    for (int cc = 1; cc < MAXC; ++cc) x = cc == c ? v[cc] : x;
+    const u64 key = i < n ? make_key(x, (uint32_t)i) : 0ull;
+    const uint32_t run_min = (uint32_t)(shfl64(run, 31) >> 32);
+    if (__reduce_max_sync(FULL, (uint32_t)(key >> 32)) >= run_min) run = warp_merge_desc(run, warp_sort_desc(key));
+  }
+  lists[warp * 32 + lane] = run;
+  __syncthreads();
+#pragma unroll
+  for (int st = 1; st < NW; st <<= 1) {
+    if ((warp % (2 * st)) == 0 && warp + st < NW)
+      lists[warp * 32 + lane] = warp_merge_desc(lists[warp * 32 + lane], lists[(warp + st) * 32 + lane]);
+    __syncthreads();
+  }
+}
+constexpr int RANK_MAXC = 8;  // ranked decode: nblocks <= 8 warps x 32 x 8 = 2048
+
 // Rows [pos0, pos0 + len) of the logical keys, loaded by the threads of the
 // CTA into tile rows row0... : 16-byte copies for bf16 sources (the current
 // tokens, a host-resident store, any segment TMA cannot address), in-register
@@ -898,7 +942,7 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
   }
   // block ids: read now unless they come from the grid this one overlaps
   long long id_early = 0;
-  if (!p.overlap && tid < nslots) id_early = __ldg(p.ids + slot0 + tid);
+  if (!p.overlap && !p.rank_scores && tid < nslots) id_early = __ldg(p.ids + slot0 + tid);
   if (warp < 2) {  // np <= AT_MAX_SLOTS + 4 pieces live in warps 0 and 1
     const unsigned bits = __ballot_sync(FULL, by_threads);
     if (lane == 0) s_thr[warp] = bits;
@@ -954,8 +998,20 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
       thread_rows(p, h, t0 + plo[i], plen[i], prow[i], kt, vt, NR, s_ids, slot0, selEnd, sinkEnd, ringEnd);
   }
   NKV_STAMP(trc, 62);
-  if (p.overlap) pdl_wait();  // block ids are complete past this point
-  if (tid < nslots) {
+  if (p.overlap) pdl_wait();  // block ids (or scores) are complete past this point
+  if (p.rank_scores) {
+    // ranked mode: the CTAs that hold selected blocks (and CTA (0, 0), which
+    // publishes the ids) rank the block scores themselves
+    if (nslots > 0 || (split == 0 && h == 0)) {
+      __shared__ u64 s_rank[NW * 32];
+      rank_top32<NW, RANK_MAXC>(p.rank_scores, p.rank_n, s_rank);
+      if (tid < nslots) s_ids[tid] = (long long)key_id(s_rank[slot0 + tid]);
+      if (split == 0 && h == 0 && tid < p.n_sel) {
+        p.rank_out[tid] = (long long)key_id(s_rank[tid]);
+        if (p.rank_out_scores) p.rank_out_scores[tid] = key_score(s_rank[tid]);
+      }
+    }
+  } else if (tid < nslots) {
     const long long id = p.overlap ? __ldg(p.ids + slot0 + tid) : id_early;
     const bool bad = id < 0 || id >= p.max_blocks;
     if (bad && p.err) atomicExch(p.err, ERR_BAD_INDEX);
@@ -1438,7 +1494,32 @@ extern "C" size_t nkv_attend_workspace_bytes(int hkv, int hq, int nq, int max_to
   return attend_ws(hkv, (hq / hkv) * nq, max_tokens);
 }
 
+struct RankArgs {
+  const float* scores;
+  int nblocks;
+  int64_t* out_ids;
+  float* out_scores;
+};
+
+static int attend_impl(nkv_stream_t stream, const nkv_attend_args* a, const RankArgs* rank);
+
 extern "C" int nkv_attend(nkv_stream_t stream, const nkv_attend_args* a) {
+  return attend_impl(stream, a, nullptr);
+}
+
+namespace nkv {
+int attend_ranked(nkv_stream_t stream, const nkv_attend_args* a, const float* scores, int nblocks,
+                  int64_t* out_ids, float* out_scores) {
+  NKV_REQUIRE(a && a->nq == 1 && scores && out_ids, "attend_ranked: needs one query, scores and out_ids");
+  NKV_REQUIRE(a->n_sel >= 1 && a->n_sel <= 32 && a->n_sel <= nblocks, "attend_ranked: k=%d out of [1, 32]",
+              a->n_sel);
+  NKV_SUPPORTED(nblocks <= 8 * 32 * RANK_MAXC, "attend_ranked: %d blocks exceed the in-kernel ranking", nblocks);
+  RankArgs r{scores, nblocks, out_ids, out_scores};
+  return attend_impl(stream, a, &r);
+}
+}  // namespace nkv
+
+static int attend_impl(nkv_stream_t stream, const nkv_attend_args* a, const RankArgs* rank) {
   NKV_REQUIRE(a, "attend: null args");
   NKV_SUPPORTED(a->head_dim == NKV_D, "attend: head_dim %d unsupported (128 only)", a->head_dim);
   NKV_REQUIRE(a->hkv >= 1 && a->hq % a->hkv == 0, "attend: hq %d not a multiple of hkv %d", a->hq,
@@ -1553,6 +1634,10 @@ extern "C" int nkv_attend(nkv_stream_t stream, const nkv_attend_args* a) {
   // NKV_ATTEND_MERGE: 0 = workspace merge, 1 = cluster merge where it fits
   if (env_int("NKV_ATTEND_MERGE", 1) == 0) p.cluster = 0;
   p.stop = env_int("NKV_DEBUG_STOP", 0);
+  p.rank_scores = rank ? rank->scores : nullptr;
+  p.rank_n = rank ? rank->nblocks : 0;
+  p.rank_out = rank ? (long long*)rank->out_ids : nullptr;
+  p.rank_out_scores = rank ? rank->out_scores : nullptr;
   AttendParams pg = p;  // workspace-merge configuration (fallback)
   pg.cluster = 0;
   {

@@ -1,6 +1,7 @@
 // C-ABI plumbing shared by all entry points: error message, version, and the
 // read-back of the error word kernels leave in a workspace.
 #include <stdarg.h>
+#include <stdlib.h>
 #include <stdio.h>
 
 #include "nkv_host.h"
@@ -55,6 +56,22 @@ extern "C" int nkv_decode_step(nkv_stream_t stream, const nkv_decode_args* a) {
   NKV_REQUIRE(a, "decode_step: null args");
   const nkv_attend_args& t = a->attend;
   NKV_REQUIRE(t.nq == 1 && t.n_cur == 1, "decode_step: needs one query and one current token");
+  // fused form: a scoring grid, then the attention grid ranks the scores in
+  // each CTA (no ranking tail between the two); NKV_DECODE_FUSED=0 selects
+  // the two public kernels instead
+  const char* env = getenv("NKV_DECODE_FUSED");
+  if ((!env || atoi(env) != 0) && a->k <= 32 && a->nblocks <= 2048) {
+    const float* scores = nullptr;
+    int rc = nkv::select_scores((cudaStream_t)stream, t.q, t.q_row_stride, t.q_head_stride, t.hq, t.hkv, t.head_dim,
+                                a->reps, a->r, a->reps_blocks, a->nblocks, a->protected_ids, a->n_protected, a->k,
+                                a->select_workspace, a->select_workspace_bytes, &scores);
+    if (rc != NKV_OK) return rc;
+    nkv_attend_args b = t;
+    b.block_ids = a->out_ids;
+    b.n_sel = a->k;
+    b.overlap_select = 1;
+    return nkv::attend_ranked(stream, &b, scores, a->nblocks, a->out_ids, a->out_topk_scores);
+  }
   int rc = nkv_select(stream, t.q, 1, t.q_row_stride, t.q_head_stride, t.hq, t.hkv, t.head_dim, a->reps, a->r,
                       a->reps_blocks, a->nblocks, a->protected_ids, a->n_protected, a->k, a->out_ids,
                       a->out_topk_scores, nullptr, a->select_workspace, a->select_workspace_bytes);

@@ -32,6 +32,7 @@ struct SelectParams {
   int n_protected;
   int k;
   int per_query;  // 1: separate ranking per query row (lossless verify)
+  int score_only; // 1: write the masked block scores and stop (the ranking happens in the consumer)
   long long* out_ids;
   float* out_topk_scores;
   float* out_block_scores;
@@ -241,6 +242,16 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel(SelectParams p) {
   const int b0 = blockIdx.x * p.bpc;
   const int nb = min(p.bpc, p.nblocks - b0);
   const int nrows = p.per_query ? p.nq : 1;
+  // protected flags of this CTA's blocks, set in one parallel pass (the list
+  // is short; a per-block scan would chain its loads)
+  __shared__ unsigned char s_prot[256];
+  for (int i = threadIdx.x; i < nb && i < 256; i += blockDim.x) s_prot[i] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < p.n_protected; i += blockDim.x) {
+    const int b = __ldg(p.protected_ids + i) - b0;
+    if (b >= 0 && b < nb && b < 256) s_prot[b] = 1;
+  }
+  // (made visible by the barrier that follows the first scoring round)
 
   // ---- phase 1: scores for this CTA's blocks ---------------------------------
   for (int row = 0; row < nrows; ++row) {
@@ -267,7 +278,7 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel(SelectParams p) {
         const int b = b0 + bl0 + threadIdx.x;
         float m = -INFINITY;
         for (int w = 0; w < SEL_WARPS; ++w) m = fmaxf(m, part[w][threadIdx.x]);
-        if (is_protected(p, b)) m = -INFINITY;
+        if ((bl0 + threadIdx.x < 256) ? s_prot[bl0 + threadIdx.x] : is_protected(p, b)) m = -INFINITY;
         p.scores[(long long)row * p.nblocks + b] = m;
         if (p.out_block_scores) p.out_block_scores[(long long)row * p.nblocks + b] = m;
       }
@@ -275,8 +286,10 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel(SelectParams p) {
     }
   }
 
-  // ---- hand-off: the last CTA ranks --------------------------------------------
   NKV_STAMP(trc, 1);
+  if (p.score_only) return;
+
+  // ---- hand-off: the last CTA ranks --------------------------------------------
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) s_ticket = atomicAdd(p.ticket, 1u);
@@ -467,6 +480,20 @@ extern "C" int nkv_select(nkv_stream_t stream, const void* q, int nq, int64_t q_
   p.out_block_scores = out_block_scores;
   return launch_select((cudaStream_t)stream, p, hq / hkv);
 }
+
+namespace nkv {
+int select_scores(cudaStream_t st, const void* q, int64_t q_row_stride, int64_t q_head_stride, int hq, int hkv,
+                  int head_dim, const void* reps, int r, int max_blocks, int nblocks, const int32_t* protected_ids,
+                  int n_protected, int k, void* workspace, size_t workspace_bytes, const float** scores) {
+  SelectParams p;
+  int rc = select_common(st, q, 1, q_row_stride, q_head_stride, hq, hkv, head_dim, reps, r, max_blocks, nblocks,
+                         protected_ids, n_protected, k, workspace, workspace_bytes, 0, p);
+  if (rc) return rc;
+  p.score_only = 1;
+  *scores = p.scores;
+  return launch_select(st, p, hq / hkv);
+}
+}  // namespace nkv
 
 extern "C" int nkv_select_per_query(nkv_stream_t stream, const void* q, int nq, int64_t q_row_stride,
                                     int64_t q_head_stride, int hq, int hkv, int head_dim,
