@@ -92,6 +92,11 @@ int select_scores(cudaStream_t st, const void* q, int64_t q_row_stride, int64_t 
 int attend_ranked(nkv_stream_t stream, const nkv_attend_args* args, const float* scores, int nblocks,
                   int64_t* out_ids, float* out_scores);
 
+// prefill_tc: kernel (4) on tcgen05/TMEM for the calls it supports (bf16
+// history in device memory, block_size 64, TMA-addressable tensors); returns
+// NKV_ERR_UNSUPPORTED without launching for the others.
+int prefill_tc(cudaStream_t st, const nkv_attend_args* args);
+
 }  // namespace nkv
 
 #define NKV_REQUIRE(cond, ...)              \

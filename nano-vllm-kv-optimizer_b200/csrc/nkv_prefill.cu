@@ -20,6 +20,8 @@
 //           fragments, O += P V with P re-packed as the bf16 A operand and V
 //           via ldmatrix.trans.  fp32 accumulation throughout.
 // Position tiles are scheduled last-first (they see the most keys).
+#include <stdlib.h>
+
 #include "nkv_common.cuh"
 #include "nkv_host.h"
 
@@ -406,9 +408,15 @@ extern "C" int nkv_prefill(nkv_stream_t stream, const nkv_attend_args* a) {
   p.out_head = a->out_head_stride;
   p.err = (int*)a->workspace;
 
+  cudaStream_t st = (cudaStream_t)stream;
+  // the tcgen05/TMEM kernel takes every call it supports (NKV_PREFILL_TC=0: never)
+  const char* tc_env = getenv("NKV_PREFILL_TC");
+  if (!tc_env || atoi(tc_env) != 0) {
+    const int rc = prefill_tc(st, a);
+    if (rc != NKV_ERR_UNSUPPORTED) return rc;
+  }
   const int P = PF_ROWS / G;
   dim3 grid((a->nq + P - 1) / P, a->hkv);
-  cudaStream_t st = (cudaStream_t)stream;
   switch (G) {
 #define NKV_PF_CASE(GG)                                                            \
   case GG:                                                                         \
