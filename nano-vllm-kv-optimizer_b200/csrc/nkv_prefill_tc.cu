@@ -9,7 +9,7 @@
 // the physical wrap (each padded to whole tiles), then the chunk.  Padding rows
 // are masked; every tile is one 64-row TMA box per 64-column half.
 //
-// CTA = 128 query rows (128 / G positions x G heads of one KV head), 192 threads:
+// CTA = 128 query rows (128 / G positions x G heads of one KV head), 320 threads:
 //   warp 0     TMA producer: Q once (3D map over [T][hq][D]), K and V of each
 //              tile into a 3-stage ring (2D maps over the store, sink and ring,
 //              3D maps over the chunk), 128-byte swizzle.
@@ -17,11 +17,12 @@
 //              thread: S_j = Q K_j^T (M 128, N 64, K 128; double-buffered S),
 //              then O += P_{j-1} V_{j-1} (M 128, N 128, K 64; V as an MN-major
 //              operand), tcgen05.commit to mbarriers.
-//   warps 2-5  one query row per thread (TMEM lane): S row from TMEM, mask,
-//              online softmax in the exp2 domain with lazy rescaling of O (only
-//              when the row max grows by more than 2^8), P as bf16 into a
-//              swizzled shared tile (the A operand of the next MMA), and the
-//              epilogue O / l -> bf16.
+//   warps 2-9  two threads per query row (TMEM lane), 32 scores each: S from
+//              TMEM, mask, online softmax in the exp2 domain with lazy rescaling
+//              of O (only when the row max grows by more than 2^8; the pair
+//              shares the row max through shared memory), P as bf16 into a
+//              double-buffered swizzled shared tile (the A operand of the next
+//              MMA), and the epilogue O / l -> bf16.
 // Every wait is bounded (error word + fall through); TMEM is freed by warp 1
 // after all warps meet at the end.
 #include <cuda.h>
@@ -31,7 +32,7 @@
 
 namespace nkv {
 
-constexpr int TC_THREADS = 192;
+constexpr int TC_THREADS = 320;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-9 softmax
 constexpr int TC_M = 128;
 constexpr int TC_N = 64;
 constexpr int TC_STAGES = 3;
@@ -128,10 +129,20 @@ __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.
 // Bounded wait that fails fast: the first wait to run out (0.2 s) records
 // ERR_WAIT_TIMEOUT and raises the CTA's flag, after which every wait returns
 // at once, so a broken hand-off ends the kernel instead of stalling it.
+__device__ __forceinline__ bool tc_try(uint64_t* bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ void tc_wait(uint64_t* bar, uint32_t phase, int* err, volatile int* fail) {
+  if (tc_try(bar, phase)) return;
   if (*fail) return;
-  for (int i = 0; i < 2000; ++i) {
-    if (mbar_try_wait(bar, phase)) return;
+  for (long long t0 = clock64(); clock64() - t0 < 400000000ll;) {  // ~0.2 s at 2 GHz
+    if (tc_try(bar, phase)) return;
     if (*fail) return;
   }
   *fail = 1;
@@ -153,10 +164,14 @@ __device__ __forceinline__ void tc_drain(uint64_t* bar, uint32_t phase, int* err
 struct Tile {
   int src, y, valid;
 };
-__device__ __forceinline__ Tile tile_of(const TcParams& p, int h, int j, int lenA, int nA, int nB) {
+__device__ __forceinline__ Tile tile_of(const TcParams& p, int h, int j, int lenA, int nA, int nB,
+                                        bool rows = true) {
   Tile t;
   t.valid = TC_N;
   if (j < p.n_sel) {
+    t.src = 0;
+    t.y = 0;
+    if (!rows) return t;  // the softmax threads need only the kind of tile
     long long id = __ldg(p.ids + j);
     if (id < 0 || id >= p.max_blocks) {
       if (p.err) atomicExch(p.err, ERR_BAD_INDEX);
@@ -229,9 +244,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParam
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&s_free[b], 128);
+      mbar_init(&s_free[b], 256);
     }
-    mbar_init(&p_full, 128);
+    mbar_init(&p_full, 256);
     mbar_init(&o_done[0], 1);
     mbar_init(&o_done[1], 1);
     mbar_init(&fin, 1);
@@ -325,8 +340,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParam
     __syncwarp();
   } else {
     // ---------------- softmax / correction / epilogue ----------------
-    const int q4 = warp & 3;
+    // two warps per TMEM lane quadrant: warp 2 + q (half 0) and warp 6 + q
+    // (half 1) share rows q*32..q*32+31; a thread owns 32 of its row's 64
+    // scores and 64 of its 128 output columns; the pair exchanges row maxima
+    // through shared memory and a 64-thread named barrier (id 1 + quadrant)
+    __shared__ float s_pmax[2][2][TC_M];
+    const int q4 = warp & 3, half = (warp - 2) >> 2;
     const int row = q4 * 32 + lane;
+    const uint32_t bar_id = 1 + q4;
     const uint32_t trow = tbase + ((uint32_t)(q4 * 32) << 16);
     const int pos = p0 + row / G, g = row % G;
     float m_ref = -INFINITY, l = 0.f;
@@ -334,32 +355,31 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParam
       const int sb = j & 1;
       tc_wait(&s_full[sb], (j >> 1) & 1, p.err, &s_fail);
       tc_fence_after();
-      uint32_t sr[64];
-      {
-        uint32_t (&lo)[32] = *reinterpret_cast<uint32_t(*)[32]>(sr);
-        uint32_t (&hi)[32] = *reinterpret_cast<uint32_t(*)[32]>(sr + 32);
-        tmem_ld32(trow + sb * TC_N, lo);
-        tmem_ld32(trow + sb * TC_N + 32, hi);
-      }
+      uint32_t sr[32];
+      tmem_ld32(trow + sb * TC_N + half * 32, sr);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&s_free[sb]);
-      const Tile t = tile_of(p, 0, j, lenA, nA, nB);  // only src / valid / chunk base are used here
+      const Tile t = tile_of(p, 0, j, lenA, nA, nB, false);  // only src / valid / chunk base are used
       // masking only where a tile has padding rows or chunk keys past the
       // first row's position; the scale is applied inside the exponent
       const bool need_mask = t.src == 3 ? (t.y + TC_N - 1 > p0 + off) : (t.valid < TC_N);
       float mxr = -INFINITY;
       if (need_mask) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const bool vis = t.src == 3 ? (t.y + c <= pos + off) : (c < t.valid);
+        for (int c = 0; c < 32; ++c) {
+          const int kc = half * 32 + c;
+          const bool vis = t.src == 3 ? (t.y + kc <= pos + off) : (kc < t.valid);
           if (!vis) sr[c] = __float_as_uint(-INFINITY);
           mxr = fmaxf(mxr, __uint_as_float(sr[c]));
         }
       } else {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) mxr = fmaxf(mxr, __uint_as_float(sr[c]));
+        for (int c = 0; c < 32; ++c) mxr = fmaxf(mxr, __uint_as_float(sr[c]));
       }
+      s_pmax[j & 1][half][row] = mxr;
+      asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
+      mxr = fmaxf(mxr, s_pmax[j & 1][half ^ 1][row]);
       const float m_new = fmaxf(m_ref, mxr * p.sl2);
       const bool rescale = m_new > m_ref + 8.f;
       // P buffer j % 2 is free once PV_{j-2} is done; O is current once PV_{j-1} is
@@ -370,13 +390,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParam
           const float alpha = exp2f(m_ref - m_new);
           tc_fence_after();
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
+          for (int cc = 0; cc < 2; ++cc) {
             uint32_t o[32];
-            tmem_ld32(trow + 2 * TC_N + cc * 32, o);
+            const uint32_t ta = trow + 2 * TC_N + half * 64 + cc * 32;
+            tmem_ld32(ta, o);
             tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st32(trow + 2 * TC_N + cc * 32, o);
+            tmem_st32(ta, o);
           }
           tmem_wait_st();
           l *= alpha;
@@ -384,9 +405,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParam
         m_ref = m_new;
       }
       const float nbase = m_ref == -INFINITY ? 0.f : -m_ref;
-      uint32_t pw[32];
+      uint32_t pw[16];
 #pragma unroll
-      for (int c = 0; c < 64; c += 2) {
+      for (int c = 0; c < 32; c += 2) {
         const float a = exp2f(fmaf(__uint_as_float(sr[c]), p.sl2, nbase));
         const float b = exp2f(fmaf(__uint_as_float(sr[c + 1]), p.sl2, nbase));
         l += a + b;
@@ -395,22 +416,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParam
       }
       unsigned char* prow = ps + (j & 1) * TC_P_BYTES + row * 128;
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch)
-        *reinterpret_cast<uint4*>(prow + ((ch ^ (row & 7)) << 4)) =
+      for (int ch = 0; ch < 4; ++ch)
+        *reinterpret_cast<uint4*>(prow + (((half * 4 + ch) ^ (row & 7)) << 4)) =
             make_uint4(pw[ch * 4], pw[ch * 4 + 1], pw[ch * 4 + 2], pw[ch * 4 + 3]);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full);
     }
-    // epilogue: O / l -> bf16
+    // epilogue: O / l -> bf16 (row sums of the pair added through shared memory)
+    s_pmax[0][half][row] = l;
+    asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
+    l += s_pmax[0][half ^ 1][row];
     if (ntiles > 0) tc_wait(&o_done[(ntiles - 1) & 1], ((ntiles - 1) >> 1) & 1, p.err, &s_fail);
     tc_fence_after();
     const float inv = 1.f / l;
-    __nv_bfloat16* dst = p.out + (long long)pos * p.out_row + (long long)(h * G + g) * p.out_head;
+    __nv_bfloat16* dst = p.out + (long long)pos * p.out_row + (long long)(h * G + g) * p.out_head + half * 64;
 #pragma unroll
-    for (int cc = 0; cc < 4; ++cc) {
+    for (int cc = 0; cc < 2; ++cc) {
       uint32_t o[32];
-      tmem_ld32(trow + 2 * TC_N + cc * 32, o);
+      tmem_ld32(trow + 2 * TC_N + half * 64 + cc * 32, o);
       tmem_wait_ld();
       if (pos < p.nq) {
 #pragma unroll
