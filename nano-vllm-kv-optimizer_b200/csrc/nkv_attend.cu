@@ -1048,12 +1048,12 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
     while (pb + 1 < np && plo[pb + 1] < hi) ++pb;
   }
   for (int i = pa; i <= pb; ++i)
-    if (ptype[i] <= PT_RING) mbar_wait_bounded(&kbar[i], 0, p.err);
+    if (ptype[i] <= PT_RING) mbar_wait_poll(&kbar[i], 0, p.err);
   NKV_STAMP(trc, 51);
 #ifdef NKV_CHECKED
   if (p.stop == 1) {
     for (int i = pa; i <= pb; ++i)
-      if (ptype[i] <= PT_RING) mbar_wait_bounded(&vbar[i], 0, p.err);
+      if (ptype[i] <= PT_RING) mbar_wait_poll(&vbar[i], 0, p.err);
     return;
   }
 #endif
@@ -1130,7 +1130,7 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
   lloc += __shfl_xor_sync(FULL, lloc, 2);
   NKV_STAMP(trc, 52);
   for (int i = pa; i <= pb; ++i)
-    if (ptype[i] <= PT_RING) mbar_wait_bounded(&vbar[i], 0, p.err);
+    if (ptype[i] <= PT_RING) mbar_wait_poll(&vbar[i], 0, p.err);
   NKV_STAMP(trc, 53);
 #ifdef NKV_CHECKED
   if (p.stop == 2) { if (lane == 0 && mloc == 1.2345f) p.out[0] = __float2bfloat16(lloc); return; }
@@ -1617,6 +1617,13 @@ static int attend_impl(nkv_stream_t stream, const nkv_attend_args* a, const Rank
   if (cl_env != 0 && (cl_env > 0 || a->hkv * AT_CLUSTER_MAX >= sms / 2 || a->hkv * 8 >= sms / 2)) {
     C = cl_env > 0 ? (cl_env > AT_CLUSTER_MAX ? AT_CLUSTER_MAX : cl_env) : AT_CLUSTER_MAX;
     while (cl_env <= 0 && C > 1 && a->hkv * C > sms + sms / 4) C >>= 1;
+    if (cl_env <= 0 && a->nq == 1) {
+      // single query: the fewest CTAs per head that keep <= 336 keys each
+      // (the per-CTA prologue and merge dominate small CTAs)
+      int c = 1;
+      while (c < AT_CLUSTER_MAX && (p.ntok + c - 1) / c > 336) c <<= 1;
+      if (c < C) C = c;
+    }
     int tps = (p.ntok + C - 1) / C;
     if (tps < AT_MIN_TPS) {
       C = (p.ntok + AT_MIN_TPS - 1) / AT_MIN_TPS;

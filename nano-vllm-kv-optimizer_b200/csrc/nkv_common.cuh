@@ -184,6 +184,26 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase,
   return false;
 }
 
+// Polled wait (no suspend hint: a suspended thread can wake long after the
+// phase completes).  Bounded by ~0.2 s of SM clock; returns false and records
+// ERR_WAIT_TIMEOUT when the bound is hit.
+__device__ __forceinline__ bool mbar_try_wait_poll(uint64_t* bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_poll(uint64_t* bar, uint32_t phase, int* err) {
+  if (mbar_try_wait_poll(bar, phase)) return true;
+  for (long long t0 = clock64(); clock64() - t0 < 400000000ll;)
+    if (mbar_try_wait_poll(bar, phase)) return true;
+  if (err) atomicExch(err, ERR_WAIT_TIMEOUT);
+  return false;
+}
+
 // 16-byte asynchronous global->shared copies (the L1 path); completion is
 // tracked per thread by commit groups.
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
