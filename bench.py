@@ -68,6 +68,131 @@ def tensor_peak():
     return 1590.0, "fallback"
 
 
+# int8 history (per-token per-KV-head bf16 scale) in pinned
+# host memory; per layer-token the selected blocks cross the host link
+OFF_LAYERS = 8
+OFF_BYTES = TOPK * B * HKV * D * 2 + TOPK * B * HKV * 2 * 2  # int8 K+V + bf16 K,V scales
+
+
+def host_link_gbs(dev, mib=256):
+    """Pinned host -> device copy bandwidth of this box (the offload roofline)."""
+    h = torch.empty(mib << 20, dtype=torch.uint8).pin_memory()
+    d = torch.empty(mib << 20, dtype=torch.uint8, device=dev)
+    for _ in range(2):
+        d.copy_(h, non_blocking=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        d.copy_(h, non_blocking=True)
+    e1.record()
+    e1.synchronize()
+    gbs = 5 * (mib << 20) / (e0.elapsed_time(e1) * 1e-3) / 1e9
+    del h, d
+    return gbs
+
+
+def offload_measure(nkv, dev, steps=20):
+    """Decode step (select + attend) with the history int8 in mapped pinned host
+    memory; the attention kernel reads the selected blocks over the host link
+    and dequantises them in registers."""
+    g = torch.Generator(device=dev).manual_seed(77)
+    layers = []
+    for li in range(OFF_LAYERS):
+        rt = nkv.M12LayerRuntime(li, nkv.M12Config(max_model_len=CTX + 4096, device=dev, quant_history=True,
+                                                   quant_scheme="token", kv_residency="host"))
+        rt.reserve_blocks(CTX // B)
+        for c in range(CTX // 4096):
+            k = torch.randn(4096, HKV, D, generator=g, device=dev).bfloat16()
+            v = torch.randn(4096, HKV, D, generator=g, device=dev).bfloat16()
+            if c == 0:
+                rt.prefill_first(None, k, v)
+            else:
+                rt._store_kv(k, v)
+        layers.append(rt)
+    torch.cuda.synchronize()
+    qs = torch.randn(OFF_LAYERS, 1, HQ, D, generator=g, device=dev).bfloat16()
+    ks = torch.randn(OFF_LAYERS, 1, HKV, D, generator=g, device=dev).bfloat16()
+    vs = torch.randn(OFF_LAYERS, 1, HKV, D, generator=g, device=dev).bfloat16()
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for li, rt in enumerate(layers):
+            rt.decode(qs[li], ks[li], vs[li], dev)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for li, rt in enumerate(layers):
+            rt.decode(qs[li], ks[li], vs[li], dev)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        e1.record(stream)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / (steps * OFF_LAYERS)
+    link = host_link_gbs(dev)
+    achieved = OFF_BYTES / (us * 1e-6) / 1e9
+    del graph, layers
+    return {"workload": "decode step @32K, int8 history (per-token bf16 scales) in pinned host memory, "
+                        "8 layer states, Top-32 selected blocks read over the host link",
+            "us_per_layer": round(us, 2), "host_bytes_per_layer": OFF_BYTES,
+            "roofline": {"bound": "host link", "achieved": round(achieved, 1), "peak": round(link, 1),
+                         "unit": "GB/s", "frac": round(achieved / link, 4),
+                         "peak_kind": "measured pinned H2D copy (256 MiB) on this box"}}
+
+
+# BASELINE config 5 (operator part): KV heads sharded over the N ranks, 128K history
+SH_CTX, SH_LAYERS = 131072, 4
+
+
+def sharded_measure(nkv, dev, world, steps=20):
+    """Decode step with the KV heads split over the ranks (KVHeadShardedLayer):
+    per layer, scoring of the rank's heads, MAX all-reduce of the block scores,
+    attention of the rank's heads, all-gather of the outputs.  Eager (NCCL
+    calls between the kernels); device time between events, max over ranks."""
+    import torch.distributed as dist
+    g = torch.Generator(device=dev).manual_seed(5150)
+    layers = []
+    for li in range(SH_LAYERS):
+        lay = nkv.KVHeadShardedLayer(li, nkv.M12Config(max_model_len=SH_CTX + 4096, device=dev))
+        lay.rt.reserve_blocks(SH_CTX // B)
+        for c in range(SH_CTX // 4096):
+            k = torch.randn(4096, HKV, D, generator=g, device=dev).bfloat16()
+            v = torch.randn(4096, HKV, D, generator=g, device=dev).bfloat16()
+            if c == 0:
+                lay.prefill_first(None, k, v)
+            else:
+                lay.store(k, v)
+        layers.append(lay)
+    q = torch.randn(SH_LAYERS, 1, HQ, D, generator=g, device=dev).bfloat16()
+    k = torch.randn(SH_LAYERS, 1, HKV, D, generator=g, device=dev).bfloat16()
+    v = torch.randn(SH_LAYERS, 1, HKV, D, generator=g, device=dev).bfloat16()
+
+    def step():
+        for li, lay in enumerate(layers):
+            lay.decode(q[li], k[li], v[li])
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    e1.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) * 1000.0 / (steps * SH_LAYERS)], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    del layers
+    return {"workload": f"decode step @128K, KV heads sharded {world} ways (NCCL MAX all-reduce of block "
+                        "scores + all-gather of outputs per layer), 4 layer states, eager",
+            "us_per_layer": round(float(t.item()), 2), "kv_heads_per_gpu": HKV // world}
+
+
 def prefill_measure(nkv, dev, iters=5):
     """Kernel (4) at BASELINE config 4: one 4096-token chunk at positions
     28672-32767 over its Top-32 blocks, sink, recent window and causal chunk."""
@@ -200,6 +325,8 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--cpu-steps", type=int, default=20)
     ap.add_argument("--no-prefill", action="store_true", help="skip the kernel (4) measurement")
+    ap.add_argument("--no-offload", action="store_true", help="skip the host-offload decode measurement")
+    ap.add_argument("--no-sharded", action="store_true", help="skip the KV-head-sharded measurement (N > 1)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -338,10 +465,14 @@ def main():
     e2e_value = e2e_ms * 1000.0 / (L * world)
 
     line = None
-    prefill = None
+    prefill = offload = sharded = None
+    if world > 1 and not args.no_sharded:
+        sharded = sharded_measure(nkv, dev, world)
     if rank == 0 and not args.no_prefill:
         with torch.cuda.stream(stream):
             prefill = prefill_measure(nkv, dev)
+    if rank == 0 and not args.no_offload:
+        offload = offload_measure(nkv, dev)
     if rank == 0:
         cpu_us, n_cpu = cpu_reference(args.cpu_steps, 3, threads)
         line = {
@@ -368,6 +499,8 @@ def main():
                               "keys_per_cta": attend_cfg[2]},
             "clocks": clocks,
             "prefill": prefill,
+            "offload": offload,
+            "kv_head_sharded": sharded,
         }
         print(json.dumps(line))
     del graph, g_att

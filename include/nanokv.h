@@ -193,6 +193,24 @@ typedef struct {
 } nkv_decode_args;
 int nkv_decode_step(nkv_stream_t stream, const nkv_decode_args* args);
 
+/* The two halves of nkv_decode_step, for a caller that combines block scores
+ * across devices between them (KV heads sharded over GPUs: each rank scores
+ * its own heads, the scores are max-reduced over the ranks, then every rank
+ * attends its heads to the blocks ranked from the reduced scores).
+ * nkv_select_scores writes the protection-masked block scores of one query
+ * row (max over the given heads and reps) to out_scores [nblocks]; it is
+ * M12LayerRuntime._gpu_select's scoring (m12_runtime.py:999-1003) without the
+ * topk.  nkv_attend_ranked is nkv_attend for one query whose CTAs rank
+ * `scores` themselves (top args->n_sel, nkv_select's order; n_sel <= 32,
+ * nblocks <= 2048); the ranked ids (and scores when out_scores != NULL) are
+ * written to out_ids.  args->block_ids must equal out_ids. */
+int nkv_select_scores(nkv_stream_t stream, const void* q, int64_t q_row_stride, int64_t q_head_stride, int hq,
+                      int hkv, int head_dim, const void* reps, int r, int max_blocks, int nblocks,
+                      const int32_t* protected_ids, int n_protected, float* out_scores, void* workspace,
+                      size_t workspace_bytes);
+int nkv_attend_ranked(nkv_stream_t stream, const nkv_attend_args* args, const float* scores, int nblocks,
+                      int64_t* out_ids, float* out_scores);
+
 /* ------------------------------------------------------------------------ */
 /* (4) Segmented prefill attention on the tensor cores: the same four segments
  * as nkv_attend for a whole chunk of nq queries (nq == n_cur, causal in-chunk,

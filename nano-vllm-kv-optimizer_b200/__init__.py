@@ -16,8 +16,10 @@ from .m12_runtime import (
     prefill_query_summaries,
     prefill_recent_slice,
 )
+from .sharded import KVHeadShardedLayer
 
 __all__ = [
+    "KVHeadShardedLayer",
     "M12Config",
     "M12LayerRuntime",
     "dynamic_top_k_from_scores",

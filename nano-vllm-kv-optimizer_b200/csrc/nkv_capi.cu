@@ -64,7 +64,7 @@ extern "C" int nkv_decode_step(nkv_stream_t stream, const nkv_decode_args* a) {
     const float* scores = nullptr;
     int rc = nkv::select_scores((cudaStream_t)stream, t.q, t.q_row_stride, t.q_head_stride, t.hq, t.hkv, t.head_dim,
                                 a->reps, a->r, a->reps_blocks, a->nblocks, a->protected_ids, a->n_protected, a->k,
-                                a->select_workspace, a->select_workspace_bytes, &scores);
+                                a->select_workspace, a->select_workspace_bytes, &scores, nullptr);
     if (rc != NKV_OK) return rc;
     nkv_attend_args b = t;
     b.block_ids = a->out_ids;
@@ -81,4 +81,21 @@ extern "C" int nkv_decode_step(nkv_stream_t stream, const nkv_decode_args* a) {
   b.n_sel = a->k;
   b.overlap_select = 1;
   return nkv_attend(stream, &b);
+}
+
+extern "C" int nkv_select_scores(nkv_stream_t stream, const void* q, int64_t q_row_stride, int64_t q_head_stride,
+                                 int hq, int hkv, int head_dim, const void* reps, int r, int max_blocks, int nblocks,
+                                 const int32_t* protected_ids, int n_protected, float* out_scores, void* workspace,
+                                 size_t workspace_bytes) {
+  NKV_REQUIRE(out_scores, "select_scores: null out_scores");
+  const float* ws_scores = nullptr;
+  return nkv::select_scores((cudaStream_t)stream, q, q_row_stride, q_head_stride, hq, hkv, head_dim, reps, r,
+                            max_blocks, nblocks, protected_ids, n_protected, 1, workspace, workspace_bytes, &ws_scores,
+                            out_scores);
+}
+
+extern "C" int nkv_attend_ranked(nkv_stream_t stream, const nkv_attend_args* a, const float* scores, int nblocks,
+                                 int64_t* out_ids, float* out_scores) {
+  NKV_REQUIRE(a && a->block_ids == out_ids, "attend_ranked: args->block_ids must be out_ids");
+  return nkv::attend_ranked(stream, a, scores, nblocks, out_ids, out_scores);
 }

@@ -81,11 +81,13 @@ inline int ensure_nonportable_cluster(Kernel kernel, const char* what) {
 
 // Internal launchers of the fused decode step (nkv_decode_step).
 // select_scores: the scoring half of nkv_select for one query row; writes the
-// protected-masked block scores into the select workspace and returns their
-// address (the grid signals programmatic dependents at its start).
+// protected-masked block scores into the select workspace (and to
+// out_block_scores when given) and returns the workspace copy's address (the
+// grid signals programmatic dependents at its start).
 int select_scores(cudaStream_t st, const void* q, int64_t q_row_stride, int64_t q_head_stride, int hq, int hkv,
                   int head_dim, const void* reps, int r, int max_blocks, int nblocks, const int32_t* protected_ids,
-                  int n_protected, int k, void* workspace, size_t workspace_bytes, const float** scores);
+                  int n_protected, int k, void* workspace, size_t workspace_bytes, const float** scores,
+                  float* out_block_scores);
 // attend_ranked: nkv_attend for one query whose CTAs rank the block scores of
 // a preceding select_scores themselves (top args->n_sel), after waiting for it.
 // The ranked ids (and scores, when out_scores != NULL) are written to out_ids.

@@ -484,12 +484,14 @@ extern "C" int nkv_select(nkv_stream_t stream, const void* q, int nq, int64_t q_
 namespace nkv {
 int select_scores(cudaStream_t st, const void* q, int64_t q_row_stride, int64_t q_head_stride, int hq, int hkv,
                   int head_dim, const void* reps, int r, int max_blocks, int nblocks, const int32_t* protected_ids,
-                  int n_protected, int k, void* workspace, size_t workspace_bytes, const float** scores) {
+                  int n_protected, int k, void* workspace, size_t workspace_bytes, const float** scores,
+                  float* out_block_scores) {
   SelectParams p;
   int rc = select_common(st, q, 1, q_row_stride, q_head_stride, hq, hkv, head_dim, reps, r, max_blocks, nblocks,
                          protected_ids, n_protected, k, workspace, workspace_bytes, 0, p);
   if (rc) return rc;
   p.score_only = 1;
+  p.out_block_scores = out_block_scores;
   *scores = p.scores;
   return launch_select(st, p, hq / hkv);
 }

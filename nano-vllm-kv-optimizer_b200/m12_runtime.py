@@ -293,6 +293,7 @@ class M12LayerRuntime:
         self._allowed = torch.zeros(8, 8 * cfg.top_k_blocks, dtype=torch.uint8, **kw)
         self._prot_key = None
         self._dargs, self._dkey, self._ids_view = None, None, None
+        self._bscores = None
         self._lib_h = _lib.load()
         # the single-call decode applies when no selection variant is configured
         self._fast_ok = (cfg.decode_relative_a is None and not cfg.dynamic_top_k and not cfg.gather_sort
@@ -908,8 +909,9 @@ class M12LayerRuntime:
         self._ids_view = self._ids[:kk]
         return d
 
-    def _decode_fast(self, q, k, v, kk):
-        """The plain decode step as one native call (nkv_decode_step)."""
+    def _decode_fill(self, q, k, v, kk):
+        """Per-call fields of the persistent decode arguments; returns
+        (args, output, ring head after the step)."""
         cfg = self.cfg
         d = self._decode_args(kk)
         a = d.attend
@@ -931,11 +933,61 @@ class M12LayerRuntime:
                                                                  cfg.recent_tokens)
         a.ring_write_pos = w
         a.out, a.out_row_stride, a.out_head_stride = out.data_ptr(), cfg.num_heads * cfg.head_dim, cfg.head_dim
+        return d, out, head_new
+
+    def _decode_fast(self, q, k, v, kk):
+        """The plain decode step as one native call (nkv_decode_step)."""
+        d, out, head_new = self._decode_fill(q, k, v, kk)
         rc = self._lib_h.nkv_decode_step(_stream_fast(q.device.index or 0), d)
         if rc != _lib.NKV_OK:
             call("nkv_decode_step", _stream(q.device), C.byref(d))  # raises with the message
         self._ring_head = head_new
-        return out, a.sink_len, a.ring_len
+        return out, d.attend.sink_len, d.attend.ring_len
+
+    # ------------------------------------------------------------------
+    # decode split in two halves around a cross-device score reduction
+    # ------------------------------------------------------------------
+    def block_scores_dev(self, q: torch.Tensor) -> torch.Tensor:
+        """Protection-masked block scores of one decode query over this layer's
+        heads ([nblocks] fp32 on the device): the scoring half of the selection
+        (reference _gpu_select :999-1003 before its topk).  The view is reused
+        by the next call."""
+        cfg = self.cfg
+        if q.ndim == 2:
+            q = q.unsqueeze(0)
+        assert q.shape[0] == 1 and tuple(q.shape[1:]) == (cfg.num_heads, cfg.head_dim)
+        q = _aligned(q)
+        nb = self.nblocks_filled
+        prot, nprot = self._protected_dev(nb)
+        if self._bscores is None:
+            self._bscores = torch.empty(self.max_blocks, dtype=torch.float32, device=self.device)
+        ws = self._select_ws(1)
+        call("nkv_select_scores", _stream(self.device), q.data_ptr(), q.stride(0), q.stride(1), cfg.num_heads,
+             cfg.num_kv_heads, cfg.head_dim, self.reps_gpu.data_ptr(), cfg.r, self.max_blocks, nb,
+             prot.data_ptr(), nprot, self._bscores.data_ptr(), ws.data_ptr(), ws.numel())
+        return self._bscores[:nb]
+
+    def decode_ranked(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                      scores: torch.Tensor) -> torch.Tensor:
+        """The rest of a decode step given the block scores of every KV head
+        (for example max-reduced over the devices that hold the other heads):
+        the attention kernel ranks `scores` itself, attends this layer's heads
+        to the top blocks, sink, recent window and the current token, and
+        appends the token to the recent window."""
+        cfg = self.cfg
+        assert q.shape[0] == 1 and k.shape[0] == 1
+        assert scores.dtype == torch.float32 and scores.numel() == self.nblocks_filled and scores.is_contiguous()
+        kk = self._budget(self._decode_requested)
+        d, out, head_new = self._decode_fill(q, k, v, kk)
+        a = d.attend
+        a.block_ids, a.n_sel, a.overlap_select = self._ids.data_ptr(), kk, 0
+        call("nkv_attend_ranked", _stream(self.device), C.byref(a), scores.data_ptr(), scores.numel(),
+             self._ids.data_ptr(), self._topk_scores.data_ptr())
+        self._ring_head = head_new
+        self.valid_len += 1
+        self._last_ids_dev, self._last_ids_host = self._ids_view, None
+        return out
+
 
     def decode(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                device: torch.device) -> torch.Tensor:
