@@ -332,7 +332,10 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    threads = os.cpu_count() or 1
+    try:  # the cores this process may run on (cgroup / affinity), not the machine's
+        threads = len(os.sched_getaffinity(0)) or 1
+    except AttributeError:
+        threads = os.cpu_count() or 1
 
     config = {"workload": "single-layer sparse decode (select+attend) @32K history, 36 layer states",
               "model": "Qwen3-4B attention geometry (32q/8kv, d128)", "context": CTX,
@@ -474,7 +477,8 @@ def main():
     if rank == 0 and not args.no_offload:
         offload = offload_measure(nkv, dev)
     if rank == 0:
-        cpu_us, n_cpu = cpu_reference(args.cpu_steps, 3, threads)
+        # the CPU baseline is timed at N = 1 only (with N > 1 other ranks share the host)
+        cpu_us, n_cpu = cpu_reference(args.cpu_steps, 3, threads) if world == 1 else (None, 0)
         line = {
             "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
@@ -488,9 +492,9 @@ def main():
                          "traffic": ATTEND_TRAFFIC,
                          "traffic_source": "ncu dram__bytes_read+write of one launch, "
                                            "profiles/decode_kernel_l4.md"},
-            "cpu_baseline": {"value": round(cpu_us, 1), "unit": UNIT, "cores": threads,
-                             "kind": "port",
-                             "sample": f"{n_cpu} decode calls of one 32K layer state (median)"},
+            "cpu_baseline": None if cpu_us is None else {
+                "value": round(cpu_us, 1), "unit": UNIT, "cores": threads, "kind": "port",
+                "sample": f"{n_cpu} decode calls of one 32K layer state (median)"},
             "e2e": {"value": round(e2e_value, 4), "unit": UNIT,
                     "h2d_bytes_per_step": L * (HQ + 2 * HKV) * D * 2,
                     "d2h_bytes_per_step": L * HQ * D * 2},
