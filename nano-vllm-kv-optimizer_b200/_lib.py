@@ -10,9 +10,12 @@ import os
 import threading
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-# NKV_LIB=checked selects the bounds-checked debug build (libnanokv_checked.so)
-LIB_PATH = os.path.join(HERE, "libnanokv_checked.so" if os.environ.get("NKV_LIB") == "checked"
-                        else "libnanokv.so")
+# NKV_LIB=checked selects the bounds-checked debug build (libnanokv_checked.so);
+# NKV_LIB=<path>.so loads another build of the same ABI (A/B comparisons)
+_env_lib = os.environ.get("NKV_LIB", "")
+LIB_PATH = (os.path.join(HERE, "libnanokv_checked.so") if _env_lib == "checked"
+            else os.path.abspath(_env_lib) if _env_lib.endswith(".so")
+            else os.path.join(HERE, "libnanokv.so"))
 
 NKV_OK = 0
 NKV_ERR_ARG = -1

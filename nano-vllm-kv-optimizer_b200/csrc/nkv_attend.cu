@@ -39,7 +39,10 @@ constexpr int AT_THREADS = 256;
 constexpr int AT_WARPS = AT_THREADS / 32;
 // single-query decode kernel: 16 warps hide the Q.K latency chains; G = 8 needs
 // the registers of a 256-thread launch
-template <int G> struct DK { static constexpr int THREADS = 256, WARPS = THREADS / 32; };
+#ifndef NKV_DECODE_WARPS
+#define NKV_DECODE_WARPS 8
+#endif
+template <int G> struct DK { static constexpr int WARPS = NKV_DECODE_WARPS, THREADS = WARPS * 32; };
 constexpr int AT_TPS_MAX = 256;  // keys per CTA (K+V tiles: 128 KiB)
 constexpr int AT_MIN_TPS = 16;
 constexpr int AT_CLUSTER_MAX = 16;        // splits of one head merged through DSMEM
@@ -1700,7 +1703,7 @@ static int attend_impl(nkv_stream_t stream, const nkv_attend_args* a, const Rank
   };
   finish(p);
   finish(pg);
-  const int dk_warps = 8;  // DK<G>::WARPS
+  const int dk_warps = NKV_DECODE_WARPS;  // DK<G>::WARPS
   // decode_kernel: 1 KiB alignment slack + K region (tile, then warp partials)
   // + V region (tile, then the CTA partial)
   auto decode_regions = [&](AttendParams& q) {
@@ -1737,7 +1740,7 @@ static int attend_impl(nkv_stream_t stream, const nkv_attend_args* a, const Rank
     attr[1].val.clusterDim.y = 1;
     attr[1].val.clusterDim.z = 1;
     lc.gridDim = dim3(q.splits, a->hkv);
-    lc.blockDim = dim3(AT_THREADS);
+    lc.blockDim = dim3(a->nq == 1 ? NKV_DECODE_WARPS * 32 : AT_THREADS);
     lc.dynamicSmemBytes = smem_of(q);
     lc.stream = st;
     lc.attrs = attr;
