@@ -9,20 +9,21 @@
 // the physical wrap (each padded to whole tiles), then the chunk.  Padding rows
 // are masked; every tile is one 64-row TMA box per 64-column half.
 //
-// CTA = 128 query rows (128 / G positions x G heads of one KV head), 320 threads:
-//   warp 0     TMA producer: Q once (3D map over [T][hq][D]), K and V of each
+// CTA = two query tiles of 128 rows (128 / G positions x G heads of one KV head
+// each) sharing every K/V tile, 320 threads:
+//   warp 0     TMA producer: Q of both tiles once (3D map over [T][hq][D]), K and V of each
 //              tile into a 3-stage ring (2D maps over the store, sink and ring,
 //              3D maps over the chunk), 128-byte swizzle.
-//   warp 1     owns 256 TMEM columns (S0 | S1 | O) and issues the MMAs from one
-//              thread: S_j = Q K_j^T (M 128, N 64, K 128; double-buffered S),
-//              then O += P_{j-1} V_{j-1} (M 128, N 128, K 64; V as an MN-major
-//              operand), tcgen05.commit to mbarriers.
-//   warps 2-9  two threads per query row (TMEM lane), 32 scores each: S from
-//              TMEM, mask, online softmax in the exp2 domain with lazy rescaling
-//              of O (only when the row max grows by more than 2^8; the pair
-//              shares the row max through shared memory), P as bf16 into a
-//              double-buffered swizzled shared tile (the A operand of the next
-//              MMA), and the epilogue O / l -> bf16.
+//   warp 1     owns all 512 TMEM columns (per query tile: two S buffers and O)
+//              and issues the MMAs from one thread: S_j = Q_t K_j^T for both
+//              tiles (M 128, N 64, K 128), then O_t += P_t,{j-1} V_{j-1}
+//              (M 128, N 128, K 64; V as an MN-major operand), tcgen05.commit
+//              to mbarriers.
+//   warps 2-5  query tile 0, warps 6-9 query tile 1, one row (TMEM lane) per
+//              thread: S from TMEM, mask, online softmax in the exp2 domain with
+//              lazy rescaling of O (only when the row max grows by more than
+//              2^8), P as bf16 into a double-buffered swizzled shared tile (the A
+//              operand of the next MMA), and the epilogue O / l -> bf16.
 // Every wait is bounded (error word + fall through); TMEM is freed by warp 1
 // after all warps meet at the end.
 #include <cuda.h>
@@ -32,15 +33,17 @@
 
 namespace nkv {
 
-constexpr int TC_THREADS = 320;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-9 softmax
-constexpr int TC_M = 128;
+constexpr int TC_THREADS = 320;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 / 6-9 softmax of query tile 0 / 1
+constexpr int TC_M = 128;        // rows per query tile
+constexpr int TC_QT = 2;         // query tiles per CTA (sharing every K/V tile)
 constexpr int TC_N = 64;
 constexpr int TC_STAGES = 3;
-constexpr uint32_t TC_TMEM_COLS = 256;  // S0 [0, 64) | S1 [64, 128) | O [128, 256)
-constexpr int TC_Q_BYTES = TC_M * 256;   // [2 halves][128 rows][128 B]
+// TMEM columns: tile t's S buffers at t*128 + {0, 64}, its O at 256 + t*128
+constexpr uint32_t TC_TMEM_COLS = 512;
+constexpr int TC_Q_BYTES = TC_M * 256;   // per query tile: [2 halves][128 rows][128 B]
 constexpr int TC_KV_BYTES = TC_N * 256;  // [2 halves][64 rows][128 B]
-constexpr int TC_P_BYTES = TC_M * 128;   // [128 rows][128 B]  (64 keys), two buffers
-constexpr size_t TC_SMEM = 1024 + TC_Q_BYTES + 2 * TC_STAGES * TC_KV_BYTES + 2 * TC_P_BYTES;
+constexpr int TC_P_BYTES = TC_M * 128;   // per query tile and buffer: [128 rows][128 B] (64 keys)
+constexpr size_t TC_SMEM = 1024 + TC_QT * TC_Q_BYTES + 2 * TC_STAGES * TC_KV_BYTES + TC_QT * 2 * TC_P_BYTES;
 
 struct TcMaps {
   CUtensorMap q, ck, cv;  // 3D: [T][heads][128]
@@ -213,22 +216,23 @@ __device__ __forceinline__ Tile tile_of(const TcParams& p, int h, int j, int len
 template <int G>
 __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParams p, const __grid_constant__ TcMaps tm) {
   extern __shared__ __align__(16) unsigned char sm_raw[];
-  __shared__ __align__(8) uint64_t q_full, kv_full[TC_STAGES], kv_empty[TC_STAGES], s_full[2], s_free[2], p_full,
-      o_done[2], fin;
+  // [query tile][buffer] where two buffers alternate by key tile
+  __shared__ __align__(8) uint64_t q_full, kv_full[TC_STAGES], kv_empty[TC_STAGES], s_full[TC_QT][2],
+      s_free[TC_QT][2], p_full[TC_QT], o_done[TC_QT][2], fin;
   __shared__ uint32_t s_tmem;
   __shared__ volatile int s_fail;
   unsigned char* sm = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);
-  unsigned char* qs = sm;
-  unsigned char* ks = qs + TC_Q_BYTES;
+  unsigned char* qs = sm;                                  // [tile] x TC_Q_BYTES
+  unsigned char* ks = qs + TC_QT * TC_Q_BYTES;
   unsigned char* vs = ks + TC_STAGES * TC_KV_BYTES;
-  unsigned char* ps = vs + TC_STAGES * TC_KV_BYTES;
-  constexpr int P = TC_M / G;
+  unsigned char* ps = vs + TC_STAGES * TC_KV_BYTES;        // [tile][buffer] x TC_P_BYTES
+  constexpr int P = TC_M / G;  // positions per query tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y;
-  const int p0 = ((int)gridDim.x - 1 - (int)blockIdx.x) * P;  // latest positions first
+  const int p0 = ((int)gridDim.x - 1 - (int)blockIdx.x) * (TC_QT * P);  // latest positions first
   const int off = p.n_cur - p.nq;
-  const int last_pos = min(p.nq, p0 + P) - 1;
+  const int last_pos = min(p.nq, p0 + TC_QT * P) - 1;
   const int lenA = min(p.ring_len, p.ring_cap - p.ring_start);
   const int nA = (lenA + TC_N - 1) / TC_N, nB = (p.ring_len - lenA + TC_N - 1) / TC_N;
   const int nhist = p.n_sel + (p.sink_len > 0 ? 1 : 0) + nA + nB;
@@ -242,13 +246,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParam
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&s_full[b], 1);
-      mbar_init(&s_free[b], 256);
+    for (int t = 0; t < TC_QT; ++t) {
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&s_full[t][b], 1);
+        mbar_init(&s_free[t][b], 128);
+        mbar_init(&o_done[t][b], 1);
+      }
+      mbar_init(&p_full[t], 128);
     }
-    mbar_init(&p_full, 256);
-    mbar_init(&o_done[0], 1);
-    mbar_init(&o_done[1], 1);
     mbar_init(&fin, 1);
     fence_mbar_init();
   }
@@ -266,9 +271,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParam
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      mbar_expect_tx(&q_full, TC_Q_BYTES);
-      tma3d(qs, &tm.q, 0, h * G, p0, &q_full);
-      tma3d(qs + TC_M * 128, &tm.q, 64, h * G, p0, &q_full);
+      mbar_expect_tx(&q_full, TC_QT * TC_Q_BYTES);
+      for (int t = 0; t < TC_QT; ++t) {
+        tma3d(qs + t * TC_Q_BYTES, &tm.q, 0, h * G, p0 + t * P, &q_full);
+        tma3d(qs + t * TC_Q_BYTES + TC_M * 128, &tm.q, 64, h * G, p0 + t * P, &q_full);
+      }
       for (int j = 0; j < ntiles; ++j) {
         const int st = j % TC_STAGES;
         if (j >= TC_STAGES) tc_wait(&kv_empty[st], ((j / TC_STAGES) - 1) & 1, p.err, &s_fail);
@@ -295,7 +302,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParam
         tc_drain(&kv_full[j % TC_STAGES], (j / TC_STAGES) & 1, p.err);
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+    // ---------------- MMA issuer: S of both query tiles, then their P.V ----------------
     if (lane == 0) {
       // f32 accumulate, bf16 A and B; S: K-major A and B, N 64; O: MN-major B (V), N 128; M 128
       constexpr uint32_t ID_S = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TC_N >> 3) << 17) |
@@ -307,29 +314,37 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParam
         if (j < ntiles) {
           const int st = j % TC_STAGES, sb = j & 1;
           tc_wait(&kv_full[st], (j / TC_STAGES) & 1, p.err, &s_fail);
-          if (j >= 2) tc_wait(&s_free[sb], ((j >> 1) - 1) & 1, p.err, &s_fail);
-          tc_fence_after();
           const unsigned char* kt = ks + st * TC_KV_BYTES;
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint64_t a = sdesc(qs + (k >> 2) * (TC_M * 128) + (k & 3) * 32, 16, 1024);
-            const uint64_t b = sdesc(kt + (k >> 2) * (TC_N * 128) + (k & 3) * 32, 16, 1024);
-            umma(tbase + sb * TC_N, a, b, ID_S, k > 0 ? 1u : 0u);
+          for (int t = 0; t < TC_QT; ++t) {
+            if (j >= 2) tc_wait(&s_free[t][sb], ((j >> 1) - 1) & 1, p.err, &s_fail);
+            tc_fence_after();
+            const unsigned char* qt = qs + t * TC_Q_BYTES;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const uint64_t a = sdesc(qt + (k >> 2) * (TC_M * 128) + (k & 3) * 32, 16, 1024);
+              const uint64_t b = sdesc(kt + (k >> 2) * (TC_N * 128) + (k & 3) * 32, 16, 1024);
+              umma(tbase + t * 128 + sb * TC_N, a, b, ID_S, k > 0 ? 1u : 0u);
+            }
+            umma_commit(&s_full[t][sb]);
           }
-          umma_commit(&s_full[sb]);
         }
         if (j >= 1) {
           const int jj = j - 1, st = jj % TC_STAGES;
-          tc_wait(&p_full, jj & 1, p.err, &s_fail);
-          tc_fence_after();
           const unsigned char* vt = vs + st * TC_KV_BYTES;
 #pragma unroll
-          for (int k = 0; k < TC_N / 16; ++k) {
-            const uint64_t a = sdesc(ps + (jj & 1) * TC_P_BYTES + k * 32, 16, 1024);
-            const uint64_t b = sdesc(vt + k * 16 * 128, TC_N * 128, 1024);
-            umma(tbase + 2 * TC_N, a, b, ID_O, (jj > 0 || k > 0) ? 1u : 0u);
+          for (int t = 0; t < TC_QT; ++t) {
+            tc_wait(&p_full[t], jj & 1, p.err, &s_fail);
+            tc_fence_after();
+            const unsigned char* pt = ps + (t * 2 + (jj & 1)) * TC_P_BYTES;
+#pragma unroll
+            for (int k = 0; k < TC_N / 16; ++k) {
+              const uint64_t a = sdesc(pt + k * 32, 16, 1024);
+              const uint64_t b = sdesc(vt + k * 16 * 128, TC_N * 128, 1024);
+              umma(tbase + 256 + t * 128, a, b, ID_O, (jj > 0 || k > 0) ? 1u : 0u);
+            }
+            umma_commit(&o_done[t][jj & 1]);
           }
-          umma_commit(&o_done[jj & 1]);
           umma_commit(&kv_empty[st]);
         }
       }
@@ -340,64 +355,64 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParam
     __syncwarp();
   } else {
     // ---------------- softmax / correction / epilogue ----------------
-    // two warps per TMEM lane quadrant: warp 2 + q (half 0) and warp 6 + q
-    // (half 1) share rows q*32..q*32+31; a thread owns 32 of its row's 64
-    // scores and 64 of its 128 output columns; the pair exchanges row maxima
-    // through shared memory and a 64-thread named barrier (id 1 + quadrant)
-    __shared__ float s_pmax[2][2][TC_M];
-    const int q4 = warp & 3, half = (warp - 2) >> 2;
+    // warps 2-5 own query tile 0, warps 6-9 tile 1; one row (TMEM lane) per thread
+    const int t = (warp - 2) >> 2;
+    const int q4 = warp & 3;
     const int row = q4 * 32 + lane;
-    const uint32_t bar_id = 1 + q4;
     const uint32_t trow = tbase + ((uint32_t)(q4 * 32) << 16);
-    const int pos = p0 + row / G, g = row % G;
+    const uint32_t s_col = t * 128, o_col = 256 + t * 128;
+    const int tp0 = p0 + t * P;  // first position of this query tile
+    const int pos = tp0 + row / G, g = row % G;
     float m_ref = -INFINITY, l = 0.f;
     for (int j = 0; j < ntiles; ++j) {
       const int sb = j & 1;
-      tc_wait(&s_full[sb], (j >> 1) & 1, p.err, &s_fail);
+      tc_wait(&s_full[t][sb], (j >> 1) & 1, p.err, &s_fail);
       tc_fence_after();
-      uint32_t sr[32];
-      tmem_ld32(trow + sb * TC_N + half * 32, sr);
+      uint32_t sr[64];
+      {
+        uint32_t (&lo)[32] = *reinterpret_cast<uint32_t(*)[32]>(sr);
+        uint32_t (&hi)[32] = *reinterpret_cast<uint32_t(*)[32]>(sr + 32);
+        tmem_ld32(trow + s_col + sb * TC_N, lo);
+        tmem_ld32(trow + s_col + sb * TC_N + 32, hi);
+      }
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(&s_free[sb]);
-      const Tile t = tile_of(p, 0, j, lenA, nA, nB, false);  // only src / valid / chunk base are used
+      mbar_arrive(&s_free[t][sb]);
+      const Tile ti = tile_of(p, 0, j, lenA, nA, nB, false);  // only src / valid / chunk base are used
       // masking only where a tile has padding rows or chunk keys past the
-      // first row's position; the scale is applied inside the exponent
-      const bool need_mask = t.src == 3 ? (t.y + TC_N - 1 > p0 + off) : (t.valid < TC_N);
-      float mxr = -INFINITY;
+      // tile's first position; the scale is applied inside the exponent
+      const bool need_mask = ti.src == 3 ? (ti.y + TC_N - 1 > tp0 + off) : (ti.valid < TC_N);
       if (need_mask) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int kc = half * 32 + c;
-          const bool vis = t.src == 3 ? (t.y + kc <= pos + off) : (kc < t.valid);
+        for (int c = 0; c < 64; ++c) {
+          const bool vis = ti.src == 3 ? (ti.y + c <= pos + off) : (c < ti.valid);
           if (!vis) sr[c] = __float_as_uint(-INFINITY);
-          mxr = fmaxf(mxr, __uint_as_float(sr[c]));
         }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 32; ++c) mxr = fmaxf(mxr, __uint_as_float(sr[c]));
       }
-      s_pmax[j & 1][half][row] = mxr;
-      asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
-      mxr = fmaxf(mxr, s_pmax[j & 1][half ^ 1][row]);
+      // row max over 8 independent partial maxima (no 64-long dependency chain)
+      float mp[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) mp[u] = __uint_as_float(sr[u]);
+#pragma unroll
+      for (int c = 8; c < 64; ++c) mp[c & 7] = fmaxf(mp[c & 7], __uint_as_float(sr[c]));
+      const float mxr = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
       const float m_new = fmaxf(m_ref, mxr * p.sl2);
       const bool rescale = m_new > m_ref + 8.f;
       // P buffer j % 2 is free once PV_{j-2} is done; O is current once PV_{j-1} is
-      if (j >= 2) tc_wait(&o_done[j & 1], ((j - 2) >> 1) & 1, p.err, &s_fail);
+      if (j >= 2) tc_wait(&o_done[t][j & 1], ((j - 2) >> 1) & 1, p.err, &s_fail);
       if (rescale) {
         if (m_ref != -INFINITY) {  // O and l hold partial sums at the old reference: rescale
-          tc_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.err, &s_fail);
+          tc_wait(&o_done[t][(j - 1) & 1], ((j - 1) >> 1) & 1, p.err, &s_fail);
           const float alpha = exp2f(m_ref - m_new);
           tc_fence_after();
 #pragma unroll
-          for (int cc = 0; cc < 2; ++cc) {
+          for (int cc = 0; cc < 4; ++cc) {
             uint32_t o[32];
-            const uint32_t ta = trow + 2 * TC_N + half * 64 + cc * 32;
-            tmem_ld32(ta, o);
+            tmem_ld32(trow + o_col + cc * 32, o);
             tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st32(ta, o);
+            tmem_st32(trow + o_col + cc * 32, o);
           }
           tmem_wait_st();
           l *= alpha;
@@ -405,36 +420,35 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParam
         m_ref = m_new;
       }
       const float nbase = m_ref == -INFINITY ? 0.f : -m_ref;
-      uint32_t pw[16];
+      uint32_t pw[32];
+      float lp[4] = {0.f, 0.f, 0.f, 0.f};  // partial row sums (independent chains)
 #pragma unroll
-      for (int c = 0; c < 32; c += 2) {
+      for (int c = 0; c < 64; c += 2) {
         const float a = exp2f(fmaf(__uint_as_float(sr[c]), p.sl2, nbase));
         const float b = exp2f(fmaf(__uint_as_float(sr[c + 1]), p.sl2, nbase));
-        l += a + b;
+        lp[(c >> 1) & 3] += a + b;
         const __nv_bfloat162 hb = __floats2bfloat162_rn(a, b);
         pw[c / 2] = *reinterpret_cast<const uint32_t*>(&hb);
       }
-      unsigned char* prow = ps + (j & 1) * TC_P_BYTES + row * 128;
+      l += (lp[0] + lp[1]) + (lp[2] + lp[3]);
+      unsigned char* prow = ps + (t * 2 + (j & 1)) * TC_P_BYTES + row * 128;
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch)
-        *reinterpret_cast<uint4*>(prow + (((half * 4 + ch) ^ (row & 7)) << 4)) =
+      for (int ch = 0; ch < 8; ++ch)
+        *reinterpret_cast<uint4*>(prow + ((ch ^ (row & 7)) << 4)) =
             make_uint4(pw[ch * 4], pw[ch * 4 + 1], pw[ch * 4 + 2], pw[ch * 4 + 3]);
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&p_full);
+      mbar_arrive(&p_full[t]);
     }
-    // epilogue: O / l -> bf16 (row sums of the pair added through shared memory)
-    s_pmax[0][half][row] = l;
-    asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
-    l += s_pmax[0][half ^ 1][row];
-    if (ntiles > 0) tc_wait(&o_done[(ntiles - 1) & 1], ((ntiles - 1) >> 1) & 1, p.err, &s_fail);
+    // epilogue: O / l -> bf16
+    if (ntiles > 0) tc_wait(&o_done[t][(ntiles - 1) & 1], ((ntiles - 1) >> 1) & 1, p.err, &s_fail);
     tc_fence_after();
     const float inv = 1.f / l;
-    __nv_bfloat16* dst = p.out + (long long)pos * p.out_row + (long long)(h * G + g) * p.out_head + half * 64;
+    __nv_bfloat16* dst = p.out + (long long)pos * p.out_row + (long long)(h * G + g) * p.out_head;
 #pragma unroll
-    for (int cc = 0; cc < 2; ++cc) {
+    for (int cc = 0; cc < 4; ++cc) {
       uint32_t o[32];
-      tmem_ld32(trow + 2 * TC_N + half * 64 + cc * 32, o);
+      tmem_ld32(trow + o_col + cc * 32, o);
       tmem_wait_ld();
       if (pos < p.nq) {
 #pragma unroll
@@ -552,7 +566,7 @@ int prefill_tc(cudaStream_t st, const nkv_attend_args* a) {
   p.out_row = a->out_row_stride;
   p.out_head = a->out_head_stride;
   p.err = (int*)a->workspace;
-  const int P = TC_M / G;
+  const int P = TC_QT * TC_M / G;  // positions per CTA
   dim3 grid((a->nq + P - 1) / P, a->hkv);
   switch (G) {
 #define NKV_TC_CASE(GG)                                                                \
