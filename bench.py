@@ -152,8 +152,9 @@ SH_CTX, SH_LAYERS = 131072, 4
 def sharded_measure(nkv, dev, world, steps=20):
     """Decode step with the KV heads split over the ranks (KVHeadShardedLayer):
     per layer, scoring of the rank's heads, MAX all-reduce of the block scores,
-    attention of the rank's heads, all-gather of the outputs.  Eager (NCCL
-    calls between the kernels); device time between events, max over ranks."""
+    attention of the rank's heads, all-gather of the outputs, replayed from a
+    CUDA graph that holds the NCCL calls (eager if capture is refused);
+    device time between events, max over ranks."""
     import torch.distributed as dist
     g = torch.Generator(device=dev).manual_seed(5150)
     layers = []
@@ -175,21 +176,44 @@ def sharded_measure(nkv, dev, world, steps=20):
     def step():
         for li, lay in enumerate(layers):
             lay.decode(q[li], k[li], v[li])
-    for _ in range(3):
-        step()
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            step()
     torch.cuda.synchronize()
     dist.barrier()
+    # the whole sharded step (kernels and NCCL calls) captured in one CUDA graph;
+    # eager replay is the fallback when capture is refused
+    graph, mode = None, "eager"
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        mode = "cuda graph"
+    except Exception:  # noqa: BLE001 - measured eagerly instead
+        graph = None
+        torch.cuda.synchronize()
+    # every rank replays the same way (the collectives must match)
+    ok = torch.tensor([0 if graph is None else 1], device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if int(ok.item()) == 0:
+        graph, mode = None, "eager"
+    dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        step()
-    e1.record()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            graph.replay() if graph is not None else step()
+        e0.record(stream)
+        for _ in range(steps):
+            graph.replay() if graph is not None else step()
+        e1.record(stream)
     e1.synchronize()
     t = torch.tensor([e0.elapsed_time(e1) * 1000.0 / (steps * SH_LAYERS)], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    del layers
+    del graph, layers
+    torch.cuda.synchronize()
     return {"workload": f"decode step @128K, KV heads sharded {world} ways (NCCL MAX all-reduce of block "
-                        "scores + all-gather of outputs per layer), 4 layer states, eager",
+                        f"scores + all-gather of outputs per layer), 4 layer states, {mode}",
             "us_per_layer": round(float(t.item()), 2), "kv_heads_per_gpu": HKV // world}
 
 

@@ -69,7 +69,8 @@ extern "C" int nkv_decode_step(nkv_stream_t stream, const nkv_decode_args* a) {
     nkv_attend_args b = t;
     b.block_ids = a->out_ids;
     b.n_sel = a->k;
-    b.overlap_select = 1;
+    const char* pdl = getenv("NKV_PDL");  // NKV_PDL=0: plain stream order (measurement)
+    b.overlap_select = (pdl && atoi(pdl) == 0) ? 0 : 1;
     return nkv::attend_ranked(stream, &b, scores, a->nblocks, a->out_ids, a->out_topk_scores);
   }
   int rc = nkv_select(stream, t.q, 1, t.q_row_stride, t.q_head_stride, t.hq, t.hkv, t.head_dim, a->reps, a->r,

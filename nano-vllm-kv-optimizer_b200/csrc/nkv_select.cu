@@ -13,6 +13,8 @@
 //             enter the list are skipped, then a 3-level merge tree.
 //   k > 32  : bitonic sort of all keys in shared memory.
 // Keys order by (score desc, id asc), so the result is deterministic.
+#include <stdlib.h>
+
 #include "nkv_common.cuh"
 #include "nkv_host.h"
 
@@ -380,6 +382,10 @@ static int launch_select(cudaStream_t st, SelectParams& p, int G) {
   int bpc = (p.nblocks + 4 * sms - 1) / (4 * sms);
   const int unit_bpc = SEL_WARPS / (p.hkv < SEL_WARPS ? p.hkv : SEL_WARPS);
   if (bpc < unit_bpc) bpc = unit_bpc;
+  {  // NKV_SEL_BPC: blocks per scoring CTA (tuning override)
+    const char* e = getenv("NKV_SEL_BPC");
+    if (e && atoi(e) > 0) bpc = atoi(e);
+  }
   p.bpc = bpc;
   const int grid = (p.nblocks + bpc - 1) / bpc;
   int npow2 = 1;
