@@ -174,9 +174,18 @@ int nkv_attend_static(nkv_stream_t stream, const nkv_attend_args* args);
 /* One decode step of a layer: nkv_select over the layer's representatives
  * for the single query, then nkv_attend of that query over the selected
  * blocks, sink, recent ring and the current token (which it appends to the
- * ring at attend.ring_write_pos), with the attention overlapping the
- * selection (programmatic dependent launch).  attend.block_ids / n_sel are
- * replaced by out_ids / k, attend.overlap_select is implied.
+ * ring at attend.ring_write_pos).  attend.block_ids / n_sel are replaced by
+ * out_ids / k, attend.overlap_select is ignored.
+ * The step is a scoring grid followed by the attention grid ranking the
+ * scores in each CTA (programmatic dependent launch overlaps the two).  With
+ * the environment variable NKV_DECODE_ONE=1, and where it applies (k <= 32,
+ * r in {1, 2, 4}, nblocks <= 2048, one thread-block cluster per KV head that
+ * the device holds all at once), it is ONE cooperative launch instead: every
+ * CTA scores a share of the blocks for all heads on the tensor cores,
+ * publishes the masked block scores as keys tagged with a per-launch epoch in
+ * the select workspace, and selects the top k from all published keys itself
+ * (nkv_select's order; scores equal to fp32 rounding).  The select workspace
+ * must start at zero and is used by one stream at a time.
  * Replaces the device work of M12LayerRuntime.decode (m12_runtime.py:1141-1346:
  * recent shift and append :1166-1172, select :1193-1198, gather and pack
  * :1213-1309, attention :1316-1320) in one host call. */
@@ -192,6 +201,10 @@ typedef struct {
   size_t select_workspace_bytes;
 } nkv_decode_args;
 int nkv_decode_step(nkv_stream_t stream, const nkv_decode_args* args);
+/* How the calling thread's last nkv_decode_step ran: 1 one launch, 2 a
+ * scoring grid + ranked attention, 3 nkv_select + nkv_attend, 0 none yet.
+ * (Introspection for tests and benchmarks; no counterpart in the reference.) */
+int nkv_decode_last_form(void);
 
 /* The two halves of nkv_decode_step, for a caller that combines block scores
  * across devices between them (KV heads sharded over GPUs: each rank scores

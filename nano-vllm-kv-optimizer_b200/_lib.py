@@ -96,6 +96,7 @@ SIGNATURES = {
     "nkv_attend_last_config": (c_int, [C.POINTER(c_int), C.POINTER(c_int), C.POINTER(c_int)]),
     "nkv_attend_static": (c_int, [c_vp, C.POINTER(AttendArgs)]),
     "nkv_decode_step": (c_int, [c_vp, C.POINTER(DecodeArgs)]),
+    "nkv_decode_last_form": (c_int, []),
     "nkv_select_scores": (c_int, [c_vp, c_vp, c_i64, c_i64, c_int, c_int, c_int, c_vp, c_int, c_int, c_int,
                                   c_vp, c_int, c_vp, c_vp, C.c_size_t]),
     "nkv_attend_ranked": (c_int, [c_vp, C.POINTER(AttendArgs), c_vp, c_int, c_vp, c_vp]),

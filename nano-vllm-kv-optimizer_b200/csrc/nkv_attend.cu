@@ -98,6 +98,17 @@ struct AttendParams {
   int rank_n;
   long long* rank_out;     // the ranked ids, written by CTA (0, 0)
   float* rank_out_scores;  // their scores (optional)
+  // decode kernel, one-launch step (fs_keys set, rank_scores null): the CTAs
+  // also score the blocks (CTA c of the grid owns blocks [c * fs_bpc, ...) for
+  // every KV head), publish each block's masked score as a key tagged with
+  // this launch's epoch, and select the top n_sel of the rank_n keys
+  // themselves once every key carries the tag
+  const __nv_bfloat16* fs_reps;  // [hkv][fs_reps_blocks][fs_r][D]
+  int fs_r, fs_reps_blocks, fs_bpc, fs_nprot;
+  int fs_prefetch;  // 1: each CTA starts an L2 prefetch of its representatives at launch
+  const int* fs_prot;
+  unsigned long long* fs_keys;  // [rank_n]: (tag << 32) | orderable score
+  unsigned* fs_sync;            // [0] epoch, [1] CTAs done with this launch's keys
 };
 
 // 2D tensor maps of the decode kernel over [rows][128] bf16 sources with
@@ -749,6 +760,279 @@ __device__ void rank_top32(const float* __restrict__ scores, int n, u64* lists) 
 }
 constexpr int RANK_MAXC = 8;  // ranked decode: nblocks <= 8 warps x 32 x 8 = 2048
 
+// ---------------------------------------------------------------------------
+// One-launch decode step: scoring and selection inside the attention grid.
+// ---------------------------------------------------------------------------
+constexpr int FS_BPC_MAX = 64;  // blocks one CTA scores (for every KV head)
+constexpr int FS_MAXE = 8;      // keys per thread in the selection (nblocks <= 8 x threads)
+
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* a, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* a) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned* a) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+  return v;
+}
+// Bulk prefetch of `bytes` (a multiple of 16, 16-byte aligned) into L2, no completion tracking.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+// Tag of a launch's keys: never 0, so a zeroed key array holds no valid key.
+__device__ __forceinline__ uint32_t fs_tag(uint32_t epoch) { return epoch % 0xfffffffeu + 1u; }
+
+// Scores of this CTA's blocks on the tensor cores: warp w scores KV heads
+// w, w + NW, ...; for one head the CTA's representative rows (nb blocks x r,
+// contiguous in [hkv][reps_blocks][r][D]) are the N columns and the head's G
+// query rows the M rows (rows >= G zero) of mma.sync m16n8k16, K = D.  The K
+// order inside the MMA is a permutation of the head dims, the same for both
+// operands: at k-steps 2i and 2i + 1 lane quad t holds dims 32i + 8t ... + 7
+// (one 16-byte load per operand row), so the products are the full dot
+// products.  Per representative row the max over query rows (xor 4, 8, 16),
+// then over the r rows of a block (r in {1, 2, 4}: the rows of a block sit in
+// adjacent lanes), kept per (warp, block) in shared memory (orderable bits,
+// no atomics); the block score is the max over the warps' entries, and
+// protected blocks publish -inf.  Scores are fp32 sums of exact bf16
+// products, in the tensor core's summation order.
+template <int G, int NW>
+__device__ void fs_score_publish(const AttendParams& p, int cta, uint32_t tag, unsigned (*s_part)[FS_BPC_MAX],
+                                 [[maybe_unused]] int* trc) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int b0 = cta * p.fs_bpc, nb = min(p.fs_bpc, p.rank_n - b0);
+  if (nb <= 0) return;  // CTA-uniform
+  const int g = lane >> 2, t = lane & 3;
+  const int rows = nb * p.fs_r;
+  for (int hh = warp; hh < p.hkv; hh += NW) {
+    uint4 qf[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      qf[i] = g < G ? __ldg(reinterpret_cast<const uint4*>(p.q + (long long)(hh * G + g) * p.q_head + i * 32 + t * 8))
+                    : make_uint4(0u, 0u, 0u, 0u);
+    const __nv_bfloat16* rbase = p.fs_reps + ((long long)hh * p.fs_reps_blocks + b0) * p.fs_r * NKV_D;
+    for (int row0 = 0; row0 < rows; row0 += 32) {
+      uint4 rf[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int rr = row0 + j * 8 + g;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          rf[j][i] = rr < rows ? __ldg(reinterpret_cast<const uint4*>(rbase + (long long)rr * NKV_D + i * 32 + t * 8))
+                               : make_uint4(0u, 0u, 0u, 0u);
+      }
+      float c[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) mma_bf16(c[j], qf[i].x, 0u, qf[i].y, 0u, rf[j][i].x, rf[j][i].y);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) mma_bf16(c[j], qf[i].z, 0u, qf[i].w, 0u, rf[j][i].z, rf[j][i].w);
+      }
+      if (row0 == 0) NKV_STAMP(trc, 45);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        // c[j][0..1]: query row g x representative rows row0 + 8j + 2t, + 1
+        float v0 = g < G ? c[j][0] : -INFINITY, v1 = g < G ? c[j][1] : -INFINITY;
+#pragma unroll
+        for (int x = 4; x < 32; x <<= 1) {
+          v0 = fmaxf(v0, __shfl_xor_sync(FULL, v0, x));
+          v1 = fmaxf(v1, __shfl_xor_sync(FULL, v1, x));
+        }
+        const int rr = row0 + j * 8 + 2 * t;
+        if (p.fs_r == 1) {
+          if (g == 0 && rr < rows) s_part[warp][rr] = max(s_part[warp][rr], f32_order(v0));
+          if (g == 0 && rr + 1 < rows) s_part[warp][rr + 1] = max(s_part[warp][rr + 1], f32_order(v1));
+        } else {
+          float m = fmaxf(v0, v1);  // rows rr, rr + 1: one block
+          if (p.fs_r == 4) m = fmaxf(m, __shfl_xor_sync(FULL, m, 1));
+          if (g == 0 && rr < rows && (rr % p.fs_r) == 0) {
+            const int bl = rr / p.fs_r;
+            s_part[warp][bl] = max(s_part[warp][bl], f32_order(m));
+          }
+        }
+      }
+    }
+  }
+  NKV_STAMP(trc, 44);
+  __syncthreads();
+  if (tid < nb) {
+    const int b = b0 + tid;
+    uint32_t u = 0u;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) u = max(u, s_part[w][tid]);
+    for (int i = 0; i < p.fs_nprot; ++i)
+      if (__ldg(p.fs_prot + i) == b) u = f32_order(-INFINITY);
+    st_relaxed_u64(p.fs_keys + b, ((unsigned long long)tag << 32) | u);
+  }
+}
+
+constexpr int FS_CAND_MAX = 256;  // candidates ranked by counting (more: extraction rounds)
+
+// Top n_sel of the rank_n published keys, in rank order (score descending,
+// then block id ascending: nkv_select's order), into s_sel as make_key keys.
+// Thread t holds keys t, t + NT, ...: it polls them until they carry `tag`
+// (bounded: ~0.2 s of SM clock, then ERR_WAIT_TIMEOUT).
+//  1. threshold: every warp finds its 4th largest distinct score (4 warp max
+//     reductions); theta = the smallest over the warps, so at least 4 x NW
+//     keys score >= theta and the top n_sel (<= 32) are among them (theta = 0,
+//     every key, when fewer than n_sel keys can be guaranteed that way);
+//  2. the keys >= theta are compacted into shared memory (warp ballots);
+//  3. each candidate's rank = the number of larger candidate keys; ranks below
+//     n_sel land in s_sel[rank].
+// With more than FS_CAND_MAX candidates (flat or tied scores) the top n_sel
+// are extracted one per round (block-wide max of the remaining keys) instead.
+// All threads of the CTA must call.
+template <int NW>
+__device__ void fs_select(const AttendParams& p, uint32_t tag, u64* s_sel, u64* s_cand, unsigned* s_misc,
+                          [[maybe_unused]] int* trc) {
+  constexpr int NT = NW * 32;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n = p.rank_n, k = p.n_sel;
+  const int E = (n + NT - 1) / NT;
+  uint32_t u[FS_MAXE];
+  unsigned live = 0;
+#pragma unroll
+  for (int e = 0; e < FS_MAXE; ++e) {
+    u[e] = 0u;
+    if (e < E && tid + e * NT < n) live |= 1u << e;
+  }
+  unsigned pending = live;
+  const long long t_start = clock64();
+  while (pending) {
+#pragma unroll
+    for (int e = 0; e < FS_MAXE; ++e) {
+      if ((pending >> e) & 1u) {
+        const unsigned long long v = ld_relaxed_u64(p.fs_keys + tid + e * NT);
+        if ((uint32_t)(v >> 32) == tag) {
+          u[e] = (uint32_t)v;
+          pending &= ~(1u << e);
+        }
+      }
+    }
+    if (pending && clock64() - t_start > 400000000ll) {
+      if (p.err) atomicExch(p.err, ERR_WAIT_TIMEOUT);
+      break;
+    }
+  }
+  NKV_STAMP(trc, 40);
+  // 1. per-warp 4th largest distinct score
+  uint32_t prev = 0xffffffffu, th = 0u;
+  bool more = true;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    uint32_t m = 0u;
+    bool any = false;
+#pragma unroll
+    for (int e = 0; e < FS_MAXE; ++e)
+      if (((live >> e) & 1u) && (r == 0 || u[e] < prev)) {
+        m = max(m, u[e]);
+        any = true;
+      }
+    more = __any_sync(FULL, any) && more;
+    m = __reduce_max_sync(FULL, m);
+    prev = m;
+    th = m;
+  }
+  const bool warp_live = __any_sync(FULL, live != 0u);
+  if (lane == 0) s_misc[warp] = !warp_live ? 0xffffffffu : more ? th : 0u;
+  __syncthreads();
+  NKV_STAMP(trc, 36);
+  uint32_t theta = 0xffffffffu;
+  int nlive = 0;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) {
+    theta = min(theta, s_misc[w]);
+    nlive += s_misc[w] != 0xffffffffu ? 1 : 0;
+  }
+  if (nlive * 4 < k) theta = 0u;
+  // 2. candidates: per-warp counts, then each warp writes at its prefix
+  unsigned cmask = 0u, wcount = 0u;
+#pragma unroll
+  for (int e = 0; e < FS_MAXE; ++e) {
+    if (e >= E) break;  // CTA-uniform
+    const bool cand = ((live >> e) & 1u) && u[e] >= theta;
+    cmask |= cand ? 1u << e : 0u;
+    wcount += (unsigned)__popc(__ballot_sync(FULL, cand));
+  }
+  if (lane == 0) s_misc[NW + warp] = wcount;
+  __syncthreads();
+  unsigned off = 0u, C = 0u;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) {
+    const unsigned c = s_misc[NW + w];
+    off += w < warp ? c : 0u;
+    C += c;
+  }
+#pragma unroll
+  for (int e = 0; e < FS_MAXE; ++e) {
+    if (e >= E) break;  // CTA-uniform
+    const bool cand = (cmask >> e) & 1u;
+    const unsigned bal = __ballot_sync(FULL, cand);
+    const unsigned at = off + __popc(bal & ((1u << lane) - 1u));
+    if (cand && at < FS_CAND_MAX) s_cand[at] = ((u64)u[e] << 32) | (u64)(0xffffffffu - (uint32_t)(tid + e * NT));
+    off += __popc(bal);
+  }
+  __syncthreads();
+  NKV_STAMP(trc, 37);
+#ifdef NKV_CHECKED
+  if (trc && tid == 0) trc[39] = (int)C;
+#endif
+  if (C <= FS_CAND_MAX) {
+    // 3. rank by counting: 4 adjacent lanes per candidate, each over a quarter
+    for (unsigned base = 0; base < C; base += NT / 4) {
+      const unsigned c = base + (unsigned)(tid >> 2);
+      const u64 key = c < C ? s_cand[c] : ~0ull;
+      unsigned rank = 0u;
+      for (unsigned d = (unsigned)(tid & 3); d < C; d += 4) rank += s_cand[d] > key ? 1u : 0u;
+      rank += __shfl_xor_sync(FULL, rank, 1);
+      rank += __shfl_xor_sync(FULL, rank, 2);
+      if (c < C && (tid & 3) == 0 && rank < (unsigned)k) s_sel[rank] = key;
+    }
+  } else {
+    // flat scores: k extraction rounds, each a block-wide max of the remaining keys
+    u64 mine[FS_MAXE];
+#pragma unroll
+    for (int e = 0; e < FS_MAXE; ++e)
+      mine[e] = ((live >> e) & 1u) ? ((u64)u[e] << 32) | (u64)(0xffffffffu - (uint32_t)(tid + e * NT)) : 0ull;
+    u64* s_red = s_cand;  // NW partial maxima
+    for (int r = 0; r < k; ++r) {
+      u64 best = 0ull;
+#pragma unroll
+      for (int e = 0; e < FS_MAXE; ++e) best = umax64(best, mine[e]);
+#pragma unroll
+      for (int x = 1; x < 32; x <<= 1) best = umax64(best, shfl_xor64(best, x));
+      __syncthreads();  // the previous round's reads of s_red are done
+      if (lane == 0) s_red[warp] = best;
+      __syncthreads();
+      u64 top = 0ull;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) top = umax64(top, s_red[w]);
+      if (tid == 0) s_sel[r] = top;
+#pragma unroll
+      for (int e = 0; e < FS_MAXE; ++e)
+        if (mine[e] == top) mine[e] = 0ull;
+    }
+  }
+  NKV_STAMP(trc, 41);
+  __syncthreads();
+}
+
+// The launch is done with its keys once every CTA has arrived here: the last
+// CTA resets the arrival count and advances the epoch (read by the next launch).
+__device__ __forceinline__ void fs_arrive(const AttendParams& p) {
+  const unsigned total = gridDim.x * gridDim.y;
+  if (atomicAdd(p.fs_sync + 1, 1u) == total - 1u) {
+    p.fs_sync[1] = 0u;
+    atomicAdd(p.fs_sync, 1u);
+  }
+}
+
 // Rows [pos0, pos0 + len) of the logical keys, loaded by the threads of the
 // CTA into tile rows row0... : 16-byte copies for bf16 sources (the current
 // tokens, a host-resident store, any segment TMA cannot address), in-register
@@ -854,7 +1138,7 @@ __device__ void thread_rows(const AttendParams& p, int h, int pos0, int len, int
 //  merge:  warp partials through shared memory (over the K tile, after every
 //          warp is done with it), then the splits of a head through the
 //          cluster (DSMEM) or the workspace.
-template <int G>
+template <int G, bool FS = false>
 __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendParams p,
                                                                const __grid_constant__ DecodeMaps tm) {
   extern __shared__ __align__(16) unsigned char sm_raw[];
@@ -865,6 +1149,12 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
   __shared__ long long s_ids[AT_MAX_SLOTS];
   __shared__ short srow[AT_TPS_MAX_CLUSTER];
   constexpr int NW = DK<G>::WARPS;
+  // one-launch step: per-block score maxima, the selected keys, the radix
+  // histogram and the scan's warp sums
+  __shared__ unsigned s_part[NW][FS_BPC_MAX];
+  __shared__ u64 s_sel[32];
+  __shared__ u64 s_cand[FS_CAND_MAX];
+  __shared__ unsigned s_misc[2 * NW];
 
   const int split = blockIdx.x, h = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -884,6 +1174,17 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
   [[maybe_unused]] int* trc = nullptr;
 #endif
   NKV_STAMP(trc, 48);
+  // one-launch step: this launch's tag (the epoch load overlaps the prologue)
+  uint32_t fs_tg = 0u;
+  if constexpr (FS) {
+    fs_tg = fs_tag(ld_relaxed_u32(p.fs_sync));
+    for (int i = tid; i < NW * FS_BPC_MAX; i += NW * 32) s_part[i / FS_BPC_MAX][i % FS_BPC_MAX] = 0u;
+    // the representatives this CTA scores, one contiguous range per KV head
+    const int b0 = (h * gridDim.x + split) * p.fs_bpc, nb = min(p.fs_bpc, p.rank_n - b0);
+    if (p.fs_prefetch && tid < p.hkv && nb > 0)
+      prefetch_l2_bulk(p.fs_reps + ((long long)tid * p.fs_reps_blocks + b0) * p.fs_r * NKV_D,
+                       (uint32_t)(nb * p.fs_r * NKV_D * 2));
+  }
 
   // ---- pieces ------------------------------------------------------------------------
   // Fixed table: pieces [0, nslots) are the selected blocks the range touches,
@@ -945,7 +1246,7 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
   }
   // block ids: read now unless they come from the grid this one overlaps
   long long id_early = 0;
-  if (!p.overlap && !p.rank_scores && tid < nslots) id_early = __ldg(p.ids + slot0 + tid);
+  if (!FS && !p.overlap && !p.rank_scores && tid < nslots) id_early = __ldg(p.ids + slot0 + tid);
   if (warp < 2) {  // np <= AT_MAX_SLOTS + 4 pieces live in warps 0 and 1
     const unsigned bits = __ballot_sync(FULL, by_threads);
     if (lane == 0) s_thr[warp] = bits;
@@ -1002,7 +1303,24 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
   }
   NKV_STAMP(trc, 62);
   if (p.overlap) pdl_wait();  // block ids (or scores) are complete past this point
-  if (p.rank_scores) {
+  if constexpr (FS) {
+    // one-launch step: score this CTA's blocks, then (CTAs that hold selected
+    // blocks, and CTA (0, 0), which publishes the ids) select from every
+    // CTA's published keys; slots take the selected blocks in rank order
+    fs_score_publish<G, NW>(p, h * gridDim.x + split, fs_tg, s_part, trc);
+    NKV_STAMP(trc, 46);
+    if (nslots > 0 || (split == 0 && h == 0)) {
+      fs_select<NW>(p, fs_tg, s_sel, s_cand, s_misc, trc);
+      NKV_STAMP(trc, 47);
+      if (tid < nslots) {
+        const long long id = (long long)key_id(s_sel[slot0 + tid]);
+        const bool bad = id >= p.rank_n;  // only after a timed-out wait
+        if (bad && p.err) atomicExch(p.err, ERR_BAD_INDEX);
+        s_ids[tid] = bad ? -1 : id;
+      }
+    }
+    if (tid == 0) fs_arrive(p);
+  } else if (p.rank_scores) {
     // ranked mode: the CTAs that hold selected blocks (and CTA (0, 0), which
     // publishes the ids) rank the block scores themselves
     if (nslots > 0 || (split == 0 && h == 0)) {
@@ -1031,6 +1349,13 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
     if (id < 0) id = 0;  // masked in the scores
     const int y0 = (int)((id * p.hkv + h) * B + (pos0 & (B - 1)));
     issue_piece(tm, PT_SEL, y0, plen[i], prow[i], kt, vt, NR, &kbar[i], &vbar[i], lane);
+    if (i == 0) NKV_STAMP(trc, 42);
+  }
+  NKV_STAMP(trc, 43);
+  if (FS && split == 0 && h == 0 && warp == NW - 1 && lane < p.n_sel) {
+    // the selected ids in rank order
+    p.rank_out[lane] = (long long)key_id(s_sel[lane]);
+    if (p.rank_out_scores) p.rank_out_scores[lane] = key_score(s_sel[lane]);
   }
   NKV_STAMP(trc, 63);
   for (unsigned long long m = thr_pieces; m; m &= m - 1) {
@@ -1498,11 +1823,18 @@ extern "C" size_t nkv_attend_workspace_bytes(int hkv, int hq, int nq, int max_to
 }
 
 struct RankArgs {
-  const float* scores;
+  const float* scores;  // ranked mode: block scores of a scoring grid; null: one-launch step
   int nblocks;
   int64_t* out_ids;
   float* out_scores;
+  // one-launch step: the attention grid scores the blocks itself
+  const void* reps;
+  int r, reps_blocks;
+  const int32_t* prot;
+  int nprot;
+  void* sel_ws;  // select workspace: epoch at +16, arrivals at +20, keys at +256
 };
+static bool g_fs_unavailable = false;  // the cooperative cluster launch was refused once
 
 static int attend_impl(nkv_stream_t stream, const nkv_attend_args* a, const RankArgs* rank);
 
@@ -1517,8 +1849,26 @@ int attend_ranked(nkv_stream_t stream, const nkv_attend_args* a, const float* sc
   NKV_REQUIRE(a->n_sel >= 1 && a->n_sel <= 32 && a->n_sel <= nblocks, "attend_ranked: k=%d out of [1, 32]",
               a->n_sel);
   NKV_SUPPORTED(nblocks <= 8 * 32 * RANK_MAXC, "attend_ranked: %d blocks exceed the in-kernel ranking", nblocks);
-  RankArgs r{scores, nblocks, out_ids, out_scores};
+  RankArgs r{scores, nblocks, out_ids, out_scores, nullptr, 0, 0, nullptr, 0, nullptr};
   return attend_impl(stream, a, &r);
+}
+
+// One-launch decode step: scoring, selection and attention in one cooperative
+// cluster launch.  Returns FS_DECLINED (nothing launched) where it does not
+// apply; the caller then runs the scoring grid and the ranked attention.
+int attend_step(nkv_stream_t stream, const nkv_attend_args* a, const void* reps, int r, int reps_blocks,
+                int nblocks, const int32_t* prot, int nprot, void* sel_ws, size_t sel_ws_bytes, int64_t* out_ids,
+                float* out_scores) {
+  NKV_REQUIRE(a && a->nq == 1 && reps && out_ids && sel_ws, "decode step: null argument");
+  NKV_REQUIRE(a->n_sel >= 1 && a->n_sel <= nblocks && nblocks <= reps_blocks, "decode step: k=%d, nblocks=%d",
+              a->n_sel, nblocks);
+  NKV_REQUIRE(nprot == 0 || prot, "decode step: protected ids missing");
+  NKV_REQUIRE(((uintptr_t)reps & 15) == 0, "decode step: reps must be 16-byte aligned");
+  NKV_REQUIRE(sel_ws_bytes >= nkv_select_workspace_bytes(reps_blocks, 1), "decode step: select workspace too small");
+  if (g_fs_unavailable || a->n_sel > 32 || r < 1 || r > 4 || r == 3 || nblocks > FS_MAXE * NKV_DECODE_WARPS * 32)
+    return FS_DECLINED;
+  RankArgs ra{nullptr, nblocks, out_ids, out_scores, reps, r, reps_blocks, prot, nprot, sel_ws};
+  return attend_impl(stream, a, &ra);
 }
 }  // namespace nkv
 
@@ -1648,6 +1998,16 @@ static int attend_impl(nkv_stream_t stream, const nkv_attend_args* a, const Rank
   p.rank_n = rank ? rank->nblocks : 0;
   p.rank_out = rank ? (long long*)rank->out_ids : nullptr;
   p.rank_out_scores = rank ? rank->out_scores : nullptr;
+  const bool one_launch = rank && !rank->scores;
+  p.fs_reps = one_launch ? (const __nv_bfloat16*)rank->reps : nullptr;
+  p.fs_r = one_launch ? rank->r : 0;
+  p.fs_reps_blocks = one_launch ? rank->reps_blocks : 0;
+  p.fs_prot = one_launch ? rank->prot : nullptr;
+  p.fs_nprot = one_launch ? rank->nprot : 0;
+  p.fs_keys = one_launch ? (unsigned long long*)((char*)rank->sel_ws + 256) : nullptr;
+  p.fs_sync = one_launch ? (unsigned*)((char*)rank->sel_ws + 16) : nullptr;
+  p.fs_bpc = 0;
+  p.fs_prefetch = env_int("NKV_FS_PREFETCH", 1);
   AttendParams pg = p;  // workspace-merge configuration (fallback)
   pg.cluster = 0;
   {
@@ -1730,7 +2090,16 @@ static int attend_impl(nkv_stream_t stream, const nkv_attend_args* a, const Rank
   cudaStream_t st = (cudaStream_t)stream;
   const bool q1 = a->nq == 1;
   p.overlap = pg.overlap = a->overlap_select ? 1 : 0;
-  cudaLaunchAttribute attr[2];
+  if (one_launch) {
+    // every CTA of the grid waits for every other CTA's keys: cluster mode
+    // only, as one cooperative launch (all CTAs co-resident), no overlap
+    // with the preceding kernel
+    if (!p.cluster || !q1) return FS_DECLINED;
+    p.fs_bpc = (rank->nblocks + p.splits * a->hkv - 1) / (p.splits * a->hkv);
+    if (p.fs_bpc > FS_BPC_MAX) return FS_DECLINED;
+    p.overlap = 0;
+  }
+  cudaLaunchAttribute attr[3];
   cudaLaunchConfig_t lc = {};
   auto config = [&](const AttendParams& q) {
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1745,6 +2114,11 @@ static int attend_impl(nkv_stream_t stream, const nkv_attend_args* a, const Rank
     lc.stream = st;
     lc.attrs = attr;
     lc.numAttrs = 2;
+    if (q.fs_keys) {
+      attr[2].id = cudaLaunchAttributeCooperative;
+      attr[2].val.cooperative = 1;
+      lc.numAttrs = 3;
+    }
   };
   DecodeMaps maps;
   memset(&maps, 0, sizeof(maps));
@@ -1766,22 +2140,32 @@ static int attend_impl(nkv_stream_t stream, const nkv_attend_args* a, const Rank
   switch (G * 2 + (q1 ? 1 : 0)) {
 #define NKV_AT_CASE(GG, QQ)                                                                     \
   case GG * 2 + (QQ ? 1 : 0): {                                                                 \
-    auto kern = QQ ? (const void*)decode_kernel<GG> : (const void*)attend_kernel<GG, false>;    \
+    auto kern = !QQ ? (const void*)attend_kernel<GG, false>                                     \
+                : one_launch ? (const void*)decode_kernel<GG, true> : (const void*)decode_kernel<GG>; \
     if (ensure_smem(kern, smem_of(p) > smem_of(pg) ? smem_of(p) : smem_of(pg), "attend"))       \
       return NKV_ERR_CUDA;                                                                      \
     if (p.cluster) {                                                                            \
       int ok = p.splits <= 8 || !ensure_nonportable_cluster(kern, "attend");                    \
       int nclusters = 0;                                                                        \
       config(p);                                                                                \
+      lc.numAttrs = 2; /* occupancy of the cluster shape (without the cooperative flag) */     \
       if (ok && !cluster_occupancy(kern, lc, &nclusters)) ok = 0;                             \
+      if (one_launch && (!ok || nclusters < a->hkv)) return FS_DECLINED;                        \
       if (!ok || nclusters < 1) p = pg;                                                         \
     }                                                                                           \
     config(p);                                                                                  \
     g_last_cluster = p.cluster;                                                                 \
     g_last_splits = p.splits;                                                                   \
     g_last_tps = p.tps;                                                                         \
-    cudaError_t le = QQ ? cudaLaunchKernelEx(&lc, decode_kernel<GG>, p, maps)                   \
-                        : cudaLaunchKernelEx(&lc, attend_kernel<GG, false>, p);                 \
+    cudaError_t le = !QQ ? cudaLaunchKernelEx(&lc, attend_kernel<GG, false>, p)                 \
+                     : one_launch ? cudaLaunchKernelEx(&lc, decode_kernel<GG, true>, p, maps)   \
+                                  : cudaLaunchKernelEx(&lc, decode_kernel<GG>, p, maps);        \
+    if (le != cudaSuccess && one_launch) {                                                      \
+      /* a refused launch configuration (nothing ran): fall back from now on */                \
+      cudaGetLastError();                                                                       \
+      g_fs_unavailable = true;                                                                  \
+      return FS_DECLINED;                                                                       \
+    }                                                                                           \
     if (le != cudaSuccess) return check_launch("attend");                                       \
     break;                                                                                      \
   }

@@ -52,11 +52,33 @@ extern "C" int nkv_map_host(void* host_ptr, void** dev_ptr) {
   return NKV_OK;
 }
 
+static thread_local int g_decode_form = 0;
+extern "C" int nkv_decode_last_form(void) { return g_decode_form; }
+
 extern "C" int nkv_decode_step(nkv_stream_t stream, const nkv_decode_args* a) {
   NKV_REQUIRE(a, "decode_step: null args");
   const nkv_attend_args& t = a->attend;
   NKV_REQUIRE(t.nq == 1 && t.n_cur == 1, "decode_step: needs one query and one current token");
-  // fused form: a scoring grid, then the attention grid ranks the scores in
+  // one launch (NKV_DECODE_ONE=1): the attention grid scores and selects the
+  // blocks itself; falls through where it does not apply.  Off by default:
+  // on B200 at 32K it measured 16.7 us per layer against 14.9 us for the two
+  // launches below (its in-CTA scoring and selection take longer than the
+  // scoring grid and the launch it saves).
+  const char* one = getenv("NKV_DECODE_ONE");
+  if (one && atoi(one) != 0) {
+    nkv_attend_args b = t;
+    b.block_ids = a->out_ids;
+    b.n_sel = a->k;
+    b.overlap_select = 0;
+    const int rc = nkv::attend_step(stream, &b, a->reps, a->r, a->reps_blocks, a->nblocks, a->protected_ids,
+                                    a->n_protected, a->select_workspace, a->select_workspace_bytes, a->out_ids,
+                                    a->out_topk_scores);
+    if (rc != nkv::FS_DECLINED) {
+      g_decode_form = 1;
+      return rc;
+    }
+  }
+  // two launches: a scoring grid, then the attention grid ranks the scores in
   // each CTA (no ranking tail between the two); NKV_DECODE_FUSED=0 selects
   // the two public kernels instead
   const char* env = getenv("NKV_DECODE_FUSED");
@@ -71,6 +93,7 @@ extern "C" int nkv_decode_step(nkv_stream_t stream, const nkv_decode_args* a) {
     b.n_sel = a->k;
     const char* pdl = getenv("NKV_PDL");  // NKV_PDL=0: plain stream order (measurement)
     b.overlap_select = (pdl && atoi(pdl) == 0) ? 0 : 1;
+    g_decode_form = 2;
     return nkv::attend_ranked(stream, &b, scores, a->nblocks, a->out_ids, a->out_topk_scores);
   }
   int rc = nkv_select(stream, t.q, 1, t.q_row_stride, t.q_head_stride, t.hq, t.hkv, t.head_dim, a->reps, a->r,
@@ -81,6 +104,7 @@ extern "C" int nkv_decode_step(nkv_stream_t stream, const nkv_decode_args* a) {
   b.block_ids = a->out_ids;
   b.n_sel = a->k;
   b.overlap_select = 1;
+  g_decode_form = 3;
   return nkv_attend(stream, &b);
 }
 

@@ -93,6 +93,16 @@ int select_scores(cudaStream_t st, const void* q, int64_t q_row_stride, int64_t 
 // The ranked ids (and scores, when out_scores != NULL) are written to out_ids.
 int attend_ranked(nkv_stream_t stream, const nkv_attend_args* args, const float* scores, int nblocks,
                   int64_t* out_ids, float* out_scores);
+// attend_step: the whole decode step (scoring of every block, protection,
+// top args->n_sel selection, attention) as one cooperative cluster launch.
+// The keys it publishes live in the select workspace, which must start at
+// zero and belong to one stream.  Returns FS_DECLINED, with nothing launched,
+// where the configuration is outside it (the caller then runs select_scores +
+// attend_ranked).
+constexpr int FS_DECLINED = 1;
+int attend_step(nkv_stream_t stream, const nkv_attend_args* args, const void* reps, int r, int reps_blocks,
+                int nblocks, const int32_t* protected_ids, int n_protected, void* select_workspace,
+                size_t select_workspace_bytes, int64_t* out_ids, float* out_scores);
 
 // prefill_tc: kernel (4) on tcgen05/TMEM for the calls it supports (bf16
 // history in device memory, block_size 64, TMA-addressable tensors); returns

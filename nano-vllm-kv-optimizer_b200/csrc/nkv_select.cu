@@ -415,7 +415,9 @@ static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 extern "C" size_t nkv_select_workspace_bytes(int max_blocks, int nq) {
   if (max_blocks < 1) max_blocks = 1;
   if (nq < 1) nq = 1;
-  return 256 /* ticket + error words */ + align256((size_t)max_blocks * nq * sizeof(float));
+  // header (ticket, error word, the one-launch decode step's epoch and
+  // arrivals), the one-launch step's tagged keys, then the block scores
+  return 256 + align256((size_t)max_blocks * 8) + align256((size_t)max_blocks * nq * sizeof(float));
 }
 
 static int select_common(cudaStream_t st, const void* q, int nq, int64_t q_row_stride,
@@ -463,7 +465,7 @@ static int select_common(cudaStream_t st, const void* q, int nq, int64_t q_row_s
     if (workspace_bytes >= need + (1 << 16)) p.trace = (int*)((char*)workspace + workspace_bytes - (1 << 16));
   }
 #endif
-  p.scores = (float*)((char*)workspace + 256);
+  p.scores = (float*)((char*)workspace + 256 + align256((size_t)max_blocks * 8));
   return NKV_OK;
 }
 
