@@ -23,7 +23,11 @@
 //              thread: S from TMEM, mask, online softmax in the exp2 domain with
 //              lazy rescaling of O (only when the row max grows by more than
 //              2^8), P as bf16 into a double-buffered swizzled shared tile (the A
-//              operand of the next MMA), and the epilogue O / l -> bf16.
+//              operand of the next MMA), and the epilogue O / l -> bf16.  The
+//              softmax stream is issue-bound, so it is kept short: row max by
+//              3-input max, exponent arguments and row sums on packed fp32
+//              pairs, ex2.approx on the MUFU unit (moving a share of the
+//              exponentials to an FMA-pipe polynomial measured slower).
 // Every wait is bounded (error word + fall through); TMEM is freed by warp 1
 // after all warps meet at the end.
 #include <cuda.h>
@@ -213,6 +217,27 @@ __device__ __forceinline__ Tile tile_of(const TcParams& p, int h, int j, int len
   return t;
 }
 
+// Three-input maximum (one instruction on sm_100a) and packed fp32 pairs.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+// 2^x with the MUFU instruction alone (subnormal results flush to zero: such
+// terms are below 2^-126 of the row maximum's).
+__device__ __forceinline__ float ex2_mufu(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  unsigned long long ra = (unsigned long long)__float_as_uint(a.x) | ((unsigned long long)__float_as_uint(a.y) << 32);
+  unsigned long long rb = (unsigned long long)__float_as_uint(b.x) | ((unsigned long long)__float_as_uint(b.y) << 32);
+  unsigned long long rd;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(rd) : "l"(ra), "l"(rb));
+  return make_float2(__uint_as_float((uint32_t)rd), __uint_as_float((uint32_t)(rd >> 32)));
+}
+
 template <int G>
 __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParams p, const __grid_constant__ TcMaps tm) {
   extern __shared__ __align__(16) unsigned char sm_raw[];
@@ -389,13 +414,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParam
           if (!vis) sr[c] = __float_as_uint(-INFINITY);
         }
       }
-      // row max over 8 independent partial maxima (no 64-long dependency chain)
+      // row max: 8 independent partial maxima, two new columns per 3-input max
       float mp[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) mp[u] = __uint_as_float(sr[u]);
+      for (int u = 0; u < 8; ++u) mp[u] = fmaxf(__uint_as_float(sr[2 * u]), __uint_as_float(sr[2 * u + 1]));
 #pragma unroll
-      for (int c = 8; c < 64; ++c) mp[c & 7] = fmaxf(mp[c & 7], __uint_as_float(sr[c]));
-      const float mxr = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+      for (int c = 16; c < 64; c += 2)
+        mp[(c >> 1) & 7] = fmax3(mp[(c >> 1) & 7], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+      const float mxr = fmax3(fmax3(mp[0], mp[1], mp[2]), fmax3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
       const float m_new = fmaxf(m_ref, mxr * p.sl2);
       const bool rescale = m_new > m_ref + 8.f;
       // P buffer j % 2 is free once PV_{j-2} is done; O is current once PV_{j-1} is
@@ -421,16 +447,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParam
       }
       const float nbase = m_ref == -INFINITY ? 0.f : -m_ref;
       uint32_t pw[32];
-      float lp[4] = {0.f, 0.f, 0.f, 0.f};  // partial row sums (independent chains)
+      // exponent arguments and row sums on packed fp32 pairs (4 independent sum chains)
+      float2 lp[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      const float2 sl2 = make_float2(p.sl2, p.sl2), nb2 = make_float2(nbase, nbase);
 #pragma unroll
       for (int c = 0; c < 64; c += 2) {
-        const float a = exp2f(fmaf(__uint_as_float(sr[c]), p.sl2, nbase));
-        const float b = exp2f(fmaf(__uint_as_float(sr[c + 1]), p.sl2, nbase));
-        lp[(c >> 1) & 3] += a + b;
-        const __nv_bfloat162 hb = __floats2bfloat162_rn(a, b);
+        const float2 x = ffma2(make_float2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), sl2, nb2);
+        const float2 e = make_float2(ex2_mufu(x.x), ex2_mufu(x.y));
+        lp[(c >> 1) & 3] = fadd2(lp[(c >> 1) & 3], e);
+        const __nv_bfloat162 hb = __floats2bfloat162_rn(e.x, e.y);
         pw[c / 2] = *reinterpret_cast<const uint32_t*>(&hb);
       }
-      l += (lp[0] + lp[1]) + (lp[2] + lp[3]);
+      l += ((lp[0].x + lp[0].y) + (lp[1].x + lp[1].y)) + ((lp[2].x + lp[2].y) + (lp[3].x + lp[3].y));
       unsigned char* prow = ps + (t * 2 + (j & 1)) * TC_P_BYTES + row * 128;
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch)
