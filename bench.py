@@ -459,29 +459,32 @@ def main():
     achieved = ATTEND_BYTES / (att_us * 1e-6) / 1e9
     step_gbs = STEP_BYTES / (ms_per_step * 1000.0 / L * 1e-6) / 1e9
 
-    # end to end through the public API: pinned host q/k/v -> device, eager
-    # rt.decode per layer, output back to pinned host memory
-    # each layer's q, k, v packed in one pinned host row: one copy in, one out
+    # end to end through the public API: the step's q/k/v for every layer
+    # copied from pinned host memory in one transfer, eager rt.decode per
+    # layer, the step's outputs gathered and copied back in one transfer
     QKV = (HQ + 2 * HKV) * D
     hqkv = torch.randn(L, QKV).bfloat16().pin_memory()
     ho = torch.empty(L, 1, HQ, D, dtype=torch.bfloat16).pin_memory()
     e2e_steps = max(3, min(args.steps, 20))
+    # a persistent device staging buffer for the step's inputs; each layer's
+    # q, k, v are fixed views of it (as a model's qkv projection output would be)
+    xdev = torch.empty(L, QKV, dtype=torch.bfloat16, device=dev)
+    views = [(xdev[li, :HQ * D].view(1, HQ, D), xdev[li, HQ * D:(HQ + HKV) * D].view(1, HKV, D),
+              xdev[li, (HQ + HKV) * D:].view(1, HKV, D)) for li in range(L)]
     with torch.cuda.stream(stream):
         def e2e_step():
-            for li, rt in enumerate(layers):
-                x = hqkv[li].to(dev, non_blocking=True)
-                q = x[:HQ * D].view(1, HQ, D)
-                k = x[HQ * D:(HQ + HKV) * D].view(1, HKV, D)
-                v = x[(HQ + HKV) * D:].view(1, HKV, D)
-                o = rt.decode(q, k, v, dev)
-                ho[li].copy_(o, non_blocking=True)
+            xdev.copy_(hqkv, non_blocking=True)
+            outs = [rt.decode(q, k, v, dev) for rt, (q, k, v) in zip(layers, views)]
+            ho.copy_(torch.stack(outs), non_blocking=True)
         for _ in range(2):
             e2e_step()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
+        h0 = time.perf_counter()
         for _ in range(e2e_steps):
             e2e_step()
+        host_us = (time.perf_counter() - h0) * 1e6 / (e2e_steps * L)  # host issue time per layer
         e1.record(stream)
         e1.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
@@ -519,7 +522,7 @@ def main():
             "cpu_baseline": None if cpu_us is None else {
                 "value": round(cpu_us, 1), "unit": UNIT, "cores": threads, "kind": "port",
                 "sample": f"{n_cpu} decode calls of one 32K layer state (median)"},
-            "e2e": {"value": round(e2e_value, 4), "unit": UNIT,
+            "e2e": {"value": round(e2e_value, 4), "unit": UNIT, "host_us_per_layer": round(host_us, 2),
                     "h2d_bytes_per_step": L * (HQ + 2 * HKV) * D * 2,
                     "d2h_bytes_per_step": L * HQ * D * 2},
             "gpu_launches": 2 * L * args.steps,

@@ -206,6 +206,12 @@ int nkv_decode_step(nkv_stream_t stream, const nkv_decode_args* args);
  * (Introspection for tests and benchmarks; no counterpart in the reference.) */
 int nkv_decode_last_form(void);
 
+/* The NKV_* tuning variables of the environment (launch shapes, merge form,
+ * the decode step's form) are read once per host thread and cached; after
+ * changing them, call nkv_reload_env() to have every thread read them again.
+ * (No counterpart in the reference.) */
+void nkv_reload_env(void);
+
 /* The two halves of nkv_decode_step, for a caller that combines block scores
  * across devices between them (KV heads sharded over GPUs: each rank scores
  * its own heads, the scores are max-reduced over the ranks, then every rank

@@ -97,6 +97,7 @@ SIGNATURES = {
     "nkv_attend_static": (c_int, [c_vp, C.POINTER(AttendArgs)]),
     "nkv_decode_step": (c_int, [c_vp, C.POINTER(DecodeArgs)]),
     "nkv_decode_last_form": (c_int, []),
+    "nkv_reload_env": (None, []),
     "nkv_select_scores": (c_int, [c_vp, c_vp, c_i64, c_i64, c_int, c_int, c_int, c_vp, c_int, c_int, c_int,
                                   c_vp, c_int, c_vp, c_vp, C.c_size_t]),
     "nkv_attend_ranked": (c_int, [c_vp, C.POINTER(AttendArgs), c_vp, c_int, c_vp, c_vp]),
@@ -152,6 +153,17 @@ def call(name: str, *args):
         cls = NanoKVUnsupported if rc == NKV_ERR_UNSUPPORTED else NanoKVError
         raise cls(name, rc, msg)
     return rc
+
+
+def set_env(name: str, value) -> None:
+    """Set (or, with None, remove) an NKV_* tuning variable and make the
+    library read the environment again (it caches the variables)."""
+    if value is None:
+        os.environ.pop(name, None)
+    else:
+        os.environ[name] = str(value)
+    if _lib is not None:
+        _lib.nkv_reload_env()
 
 
 def device_pointer(t) -> int:

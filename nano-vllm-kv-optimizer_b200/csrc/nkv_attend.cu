@@ -1691,10 +1691,7 @@ __device__ void combine_splits(const AttendParams& p, int h, float* wbuf) {
 // Launch shape of the most recent nkv_attend call on this thread.
 static thread_local int g_last_cluster = -1, g_last_splits = 0, g_last_tps = 0;
 
-static int env_int(const char* name, int dflt) {
-  const char* v = getenv(name);
-  return (v && *v) ? atoi(v) : dflt;
-}
+static int env_int(const char* name, int dflt) { return knob(name, dflt); }
 
 static int splits_for(int ntok, int hkv, int sms) {
   int s_mem = (ntok + AT_TPS_MAX - 1) / AT_TPS_MAX;
@@ -1771,6 +1768,51 @@ static bool source_maps(DecodeMaps* m, int src, const void* k, const void* v, lo
   if (!tma_rows_map(&m->m[src][0][0], k, rows, 8) || !tma_rows_map(&m->m[src][1][0], v, rows, 8)) return false;
   if (rows < 64) return true;
   return tma_rows_map(&m->m[src][0][1], k, rows, 64) && tma_rows_map(&m->m[src][1][1], v, rows, 64);
+}
+
+// The decode kernel's tensor maps for one combination of sources (block
+// store, sink, recent ring; a null pointer = source absent), with the mask of
+// the sources TMA may read.  Cached per thread, least recently used out of 64
+// combinations: a layer's buffers stay put, so a decode step finds its maps
+// with one lookup instead of twelve.
+static const DecodeMaps& decode_maps(const void* ks, const void* vs, long long krows, const void* sk, const void* sv,
+                                     long long srows, const void* rk, const void* rv, long long rrows, int* mask) {
+  struct Entry { const void* ptr[6]; long long rows[3]; int mask; unsigned long long stamp; DecodeMaps maps; };
+  constexpr int N = 64;
+  static thread_local Entry* cache = nullptr;
+  static thread_local unsigned long long clock = 0;
+  static thread_local DecodeMaps scratch;
+  const void* ptr[6] = {ks, vs, sk, sv, rk, rv};
+  const long long rows[3] = {ks ? krows : 0, sk ? srows : 0, rk ? rrows : 0};
+  if (!cache) cache = static_cast<Entry*>(calloc(N, sizeof(Entry)));
+  Entry* victim = nullptr;
+  if (cache) {
+    for (int i = 0; i < N; ++i) {
+      Entry& e = cache[i];
+      if (e.stamp && e.ptr[0] == ptr[0] && e.ptr[1] == ptr[1] && e.ptr[2] == ptr[2] && e.ptr[3] == ptr[3] &&
+          e.ptr[4] == ptr[4] && e.ptr[5] == ptr[5] && e.rows[0] == rows[0] && e.rows[1] == rows[1] &&
+          e.rows[2] == rows[2]) {
+        e.stamp = ++clock;
+        *mask = e.mask;
+        return e.maps;
+      }
+      if (!victim || e.stamp < victim->stamp) victim = &e;
+    }
+  }
+  DecodeMaps& m = victim ? victim->maps : scratch;
+  memset(&m, 0, sizeof(m));
+  int mk = 0;
+  if (ks && source_maps(&m, 0, ks, vs, krows)) mk |= 1;
+  if (sk && source_maps(&m, 1, sk, sv, srows)) mk |= 2;
+  if (rk && source_maps(&m, 2, rk, rv, rrows)) mk |= 4;
+  if (victim) {
+    for (int i = 0; i < 6; ++i) victim->ptr[i] = ptr[i];
+    for (int i = 0; i < 3; ++i) victim->rows[i] = rows[i];
+    victim->mask = mk;
+    victim->stamp = ++clock;
+  }
+  *mask = mk;
+  return m;
 }
 
 // cudaOccupancyMaxActiveClusters for a launch configuration, cached per
@@ -2121,16 +2163,15 @@ static int attend_impl(nkv_stream_t stream, const nkv_attend_args* a, const Rank
     }
   };
   DecodeMaps maps;
-  memset(&maps, 0, sizeof(maps));
   if (q1) {
     int mask = 0;
-    if (a->n_sel > 0 && a->store_kind == NKV_STORE_BF16 &&
-        source_maps(&maps, 0, a->k_store, a->v_store, (long long)a->max_blocks * a->hkv * a->block_size))
-      mask |= 1;
-    if (a->sink_len > 0 && source_maps(&maps, 1, a->sink_k, a->sink_v, (long long)a->hkv * a->sink_cap))
-      mask |= 2;
-    if (a->ring_len > 0 && source_maps(&maps, 2, a->ring_k, a->ring_v, (long long)a->hkv * a->ring_cap))
-      mask |= 4;
+    const bool want_sel = a->n_sel > 0 && a->store_kind == NKV_STORE_BF16;
+    const DecodeMaps& dm = decode_maps(want_sel ? a->k_store : nullptr, want_sel ? a->v_store : nullptr,
+                                       (long long)a->max_blocks * a->hkv * a->block_size,
+                                       a->sink_len > 0 ? a->sink_k : nullptr, a->sink_len > 0 ? a->sink_v : nullptr,
+                                       (long long)a->hkv * a->sink_cap, a->ring_len > 0 ? a->ring_k : nullptr,
+                                       a->ring_len > 0 ? a->ring_v : nullptr, (long long)a->hkv * a->ring_cap, &mask);
+    maps = dm;
     p.tma_mask = pg.tma_mask = env_int("NKV_ATTEND_TMA", 1) ? mask : 0;
     NKV_REQUIRE(((uintptr_t)a->k_store & 15) == 0 && ((uintptr_t)a->v_store & 15) == 0 &&
                     ((uintptr_t)a->sink_k & 15) == 0 && ((uintptr_t)a->sink_v & 15) == 0 &&

@@ -4,6 +4,8 @@
 #include <stdlib.h>
 #include <stdio.h>
 
+#include <atomic>
+
 #include "nkv_host.h"
 
 namespace nkv {
@@ -15,6 +17,29 @@ void set_error(const char* fmt, ...) {
   va_end(ap);
 }
 }  // namespace nkv
+
+namespace nkv {
+static std::atomic<unsigned> g_env_gen{1};
+int knob(const char* name, int dflt) {
+  struct Entry { const char* name; int dflt, value; };
+  static thread_local Entry cache[32];
+  static thread_local int used = 0;
+  static thread_local unsigned gen = 0;
+  const unsigned g = g_env_gen.load(std::memory_order_relaxed);
+  if (gen != g) {
+    used = 0;
+    gen = g;
+  }
+  for (int i = 0; i < used; ++i)
+    if (cache[i].name == name && cache[i].dflt == dflt) return cache[i].value;
+  const char* v = getenv(name);
+  const int value = (v && *v) ? atoi(v) : dflt;
+  if (used < 32) cache[used++] = Entry{name, dflt, value};
+  return value;
+}
+}  // namespace nkv
+
+extern "C" void nkv_reload_env(void) { nkv::g_env_gen.fetch_add(1, std::memory_order_relaxed); }
 
 extern "C" const char* nkv_last_error(void) { return nkv::g_err; }
 
@@ -64,8 +89,7 @@ extern "C" int nkv_decode_step(nkv_stream_t stream, const nkv_decode_args* a) {
   // on B200 at 32K it measured 16.7 us per layer against 14.9 us for the two
   // launches below (its in-CTA scoring and selection take longer than the
   // scoring grid and the launch it saves).
-  const char* one = getenv("NKV_DECODE_ONE");
-  if (one && atoi(one) != 0) {
+  if (nkv::knob("NKV_DECODE_ONE", 0) != 0) {
     nkv_attend_args b = t;
     b.block_ids = a->out_ids;
     b.n_sel = a->k;
@@ -81,8 +105,7 @@ extern "C" int nkv_decode_step(nkv_stream_t stream, const nkv_decode_args* a) {
   // two launches: a scoring grid, then the attention grid ranks the scores in
   // each CTA (no ranking tail between the two); NKV_DECODE_FUSED=0 selects
   // the two public kernels instead
-  const char* env = getenv("NKV_DECODE_FUSED");
-  if ((!env || atoi(env) != 0) && a->k <= 32 && a->nblocks <= 2048) {
+  if (nkv::knob("NKV_DECODE_FUSED", 1) != 0 && a->k <= 32 && a->nblocks <= 2048) {
     const float* scores = nullptr;
     int rc = nkv::select_scores((cudaStream_t)stream, t.q, t.q_row_stride, t.q_head_stride, t.hq, t.hkv, t.head_dim,
                                 a->reps, a->r, a->reps_blocks, a->nblocks, a->protected_ids, a->n_protected, a->k,
@@ -91,8 +114,7 @@ extern "C" int nkv_decode_step(nkv_stream_t stream, const nkv_decode_args* a) {
     nkv_attend_args b = t;
     b.block_ids = a->out_ids;
     b.n_sel = a->k;
-    const char* pdl = getenv("NKV_PDL");  // NKV_PDL=0: plain stream order (measurement)
-    b.overlap_select = (pdl && atoi(pdl) == 0) ? 0 : 1;
+    b.overlap_select = nkv::knob("NKV_PDL", 1) != 0 ? 1 : 0;  // NKV_PDL=0: plain stream order (measurement)
     g_decode_form = 2;
     return nkv::attend_ranked(stream, &b, scores, a->nblocks, a->out_ids, a->out_topk_scores);
   }

@@ -12,6 +12,11 @@ namespace nkv {
 
 void set_error(const char* fmt, ...);
 
+// Integer tuning knob from the environment (NKV_*): `dflt` when unset or
+// empty.  Read once per thread and cached; nkv_reload_env() makes every thread
+// read the environment again.
+int knob(const char* name, int dflt);
+
 inline int sm_count() {
   static thread_local int cached_dev = -1, cached = 0;
   int dev = 0;

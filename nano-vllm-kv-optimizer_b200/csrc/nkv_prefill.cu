@@ -410,8 +410,7 @@ extern "C" int nkv_prefill(nkv_stream_t stream, const nkv_attend_args* a) {
 
   cudaStream_t st = (cudaStream_t)stream;
   // the tcgen05/TMEM kernel takes every call it supports (NKV_PREFILL_TC=0: never)
-  const char* tc_env = getenv("NKV_PREFILL_TC");
-  if (!tc_env || atoi(tc_env) != 0) {
+  if (knob("NKV_PREFILL_TC", 1) != 0) {
     const int rc = prefill_tc(st, a);
     if (rc != NKV_ERR_UNSUPPORTED) return rc;
   }

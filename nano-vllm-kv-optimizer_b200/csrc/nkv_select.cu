@@ -382,10 +382,7 @@ static int launch_select(cudaStream_t st, SelectParams& p, int G) {
   int bpc = (p.nblocks + 4 * sms - 1) / (4 * sms);
   const int unit_bpc = SEL_WARPS / (p.hkv < SEL_WARPS ? p.hkv : SEL_WARPS);
   if (bpc < unit_bpc) bpc = unit_bpc;
-  {  // NKV_SEL_BPC: blocks per scoring CTA (tuning override)
-    const char* e = getenv("NKV_SEL_BPC");
-    if (e && atoi(e) > 0) bpc = atoi(e);
-  }
+  if (knob("NKV_SEL_BPC", 0) > 0) bpc = knob("NKV_SEL_BPC", 0);  // blocks per scoring CTA (tuning override)
   p.bpc = bpc;
   const int grid = (p.nblocks + bpc - 1) / bpc;
   int npow2 = 1;

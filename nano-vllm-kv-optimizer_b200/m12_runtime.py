@@ -295,10 +295,22 @@ class M12LayerRuntime:
         self._dargs, self._dkey, self._ids_view = None, None, None
         self._bscores = None
         self._lib_h = _lib.load()
+        # nkv_decode_step taking the argument struct's address (no ctypes byref per call)
+        self._step_fn = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_void_p)(
+            C.cast(self._lib_h.nkv_decode_step, C.c_void_p).value)
         # the single-call decode applies when no selection variant is configured
         self._fast_ok = (cfg.decode_relative_a is None and not cfg.dynamic_top_k and not cfg.gather_sort
                          and cfg.decode_query_window <= 1)
         self._decode_requested = cfg.top_k_blocks if cfg.decode_top_k_blocks is None else cfg.decode_top_k_blocks
+        self._budget_key, self._budget_val = None, 0
+        self._dev_index = self.device.index
+        # the timing record of the fast decode path (the same keys as the reference's)
+        self._fast_timings = {
+            "selector_ms": 0.0, "selector_enqueue_ms": 0.0,
+            "d2h_ms": 0.0, "cpu_gather_ms": 0.0, "h2d_pack_ms": 0.0,
+            "h2d_event_spans_cpu_gather": False, "recent_ms": 0.0,
+            "packed_attn_ms": 0.0, "selected_tokens": 0, "total_attend_tokens": 0,
+        }
         self._prot_dev = torch.zeros(1, dtype=torch.int32, **kw)
         self._n_prot_dev = 0
         self._sel_ws = None
@@ -568,8 +580,13 @@ class M12LayerRuntime:
     # ------------------------------------------------------------------
     def _budget(self, requested: int) -> int:
         nblocks = self.nblocks_filled
+        key = (nblocks, requested, len(self.protected_blocks))
+        if key == self._budget_key:
+            return self._budget_val
         n_prot = len([p for p in self.protected_blocks if p < nblocks])
-        return min(requested, max(1, nblocks - n_prot))
+        kk = min(requested, max(1, nblocks - n_prot))
+        self._budget_key, self._budget_val = key, kk
+        return kk
 
     def _select_dev(self, q: torch.Tensor, k: int, block_scores=None):
         """Launch the select kernel; returns the device ids view [k]."""
@@ -902,6 +919,9 @@ class M12LayerRuntime:
         d.out_ids, d.out_topk_scores = self._ids.data_ptr(), self._topk_scores.data_ptr()
         sws = self._select_ws(1)
         d.select_workspace, d.select_workspace_bytes = sws.data_ptr(), sws.numel()
+        a.out_row_stride, a.out_head_stride = cfg.num_heads * cfg.head_dim, cfg.head_dim
+        self._dstrides = None  # (q strides, cur strides) last written into the args
+        self._daddr = C.addressof(d)
         key = (self.nblocks_filled, self.cpu_blocks_cap, self._store_ptrs, kk, id(self._ids),
                id(self.k_scale), id(self.v_scale_cpu), id(self._k_tok_scale), id(self._sel_ws),
                id(self._att_ws))
@@ -926,19 +946,23 @@ class M12LayerRuntime:
             k, v = k.contiguous(), v.contiguous()
             ks, kp, vp = k.stride(), k.data_ptr(), v.data_ptr()
         out = torch.empty(1, cfg.num_heads, cfg.head_dim, dtype=q.dtype, device=q.device)
-        a.q, a.q_row_stride, a.q_head_stride = qp, qs[0], qs[1]
-        a.cur_k, a.cur_v, a.cur_row_stride, a.cur_head_stride = kp, vp, ks[0], ks[1]
-        a.sink_len = min(cfg.sink_tokens, self.valid_len)
+        a.q, a.cur_k, a.cur_v, a.out = qp, kp, vp, out.data_ptr()
+        strides = (qs[0], qs[1], ks[0], ks[1])
+        if strides != self._dstrides:
+            a.q_row_stride, a.q_head_stride, a.cur_row_stride, a.cur_head_stride = strides
+            self._dstrides = strides
+        sink_len = min(cfg.sink_tokens, self.valid_len)
+        if a.sink_len != sink_len:
+            a.sink_len = sink_len
         w, a.ring_start, a.ring_len, head_new = ring_decode_plan(self._ring_head, self.valid_len,
                                                                  cfg.recent_tokens)
         a.ring_write_pos = w
-        a.out, a.out_row_stride, a.out_head_stride = out.data_ptr(), cfg.num_heads * cfg.head_dim, cfg.head_dim
         return d, out, head_new
 
     def _decode_fast(self, q, k, v, kk):
         """The plain decode step as one native call (nkv_decode_step)."""
         d, out, head_new = self._decode_fill(q, k, v, kk)
-        rc = self._lib_h.nkv_decode_step(_stream_fast(q.device.index or 0), d)
+        rc = self._step_fn(_stream_fast(self._dev_index), self._daddr)
         if rc != _lib.NKV_OK:
             call("nkv_decode_step", _stream(q.device), C.byref(d))  # raises with the message
         self._ring_head = head_new
@@ -1005,14 +1029,11 @@ class M12LayerRuntime:
                 self.ids_history.append(self._ids_view.cpu().tolist())
             self.valid_len += 1
             self._last_ids_dev, self._last_ids_host = self._ids_view, None
-            self.timings = {
-                "selector_ms": 0.0, "selector_enqueue_ms": 0.0,
-                "d2h_ms": 0.0, "cpu_gather_ms": 0.0, "h2d_pack_ms": 0.0,
-                "h2d_event_spans_cpu_gather": False, "recent_ms": 0.0,
-                "packed_attn_ms": (t2 - t0) * 1000.0,
-                "selected_tokens": kk * cfg.block_size,
-                "total_attend_tokens": kk * cfg.block_size + sink_len + ring_len + 1,
-            }
+            tm = self._fast_timings
+            tm["packed_attn_ms"] = (t2 - t0) * 1000.0
+            tm["selected_tokens"] = kk * cfg.block_size
+            tm["total_attend_tokens"] = kk * cfg.block_size + sink_len + ring_len + 1
+            self.timings = tm
             if cfg.check_finite_outputs and not bool(torch.isfinite(o).all()):
                 raise RuntimeError("M12 sparse decode output is non-finite")
             return o

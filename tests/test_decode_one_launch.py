@@ -64,10 +64,12 @@ def test_one_launch_matches_oracle(hist, hq, hkv, steps, verify, one, monkeypatc
         want, scores = orc.select_blocks(qc, rt1.reps_gpu[:, :nb].cpu(), nb, rt1.protected_blocks,
                                          rt1.cfg.decode_top_k_blocks or rt1.cfg.top_k_blocks)
         monkeypatch.setenv("NKV_DECODE_ONE", "1")
+        lib.nkv_reload_env()
         o1 = rt1.decode(q, k, v, DEV)
         form1 = lib.nkv_decode_last_form()
         ids1, sc1 = rt1.last_block_ids.cpu(), rt1._topk_scores[:len(rt1.last_block_ids)].cpu()
         monkeypatch.setenv("NKV_DECODE_ONE", "0")
+        lib.nkv_reload_env()
         o2 = rt2.decode(q, k, v, DEV)
         form2 = lib.nkv_decode_last_form()
         ids2, sc2 = rt2.last_block_ids.cpu(), rt2._topk_scores[:len(rt2.last_block_ids)].cpu()
@@ -85,6 +87,8 @@ def test_one_launch_matches_oracle(hist, hq, hkv, steps, verify, one, monkeypatc
                 rt.verify_lossless = True
                 rt.verify_tokens(qv, kv, vv, DEV)
                 rt.rollback_verified()
+    monkeypatch.delenv("NKV_DECODE_ONE", raising=False)
+    lib.nkv_reload_env()
     torch.cuda.synchronize()
     for rt in (rt1, rt2):  # no bounded wait timed out, no bad block id
         assert rt._att_ws[:4].view(torch.int32).item() == 0

@@ -78,7 +78,8 @@ def _static(nkv, args, like):
 def test_static_scratch_matches_caller_workspace(nq, merge):
     nkv = pkg()
     old = os.environ.get("NKV_ATTEND_MERGE")
-    os.environ["NKV_ATTEND_MERGE"] = merge
+    nkv._lib.load()
+    nkv._lib.set_env("NKV_ATTEND_MERGE", merge)
     try:
         rt = _layer(nkv, 5)
         ref, args, _keep = _attend_args(nkv, rt, nq, 11)
@@ -95,10 +96,7 @@ def test_static_scratch_matches_caller_workspace(nq, merge):
         torch.cuda.synchronize()
         torch.testing.assert_close(out.float().cpu(), ref.float().cpu(), atol=ATOL, rtol=RTOL)
     finally:
-        if old is None:
-            os.environ.pop("NKV_ATTEND_MERGE", None)
-        else:
-            os.environ["NKV_ATTEND_MERGE"] = old
+        nkv._lib.set_env("NKV_ATTEND_MERGE", old)
 
 
 def test_static_scratch_rejects_oversize():
