@@ -150,71 +150,121 @@ SH_CTX, SH_LAYERS = 131072, 4
 
 
 def sharded_measure(nkv, dev, world, steps=20):
-    """Decode step with the KV heads split over the ranks (KVHeadShardedLayer):
-    per layer, scoring of the rank's heads, MAX all-reduce of the block scores,
-    attention of the rank's heads, all-gather of the outputs, replayed from a
-    CUDA graph that holds the NCCL calls (eager if capture is refused);
-    device time between events, max over ranks."""
+    """Decode step with the KV heads split over the ranks (KVHeadShardedLayer)
+    at 128K, per layer: scoring of the rank's heads, the maximum over ranks of
+    the block scores, attention of the rank's heads, the gather of the outputs.
+    Measured for both exchange forms -- "peer" (inside the kernels, through
+    peer memory) and "nccl" (MAX all-reduce + all-gather) -- each replayed from
+    a CUDA graph (eager if capture is refused); device time between events,
+    max over ranks.  Rank 0 also times the same layers unsharded on its GPU."""
     import torch.distributed as dist
-    g = torch.Generator(device=dev).manual_seed(5150)
-    layers = []
-    for li in range(SH_LAYERS):
-        lay = nkv.KVHeadShardedLayer(li, nkv.M12Config(max_model_len=SH_CTX + 4096, device=dev))
-        lay.rt.reserve_blocks(SH_CTX // B)
-        for c in range(SH_CTX // 4096):
-            k = torch.randn(4096, HKV, D, generator=g, device=dev).bfloat16()
-            v = torch.randn(4096, HKV, D, generator=g, device=dev).bfloat16()
-            if c == 0:
-                lay.prefill_first(None, k, v)
-            else:
-                lay.store(k, v)
-        layers.append(lay)
-    q = torch.randn(SH_LAYERS, 1, HQ, D, generator=g, device=dev).bfloat16()
-    k = torch.randn(SH_LAYERS, 1, HKV, D, generator=g, device=dev).bfloat16()
-    v = torch.randn(SH_LAYERS, 1, HKV, D, generator=g, device=dev).bfloat16()
+    res = {"workload": f"decode step @128K (Top-32 of 2048 blocks), KV heads sharded {world} ways, "
+                       f"{SH_LAYERS} layer states", "kv_heads_per_gpu": HKV // world}
+    for exchange in ("peer", "nccl"):
+        g = torch.Generator(device=dev).manual_seed(5150)
+        layers = []
+        for li in range(SH_LAYERS):
+            lay = nkv.KVHeadShardedLayer(li, nkv.M12Config(max_model_len=SH_CTX + 4096, device=dev),
+                                         exchange=exchange)
+            lay.rt.reserve_blocks(SH_CTX // B)
+            for c in range(SH_CTX // 4096):
+                k = torch.randn(4096, HKV, D, generator=g, device=dev).bfloat16()
+                v = torch.randn(4096, HKV, D, generator=g, device=dev).bfloat16()
+                if c == 0:
+                    lay.prefill_first(None, k, v)
+                else:
+                    lay.store(k, v)
+            layers.append(lay)
+        q = torch.randn(SH_LAYERS, 1, HQ, D, generator=g, device=dev).bfloat16()
+        k = torch.randn(SH_LAYERS, 1, HKV, D, generator=g, device=dev).bfloat16()
+        v = torch.randn(SH_LAYERS, 1, HKV, D, generator=g, device=dev).bfloat16()
 
-    def step():
-        for li, lay in enumerate(layers):
-            lay.decode(q[li], k[li], v[li])
-    stream = torch.cuda.Stream(dev)
-    with torch.cuda.stream(stream):
-        for _ in range(3):
-            step()
-    torch.cuda.synchronize()
-    dist.barrier()
-    # the whole sharded step (kernels and NCCL calls) captured in one CUDA graph;
-    # eager replay is the fallback when capture is refused
-    graph, mode = None, "eager"
-    try:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            step()
-        mode = "cuda graph"
-    except Exception:  # noqa: BLE001 - measured eagerly instead
-        graph = None
+        def step():
+            for li, lay in enumerate(layers):
+                lay.decode(q[li], k[li], v[li])
+        stream = torch.cuda.Stream(dev)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                step()
         torch.cuda.synchronize()
-    # every rank replays the same way (the collectives must match)
-    ok = torch.tensor([0 if graph is None else 1], device=dev)
-    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-    if int(ok.item()) == 0:
+        dist.barrier()
+        # the whole sharded step captured in one CUDA graph; eager replay is the
+        # fallback when capture is refused
         graph, mode = None, "eager"
+        try:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                step()
+            mode = "cuda graph"
+        except Exception:  # noqa: BLE001 - measured eagerly instead
+            graph = None
+            torch.cuda.synchronize()
+        # every rank replays the same way (the exchanges must match)
+        ok = torch.tensor([0 if graph is None else 1], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if int(ok.item()) == 0:
+            graph, mode = None, "eager"
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                graph.replay() if graph is not None else step()
+            e0.record(stream)
+            for _ in range(steps):
+                graph.replay() if graph is not None else step()
+            e1.record(stream)
+        e1.synchronize()
+        errs = sum(int(lay.rt._att_ws[:4].view(torch.int32).item()) != 0 for lay in layers)
+        t = torch.tensor([e0.elapsed_time(e1) * 1000.0 / (steps * SH_LAYERS), float(errs)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        del graph
+        torch.cuda.synchronize()
+        for lay in layers:
+            lay.close()
+        res[exchange] = {"us_per_layer": round(float(t[0].item()), 2), "mode": mode,
+                         "exchange": layers[0].exchange, "kernel_errors": int(t[1].item())}
+        del layers
+        torch.cuda.synchronize()
+    if dist.get_rank() == 0:
+        # the same layers on one GPU, every head (the unsharded reference point)
+        g = torch.Generator(device=dev).manual_seed(5150)
+        rts = []
+        for li in range(SH_LAYERS):
+            rt = nkv.M12LayerRuntime(li, nkv.M12Config(max_model_len=SH_CTX + 4096, device=dev))
+            rt.reserve_blocks(SH_CTX // B)
+            for c in range(SH_CTX // 4096):
+                k = torch.randn(4096, HKV, D, generator=g, device=dev).bfloat16()
+                v = torch.randn(4096, HKV, D, generator=g, device=dev).bfloat16()
+                if c == 0:
+                    rt.prefill_first(None, k, v)
+                else:
+                    rt._store_kv(k, v)
+            rts.append(rt)
+        q = torch.randn(SH_LAYERS, 1, HQ, D, generator=g, device=dev).bfloat16()
+        k = torch.randn(SH_LAYERS, 1, HKV, D, generator=g, device=dev).bfloat16()
+        v = torch.randn(SH_LAYERS, 1, HKV, D, generator=g, device=dev).bfloat16()
+        stream = torch.cuda.Stream(dev)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                for li, rt in enumerate(rts):
+                    rt.decode(q[li], k[li], v[li], dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for li, rt in enumerate(rts):
+                    rt.decode(q[li], k[li], v[li], dev)
+            for _ in range(3):
+                graph.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(steps):
+                graph.replay()
+            e1.record(stream)
+        e1.synchronize()
+        res["unsharded_1gpu_us_per_layer"] = round(e0.elapsed_time(e1) * 1000.0 / (steps * SH_LAYERS), 2)
+        del graph, rts
+        torch.cuda.synchronize()
     dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        for _ in range(3):
-            graph.replay() if graph is not None else step()
-        e0.record(stream)
-        for _ in range(steps):
-            graph.replay() if graph is not None else step()
-        e1.record(stream)
-    e1.synchronize()
-    t = torch.tensor([e0.elapsed_time(e1) * 1000.0 / (steps * SH_LAYERS)], device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    del graph, layers
-    torch.cuda.synchronize()
-    return {"workload": f"decode step @128K, KV heads sharded {world} ways (NCCL MAX all-reduce of block "
-                        f"scores + all-gather of outputs per layer), 4 layer states, {mode}",
-            "us_per_layer": round(float(t.item()), 2), "kv_heads_per_gpu": HKV // world}
+    return res
 
 
 def prefill_measure(nkv, dev, iters=5):

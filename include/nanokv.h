@@ -230,6 +230,42 @@ int nkv_select_scores(nkv_stream_t stream, const void* q, int64_t q_row_stride, 
 int nkv_attend_ranked(nkv_stream_t stream, const nkv_attend_args* args, const float* scores, int nblocks,
                       int64_t* out_ids, float* out_scores);
 
+/* KV-head sharding with the exchange inside the kernels (no collective
+ * library on the data path).  The P ranks of a layer (one GPU each, P <= 8)
+ * each allocate one exchange buffer of nkv_shard_exchange_bytes() with
+ * nkv_peer_alloc (device memory, zeroed, plus a 64-byte CUDA IPC handle), send
+ * the handle to the other ranks (any host channel), and open theirs with
+ * nkv_peer_open.  `exchanges` is then the host array of the P buffers as this
+ * rank addresses them (its own at [rank]).  Per decode step:
+ *   nkv_shard_scores: the masked block scores of this rank's heads (as
+ *     nkv_select_scores), written as step-tagged words into every rank's
+ *     buffer over NVLink;
+ *   nkv_shard_attend: nkv_attend_ranked whose CTAs poll every rank's scores in
+ *     this rank's buffer (bounded waits), rank the max over ranks (the same
+ *     ids as one GPU), attend this rank's heads, write this rank's rows of the
+ *     full-width output out_full [hq * n_ranks][128] and push them as tagged
+ *     words to every other rank, and pull the other ranks' rows into
+ *     out_full before the grid ends.  args->out must be this rank's rows of
+ *     out_full (offset rank * hq * 128, head stride 128).
+ * Every rank must run the same steps in the same order (the step tags are a
+ * per-buffer epoch advanced by nkv_shard_attend); a peer that stops leaves the
+ * others' waits to time out (error word of the attend workspace).
+ * Replaces the MAX all-reduce of the scores and the all-gather of the outputs
+ * around the reference's per-layer decode (m12_runtime.py:999-1003, 1316-1320;
+ * the reference itself runs on one GPU). */
+#define NKV_IPC_HANDLE_BYTES 64
+size_t nkv_shard_exchange_bytes(int n_ranks, int max_blocks, int hq_all);
+int nkv_peer_alloc(size_t bytes, void** dptr, void* ipc_handle);
+int nkv_peer_open(const void* ipc_handle, void** dptr);
+int nkv_peer_close(void* dptr);
+int nkv_peer_free(void* dptr);
+int nkv_shard_scores(nkv_stream_t stream, const void* q, int64_t q_row_stride, int64_t q_head_stride, int hq,
+                     int hkv, int head_dim, const void* reps, int r, int max_blocks, int nblocks,
+                     const int32_t* protected_ids, int n_protected, void* const* exchanges, int n_ranks, int rank,
+                     void* workspace, size_t workspace_bytes);
+int nkv_shard_attend(nkv_stream_t stream, const nkv_attend_args* args, void* const* exchanges, int n_ranks, int rank,
+                     int max_blocks, int nblocks, int64_t* out_ids, float* out_scores, void* out_full);
+
 /* ------------------------------------------------------------------------ */
 /* (4) Segmented prefill attention on the tensor cores: the same four segments
  * as nkv_attend for a whole chunk of nq queries (nq == n_cur, causal in-chunk,

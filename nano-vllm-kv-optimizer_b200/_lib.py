@@ -18,6 +18,7 @@ LIB_PATH = (os.path.join(HERE, "libnanokv_checked.so") if _env_lib == "checked"
             else os.path.join(HERE, "libnanokv.so"))
 
 NKV_OK = 0
+IPC_HANDLE_BYTES = 64
 NKV_ERR_ARG = -1
 NKV_ERR_UNSUPPORTED = -2
 NKV_ERR_CUDA = -3
@@ -101,6 +102,14 @@ SIGNATURES = {
     "nkv_select_scores": (c_int, [c_vp, c_vp, c_i64, c_i64, c_int, c_int, c_int, c_vp, c_int, c_int, c_int,
                                   c_vp, c_int, c_vp, c_vp, C.c_size_t]),
     "nkv_attend_ranked": (c_int, [c_vp, C.POINTER(AttendArgs), c_vp, c_int, c_vp, c_vp]),
+    "nkv_shard_exchange_bytes": (C.c_size_t, [c_int, c_int, c_int]),
+    "nkv_peer_alloc": (c_int, [C.c_size_t, C.POINTER(c_vp), c_vp]),
+    "nkv_peer_open": (c_int, [c_vp, C.POINTER(c_vp)]),
+    "nkv_peer_close": (c_int, [c_vp]),
+    "nkv_peer_free": (c_int, [c_vp]),
+    "nkv_shard_scores": (c_int, [c_vp, c_vp, c_i64, c_i64, c_int, c_int, c_int, c_vp, c_int, c_int, c_int, c_vp, c_int,
+                                 c_vp, c_int, c_int, c_vp, C.c_size_t]),
+    "nkv_shard_attend": (c_int, [c_vp, C.POINTER(AttendArgs), c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp]),
     "nkv_prefill_workspace_bytes": (C.c_size_t, [c_int, c_int, c_int, c_int]),
     "nkv_prefill": (c_int, [c_vp, C.POINTER(AttendArgs)]),
     "nkv_store_chunk": (c_int, [c_vp, C.POINTER(StoreArgs)]),

@@ -49,6 +49,9 @@ constexpr int AT_CLUSTER_MAX = 16;        // splits of one head merged through D
 constexpr int AT_TPS_MAX_CLUSTER = 384;   // keys per CTA in cluster mode (K+V: 192 KiB)
 constexpr int AT_MAX_SLOTS = 32;          // block slots one CTA can touch (tps / B + 2)
 constexpr int AT_MAX_PIECES = AT_MAX_SLOTS + 8;  // + sink, two ring pieces, current tokens
+// Bound of a wait on another GPU's words (~1 s of SM clock): the peers run
+// their own launches, so their host-side skew is part of what is waited for.
+constexpr long long PEER_WAIT_CYCLES = 2000000000ll;
 
 struct AttendParams {
   const __nv_bfloat16* q;
@@ -109,6 +112,17 @@ struct AttendParams {
   const int* fs_prot;
   unsigned long long* fs_keys;  // [rank_n]: (tag << 32) | orderable score
   unsigned* fs_sync;            // [0] epoch, [1] CTAs done with this launch's keys
+  // KV-head sharding over peer memory (xp_P > 0, ranked decode): the ranking
+  // CTAs take every rank's block scores from this rank's exchange buffer
+  // (polling their step tags; the score is the max over ranks), the merges
+  // push this rank's output rows to every other rank, and each head's merging
+  // CTA pulls the other ranks' rows of the same local head index into the
+  // full-width output; the last merging CTA advances the epoch
+  const u64* xp_scores;           // this rank's xs area
+  u64* xp_out[NKV_MAX_PEERS];     // every rank's xo area
+  uint32_t* xp_sync;              // this rank's [epoch, ticket]
+  __nv_bfloat16* xp_full;         // this rank's full-width output [xp_hq][D]
+  int xp_P, xp_rank, xp_cap, xp_hq;
 };
 
 // 2D tensor maps of the decode kernel over [rows][128] bf16 sources with
@@ -365,9 +379,9 @@ __device__ __forceinline__ void pv_accumulate(const float* sc, const __nv_bfloat
 }
 
 template <int G>
-__device__ void combine_splits(const AttendParams& p, int h, float* wbuf);
+__device__ void combine_splits(const AttendParams& p, int h, float* wbuf, uint32_t xp_ep = 0u);
 template <int G>
-__device__ void combine_cluster(const AttendParams& p, int h, float* pm, float* pl, float* po);
+__device__ void combine_cluster(const AttendParams& p, int h, float* pm, float* pl, float* po, uint32_t xp_ep = 0u);
 
 template <int G, bool Q1>
 __global__ void __launch_bounds__(AT_THREADS) attend_kernel(AttendParams p) {
@@ -683,6 +697,67 @@ __global__ void __launch_bounds__(AT_THREADS) attend_kernel(AttendParams p) {
 
 
 // ---------------------------------------------------------------------------
+// Peer exchange of the outputs (KV-head sharding).
+// ---------------------------------------------------------------------------
+// One tagged word (two bf16 of the full output, word index wi of the xo area)
+// to every other rank.
+__device__ __forceinline__ void peer_push(const AttendParams& p, uint32_t ep, long long wi, uint32_t payload) {
+  const u64 w = ((u64)step_tag(ep) << 32) | payload;
+  const long long at = (long long)(ep & 1u) * p.xp_hq * (NKV_D / 2) + wi;
+  for (int r = 0; r < p.xp_P; ++r)
+    if (r != p.xp_rank) st_peer_u64(p.xp_out[r] + at, w);
+}
+// Run by the merging CTA of local head h after its own rows are written and
+// pushed: pulls the rows of local head h of every other rank (global head
+// r * heads + h) from this rank's xo area into the full output (four words in
+// flight per thread, each polled until it carries this step's tag; bounded),
+// then arrives on the epoch ticket; the last of the grid's heads to arrive
+// advances the epoch (every CTA of the grid has read it by then).
+template <int G>
+__device__ void peer_pull_arrive(const AttendParams& p, int h, uint32_t ep) {
+  const int tid = threadIdx.x, bs = (int)blockDim.x, Hl = (int)gridDim.y;
+  const uint32_t tag = step_tag(ep);
+  constexpr int WPH = G * (NKV_D / 2);  // words per head
+  const u64* xo = p.xp_out[p.xp_rank] + (long long)(ep & 1u) * p.xp_hq * (NKV_D / 2);
+  const int n = (p.xp_P - 1) * WPH;
+  bool late = false;
+  for (int base = tid; base < n; base += 4 * bs) {
+    long long wi[4];
+    u64 w[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = base + u * bs;
+      wi[u] = -1;
+      if (i < n) {
+        const int rr = i / WPH;
+        const int r = rr < p.xp_rank ? rr : rr + 1;
+        wi[u] = (long long)(r * Hl + h) * WPH + i % WPH;
+        w[u] = ld_peer_u64(xo + wi[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (wi[u] < 0) continue;
+      if ((uint32_t)(w[u] >> 32) != tag) {
+        const long long t0 = clock64();
+        while ((uint32_t)((w[u] = ld_peer_u64(xo + wi[u])) >> 32) != tag)
+          if (clock64() - t0 > PEER_WAIT_CYCLES) {
+            late = true;
+            break;
+          }
+      }
+      *reinterpret_cast<uint32_t*>(p.xp_full + wi[u] * 2) = (uint32_t)w[u];
+    }
+  }
+  if (late && p.err) atomicExch(p.err, ERR_WAIT_TIMEOUT);
+  __syncthreads();
+  if (tid == 0 && atomicAdd(p.xp_sync + 1, 1u) == (unsigned)Hl - 1u) {
+    p.xp_sync[1] = 0u;
+    atomicAdd(p.xp_sync, 1u);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Decode tiles.  The K and V keys of a CTA sit in shared memory as
 // [2][rows][128 B] (the two 64-column halves of a key row) in the 128-byte
 // swizzle that TMA writes: 16-byte chunk c of row r is stored at chunk
@@ -728,6 +803,8 @@ __device__ __forceinline__ void issue_piece(const DecodeMaps& tm, int src, int y
 // that cannot enter it, then the warp lists merge pairwise.  Returns with
 // lists[0..31] = ranks 0..31 (all threads must call).  n <= NW * 32 * MAXC.
 template <int NW, int MAXC>
+__device__ void rank_top32_vals(const float (&v)[MAXC], int n, u64* lists);
+template <int NW, int MAXC>
 __device__ void rank_top32(const float* __restrict__ scores, int n, u64* lists) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float v[MAXC];
@@ -736,6 +813,47 @@ __device__ void rank_top32(const float* __restrict__ scores, int n, u64* lists) 
     const int i = (warp + c * NW) * 32 + lane;
     v[c] = i < n ? __ldcg(scores + i) : -INFINITY;
   }
+  rank_top32_vals<NW, MAXC>(v, n, lists);
+}
+// rank_top32 over the max across ranks of the tagged scores in this rank's
+// exchange buffer: every (rank, block) word of the thread is loaded, then the
+// ones not yet carrying this step's tag are polled again (bounded, then
+// ERR_WAIT_TIMEOUT and the stale value).
+template <int NW, int MAXC>
+__device__ void rank_top32_peer(const AttendParams& p, uint32_t ep, u64* lists) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t tag = step_tag(ep);
+  const u64* xs = p.xp_scores + (long long)(ep & 1u) * p.xp_P * p.xp_cap;
+  float v[MAXC];
+#pragma unroll
+  for (int c = 0; c < MAXC; ++c) v[c] = -INFINITY;
+  for (int r = 0; r < p.xp_P; ++r) {
+    unsigned pending = 0u;
+#pragma unroll
+    for (int c = 0; c < MAXC; ++c)
+      if ((warp + c * NW) * 32 + lane < p.rank_n) pending |= 1u << c;
+    const long long t0 = clock64();
+    while (pending) {
+#pragma unroll
+      for (int c = 0; c < MAXC; ++c) {
+        if (!((pending >> c) & 1u)) continue;
+        const u64 w = ld_peer_u64(xs + (long long)r * p.xp_cap + (warp + c * NW) * 32 + lane);
+        if ((uint32_t)(w >> 32) == tag) {
+          v[c] = fmaxf(v[c], f32_unorder((uint32_t)w));
+          pending &= ~(1u << c);
+        }
+      }
+      if (pending && clock64() - t0 > PEER_WAIT_CYCLES) {
+        if (p.err) atomicExch(p.err, ERR_WAIT_TIMEOUT);
+        break;
+      }
+    }
+  }
+  rank_top32_vals<NW, MAXC>(v, p.rank_n, lists);
+}
+template <int NW, int MAXC>
+__device__ void rank_top32_vals(const float (&v)[MAXC], int n, u64* lists) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   u64 run = 0ull;  // 0 is below every real key
 #pragma unroll 1
   for (int c = 0; c < MAXC; ++c) {
@@ -1174,6 +1292,8 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
   [[maybe_unused]] int* trc = nullptr;
 #endif
   NKV_STAMP(trc, 48);
+  // peer exchange: this step's epoch (advanced only after every CTA read it)
+  const uint32_t xp_ep = p.xp_P ? ld_peer_u32(p.xp_sync) : 0u;
   // one-launch step: this launch's tag (the epoch load overlaps the prologue)
   uint32_t fs_tg = 0u;
   if constexpr (FS) {
@@ -1246,7 +1366,7 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
   }
   // block ids: read now unless they come from the grid this one overlaps
   long long id_early = 0;
-  if (!FS && !p.overlap && !p.rank_scores && tid < nslots) id_early = __ldg(p.ids + slot0 + tid);
+  if (!FS && !p.overlap && !p.rank_scores && !p.xp_P && tid < nslots) id_early = __ldg(p.ids + slot0 + tid);
   if (warp < 2) {  // np <= AT_MAX_SLOTS + 4 pieces live in warps 0 and 1
     const unsigned bits = __ballot_sync(FULL, by_threads);
     if (lane == 0) s_thr[warp] = bits;
@@ -1320,12 +1440,16 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
       }
     }
     if (tid == 0) fs_arrive(p);
-  } else if (p.rank_scores) {
+  } else if (p.rank_scores || p.xp_P) {
     // ranked mode: the CTAs that hold selected blocks (and CTA (0, 0), which
-    // publishes the ids) rank the block scores themselves
+    // publishes the ids) rank the block scores themselves (with a peer
+    // exchange: the max over ranks of the scores in the exchange buffer)
     if (nslots > 0 || (split == 0 && h == 0)) {
       __shared__ u64 s_rank[NW * 32];
-      rank_top32<NW, RANK_MAXC>(p.rank_scores, p.rank_n, s_rank);
+      if (p.xp_P)
+        rank_top32_peer<NW, RANK_MAXC>(p, xp_ep, s_rank);
+      else
+        rank_top32<NW, RANK_MAXC>(p.rank_scores, p.rank_n, s_rank);
       if (tid < nslots) s_ids[tid] = (long long)key_id(s_rank[slot0 + tid]);
       if (split == 0 && h == 0 && tid < p.n_sel) {
         p.rank_out[tid] = (long long)key_id(s_rank[tid]);
@@ -1548,7 +1672,8 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
   if (p.stop == 4) return;
 #endif
   if (p.cluster) {
-    combine_cluster<G>(p, h, pm, pl, po);  // begins with a cluster barrier
+    combine_cluster<G>(p, h, pm, pl, po, xp_ep);  // begins and ends with a cluster barrier
+    if (p.xp_P && split == 0) peer_pull_arrive<G>(p, h, xp_ep);
     NKV_STAMP(trc, 57);
     return;
   }
@@ -1559,7 +1684,8 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
   if (s_ticket != (unsigned)p.splits - 1) return;
   __threadfence();
   if (tid == 0) p.counters[h] = 0u;
-  combine_splits<G>(p, h, reinterpret_cast<float*>(kt));
+  combine_splits<G>(p, h, reinterpret_cast<float*>(kt), xp_ep);
+  if (p.xp_P) peer_pull_arrive<G>(p, h, xp_ep);
 }
 
 // Cluster merge: the CTAs of one cluster are the splits of one KV head.  After
@@ -1569,7 +1695,7 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
 // outputs, then the weights exp(m_q - M) travel by shuffle.  A second barrier
 // keeps every CTA's shared memory alive until its peers are done reading.
 template <int G>
-__device__ void combine_cluster(const AttendParams& p, int h, float* pm, float* pl, float* po) {
+__device__ void combine_cluster(const AttendParams& p, int h, float* pm, float* pl, float* po, uint32_t xp_ep) {
   cg::cluster_group cluster = cg::this_cluster();
   const int C = (int)cluster.num_blocks();
   const int rank = (int)cluster.block_rank();
@@ -1602,7 +1728,14 @@ __device__ void combine_cluster(const AttendParams& p, int h, float* pm, float* 
     for (int q = 0; q < AT_CLUSTER_MAX; ++q) acc = fmaf(__shfl_sync(FULL, w, q), v[q], acc);
     const int qn = row / G, g = row % G;
     const long long oo = qn * p.out_row + (long long)(h * G + g) * p.out_head + d;
-    if (NKV_INB(p.err, 43, oo, 1, p.ext_out)) p.out[oo] = __float2bfloat16(acc * (1.f / L));
+    const float val = acc * (1.f / L);
+    if (NKV_INB(p.err, 43, oo, 1, p.ext_out)) p.out[oo] = __float2bfloat16(val);
+    if (p.xp_P) {  // peer exchange: dims (d, d + 1) of this row to every other rank
+      const float nxt = __shfl_down_sync(FULL, val, 1);
+      if (!(lane & 1))
+        peer_push(p, xp_ep, ((long long)(p.xp_rank * gridDim.y + h) * G + g) * (NKV_D / 2) + d / 2,
+                  pack_bf16x2(val, nxt));
+    }
   }
 #ifdef NKV_CHECKED
   NKV_STAMP(trc, 60);
@@ -1616,7 +1749,7 @@ __device__ void combine_cluster(const AttendParams& p, int h, float* pm, float* 
 // outputs are weighted sums of float4 partial rows, with the splits divided
 // between two threads per output when there are few rows.
 template <int G>
-__device__ void combine_splits(const AttendParams& p, int h, float* wbuf) {
+__device__ void combine_splits(const AttendParams& p, int h, float* wbuf, uint32_t xp_ep) {
   const int tid = threadIdx.x;
   const int nr = p.nr, S = p.splits;
   float* wm = wbuf;            // [nr][S]
@@ -1683,6 +1816,11 @@ __device__ void combine_splits(const AttendParams& p, int h, float* wbuf) {
         w.x = (uint32_t)f2bf(acc.x) | ((uint32_t)f2bf(acc.y) << 16);
         w.y = (uint32_t)f2bf(acc.z) | ((uint32_t)f2bf(acc.w) << 16);
         *reinterpret_cast<uint2*>(p.out + oo) = w;
+        if (p.xp_P) {  // peer exchange: the four dims to every other rank
+          const long long wi = ((long long)(p.xp_rank * gridDim.y + h) * G + g) * (NKV_D / 2) + d4 * 2;
+          peer_push(p, xp_ep, wi, w.x);
+          peer_push(p, xp_ep, wi + 1, w.y);
+        }
       }
     }
   }
@@ -1865,10 +2003,12 @@ extern "C" size_t nkv_attend_workspace_bytes(int hkv, int hq, int nq, int max_to
 }
 
 struct RankArgs {
-  const float* scores;  // ranked mode: block scores of a scoring grid; null: one-launch step
+  const float* scores;  // ranked mode: block scores of a scoring grid; null: one-launch step or peer exchange
   int nblocks;
   int64_t* out_ids;
   float* out_scores;
+  const PeerArgs* peer;  // KV-head sharding over peer memory (scores from the exchange)
+  void* out_full;        // with peer: this rank's full-width output
   // one-launch step: the attention grid scores the blocks itself
   const void* reps;
   int r, reps_blocks;
@@ -1886,12 +2026,23 @@ extern "C" int nkv_attend(nkv_stream_t stream, const nkv_attend_args* a) {
 
 namespace nkv {
 int attend_ranked(nkv_stream_t stream, const nkv_attend_args* a, const float* scores, int nblocks,
-                  int64_t* out_ids, float* out_scores) {
-  NKV_REQUIRE(a && a->nq == 1 && scores && out_ids, "attend_ranked: needs one query, scores and out_ids");
+                  int64_t* out_ids, float* out_scores, const PeerArgs* peer, void* out_full) {
+  NKV_REQUIRE(a && a->nq == 1 && (scores || peer) && out_ids, "attend_ranked: needs one query, scores and out_ids");
+  if (peer) {
+    NKV_REQUIRE(peer->P >= 1 && peer->P <= NKV_MAX_PEERS && peer->rank >= 0 && peer->rank < peer->P && peer->exch &&
+                    nblocks <= peer->cap && peer->hq_all == a->hq * peer->P && out_full,
+                "attend_ranked: bad peer exchange (P=%d, rank=%d, cap=%d, hq_all=%d)", peer->P, peer->rank, peer->cap,
+                peer->hq_all);
+    NKV_REQUIRE((const char*)a->out == (const char*)out_full + (size_t)peer->rank * a->hq * NKV_D * 2 &&
+                    a->out_head_stride == NKV_D,
+                "attend_ranked: args->out must be this rank's rows of out_full");
+    for (int i = 0; i < peer->P; ++i)
+      NKV_REQUIRE(peer->exch[i] && ((uintptr_t)peer->exch[i] & 15) == 0, "attend_ranked: exchange %d missing", i);
+  }
   NKV_REQUIRE(a->n_sel >= 1 && a->n_sel <= 32 && a->n_sel <= nblocks, "attend_ranked: k=%d out of [1, 32]",
               a->n_sel);
   NKV_SUPPORTED(nblocks <= 8 * 32 * RANK_MAXC, "attend_ranked: %d blocks exceed the in-kernel ranking", nblocks);
-  RankArgs r{scores, nblocks, out_ids, out_scores, nullptr, 0, 0, nullptr, 0, nullptr};
+  RankArgs r{scores, nblocks, out_ids, out_scores, peer, out_full, nullptr, 0, 0, nullptr, 0, nullptr};
   return attend_impl(stream, a, &r);
 }
 
@@ -1909,7 +2060,7 @@ int attend_step(nkv_stream_t stream, const nkv_attend_args* a, const void* reps,
   NKV_REQUIRE(sel_ws_bytes >= nkv_select_workspace_bytes(reps_blocks, 1), "decode step: select workspace too small");
   if (g_fs_unavailable || a->n_sel > 32 || r < 1 || r > 4 || r == 3 || nblocks > FS_MAXE * NKV_DECODE_WARPS * 32)
     return FS_DECLINED;
-  RankArgs ra{nullptr, nblocks, out_ids, out_scores, reps, r, reps_blocks, prot, nprot, sel_ws};
+  RankArgs ra{nullptr, nblocks, out_ids, out_scores, nullptr, nullptr, reps, r, reps_blocks, prot, nprot, sel_ws};
   return attend_impl(stream, a, &ra);
 }
 }  // namespace nkv
@@ -2040,7 +2191,7 @@ static int attend_impl(nkv_stream_t stream, const nkv_attend_args* a, const Rank
   p.rank_n = rank ? rank->nblocks : 0;
   p.rank_out = rank ? (long long*)rank->out_ids : nullptr;
   p.rank_out_scores = rank ? rank->out_scores : nullptr;
-  const bool one_launch = rank && !rank->scores;
+  const bool one_launch = rank && !rank->scores && !rank->peer;
   p.fs_reps = one_launch ? (const __nv_bfloat16*)rank->reps : nullptr;
   p.fs_r = one_launch ? rank->r : 0;
   p.fs_reps_blocks = one_launch ? rank->reps_blocks : 0;
@@ -2050,6 +2201,23 @@ static int attend_impl(nkv_stream_t stream, const nkv_attend_args* a, const Rank
   p.fs_sync = one_launch ? (unsigned*)((char*)rank->sel_ws + 16) : nullptr;
   p.fs_bpc = 0;
   p.fs_prefetch = env_int("NKV_FS_PREFETCH", 1);
+  p.xp_P = 0;
+  p.xp_scores = nullptr;
+  p.xp_sync = nullptr;
+  p.xp_full = nullptr;
+  p.xp_rank = p.xp_cap = p.xp_hq = 0;
+  for (int i = 0; i < NKV_MAX_PEERS; ++i) p.xp_out[i] = nullptr;
+  if (rank && rank->peer) {
+    const PeerArgs& pa = *rank->peer;
+    p.xp_P = pa.P;
+    p.xp_rank = pa.rank;
+    p.xp_cap = pa.cap;
+    p.xp_hq = pa.hq_all;
+    p.xp_scores = (const u64*)((const char*)pa.exch[pa.rank] + peer_xs_offset());
+    p.xp_sync = (uint32_t*)pa.exch[pa.rank];
+    p.xp_full = (__nv_bfloat16*)rank->out_full;
+    for (int i = 0; i < pa.P; ++i) p.xp_out[i] = (u64*)((char*)pa.exch[i] + peer_xo_offset(pa.P, pa.cap));
+  }
   AttendParams pg = p;  // workspace-merge configuration (fallback)
   pg.cluster = 0;
   {

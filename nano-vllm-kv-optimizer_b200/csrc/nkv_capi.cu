@@ -3,6 +3,7 @@
 #include <stdarg.h>
 #include <stdlib.h>
 #include <stdio.h>
+#include <string.h>
 
 #include <atomic>
 
@@ -145,4 +146,85 @@ extern "C" int nkv_attend_ranked(nkv_stream_t stream, const nkv_attend_args* a, 
                                  int64_t* out_ids, float* out_scores) {
   NKV_REQUIRE(a && a->block_ids == out_ids, "attend_ranked: args->block_ids must be out_ids");
   return nkv::attend_ranked(stream, a, scores, nblocks, out_ids, out_scores);
+}
+
+// ---- KV-head sharding over peer memory ----------------------------------------------
+extern "C" size_t nkv_shard_exchange_bytes(int n_ranks, int max_blocks, int hq_all) {
+  if (n_ranks < 1) n_ranks = 1;
+  if (max_blocks < 1) max_blocks = 1;
+  if (hq_all < 1) hq_all = 1;
+  return nkv::peer_exchange_bytes(n_ranks, max_blocks, hq_all);
+}
+
+extern "C" int nkv_peer_alloc(size_t bytes, void** dptr, void* ipc_handle) {
+  NKV_REQUIRE(dptr && ipc_handle && bytes > 0, "peer_alloc: bad arguments");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    if (p) cudaFree(p);
+    nkv::set_error("peer_alloc: %s", cudaGetErrorString(e));
+    return NKV_ERR_CUDA;
+  }
+  memcpy(ipc_handle, &h, sizeof(h));
+  *dptr = p;
+  return NKV_OK;
+}
+
+extern "C" int nkv_peer_open(const void* ipc_handle, void** dptr) {
+  NKV_REQUIRE(ipc_handle && dptr, "peer_open: bad arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(dptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    nkv::set_error("peer_open: %s", cudaGetErrorString(e));
+    return NKV_ERR_CUDA;
+  }
+  return NKV_OK;
+}
+
+extern "C" int nkv_peer_close(void* dptr) {
+  NKV_REQUIRE(dptr, "peer_close: null pointer");
+  cudaError_t e = cudaIpcCloseMemHandle(dptr);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    nkv::set_error("peer_close: %s", cudaGetErrorString(e));
+    return NKV_ERR_CUDA;
+  }
+  return NKV_OK;
+}
+
+extern "C" int nkv_peer_free(void* dptr) {
+  NKV_REQUIRE(dptr, "peer_free: null pointer");
+  cudaError_t e = cudaFree(dptr);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    nkv::set_error("peer_free: %s", cudaGetErrorString(e));
+    return NKV_ERR_CUDA;
+  }
+  return NKV_OK;
+}
+
+extern "C" int nkv_shard_scores(nkv_stream_t stream, const void* q, int64_t q_row_stride, int64_t q_head_stride,
+                                int hq, int hkv, int head_dim, const void* reps, int r, int max_blocks, int nblocks,
+                                const int32_t* protected_ids, int n_protected, void* const* exchanges, int n_ranks,
+                                int rank, void* workspace, size_t workspace_bytes) {
+  NKV_REQUIRE(exchanges, "shard_scores: null exchanges");
+  const nkv::PeerArgs pa{exchanges, n_ranks, rank, max_blocks, hq * n_ranks};
+  const float* ws_scores = nullptr;
+  return nkv::select_scores((cudaStream_t)stream, q, q_row_stride, q_head_stride, hq, hkv, head_dim, reps, r,
+                            max_blocks, nblocks, protected_ids, n_protected, 1, workspace, workspace_bytes, &ws_scores,
+                            nullptr, &pa);
+}
+
+extern "C" int nkv_shard_attend(nkv_stream_t stream, const nkv_attend_args* a, void* const* exchanges, int n_ranks,
+                                int rank, int max_blocks, int nblocks, int64_t* out_ids, float* out_scores,
+                                void* out_full) {
+  NKV_REQUIRE(a && exchanges && a->block_ids == out_ids, "shard_attend: args->block_ids must be out_ids");
+  const nkv::PeerArgs pa{exchanges, n_ranks, rank, max_blocks, a->hq * n_ranks};
+  return nkv::attend_ranked(stream, a, nullptr, nblocks, out_ids, out_scores, &pa, out_full);
 }

@@ -92,6 +92,26 @@ __device__ __forceinline__ uint32_t f32_order(float f) {
 __device__ __forceinline__ float f32_unorder(uint32_t u) {
   return __uint_as_float((u & 0x80000000u) ? (u & 0x7fffffffu) : ~u);
 }
+// Words exchanged with peer GPUs through their memory (KV-head sharding): a
+// 64-bit word carries a 32-bit payload and a 32-bit tag of the step that wrote
+// it, so one 8-byte store is both data and flag (a reader polls until the tag
+// is the current one).  Volatile accesses: no caching in L1 on either side.
+__device__ __forceinline__ void st_peer_u64(u64* a, u64 v) {
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
+}
+__device__ __forceinline__ u64 ld_peer_u64(const u64* a) {
+  u64 v;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_peer_u32(const uint32_t* a) {
+  uint32_t v;
+  asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+  return v;
+}
+// Tag of the step with epoch e: never 0, so zeroed memory holds no valid word.
+__device__ __forceinline__ uint32_t step_tag(uint32_t e) { return e % 0xfffffffeu + 1u; }
+
 __device__ __forceinline__ u64 make_key(float score, uint32_t id) {
   return ((u64)f32_order(score) << 32) | (u64)(0xffffffffu - id);
 }

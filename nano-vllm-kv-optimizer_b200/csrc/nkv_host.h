@@ -10,6 +10,8 @@
 
 namespace nkv {
 
+constexpr int NKV_MAX_PEERS = 8;  // ranks of a KV-head-sharded layer exchanging through peer memory
+
 void set_error(const char* fmt, ...);
 
 // Integer tuning knob from the environment (NKV_*): `dflt` when unset or
@@ -89,15 +91,34 @@ inline int ensure_nonportable_cluster(Kernel kernel, const char* what) {
 // protected-masked block scores into the select workspace (and to
 // out_block_scores when given) and returns the workspace copy's address (the
 // grid signals programmatic dependents at its start).
+// KV-head sharding over peer memory: the P ranks' exchange buffers (one per
+// layer and rank, each readable and writable by every rank), laid out as
+//   [0, 256)  epoch (u32), ticket (u32) of this rank
+//   xs        [2 parities][P ranks][cap blocks] u64 tagged block scores
+//   xo        [2 parities][hq_all * D / 2] u64 tagged bf16 output pairs
+// A step writes the parity and tag of its epoch; the attention grid advances
+// the epoch once every one of its readers is done.
+struct PeerArgs {
+  void* const* exch;  // P device pointers, index = rank
+  int P, rank;
+  int cap;     // block capacity of the score area
+  int hq_all;  // query heads over all ranks
+};
+inline size_t peer_xs_offset() { return 256; }
+inline size_t peer_xo_offset(int P, int cap) { return 256 + (size_t)2 * P * cap * 8; }
+inline size_t peer_exchange_bytes(int P, int cap, int hq_all) {
+  return peer_xo_offset(P, cap) + (size_t)2 * hq_all * 64 * 8;  // head_dim 128: 64 pairs per row
+}
+
 int select_scores(cudaStream_t st, const void* q, int64_t q_row_stride, int64_t q_head_stride, int hq, int hkv,
                   int head_dim, const void* reps, int r, int max_blocks, int nblocks, const int32_t* protected_ids,
                   int n_protected, int k, void* workspace, size_t workspace_bytes, const float** scores,
-                  float* out_block_scores);
+                  float* out_block_scores, const PeerArgs* peer = nullptr);
 // attend_ranked: nkv_attend for one query whose CTAs rank the block scores of
 // a preceding select_scores themselves (top args->n_sel), after waiting for it.
 // The ranked ids (and scores, when out_scores != NULL) are written to out_ids.
 int attend_ranked(nkv_stream_t stream, const nkv_attend_args* args, const float* scores, int nblocks,
-                  int64_t* out_ids, float* out_scores);
+                  int64_t* out_ids, float* out_scores, const PeerArgs* peer = nullptr, void* out_full = nullptr);
 // attend_step: the whole decode step (scoring of every block, protection,
 // top args->n_sel selection, attention) as one cooperative cluster launch.
 // The keys it publishes live in the select workspace, which must start at

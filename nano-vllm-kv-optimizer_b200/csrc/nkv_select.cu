@@ -49,6 +49,12 @@ struct SelectParams {
   int* err;
   long long ext_reps, ext_q;
   int* trace;  // checked builds: per-CTA phase stamps (or null)
+  // KV-head sharding over peer memory (xs_P > 0): every block score is also
+  // pushed, tagged with this step's epoch, into each rank's exchange buffer at
+  // xs_peer[r] + (parity * xs_P + xs_rank) * xs_cap + block
+  u64* xs_peer[NKV_MAX_PEERS];
+  int xs_P, xs_rank, xs_cap;
+  const uint32_t* xs_epoch;  // this rank's exchange header (epoch word)
 };
 
 // Score of one (head, block) unit for query row n (or max over rows when n < 0).
@@ -283,6 +289,12 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel(SelectParams p) {
         if ((bl0 + threadIdx.x < 256) ? s_prot[bl0 + threadIdx.x] : is_protected(p, b)) m = -INFINITY;
         p.scores[(long long)row * p.nblocks + b] = m;
         if (p.out_block_scores) p.out_block_scores[(long long)row * p.nblocks + b] = m;
+        if (p.xs_P) {
+          const uint32_t ep = ld_peer_u32(p.xs_epoch);
+          const u64 w = ((u64)step_tag(ep) << 32) | f32_order(m);
+          const long long at = ((long long)(ep & 1u) * p.xs_P + p.xs_rank) * p.xs_cap + b;
+          for (int r = 0; r < p.xs_P; ++r) st_peer_u64(p.xs_peer[r] + at, w);
+        }
       }
       __syncthreads();
     }
@@ -436,7 +448,7 @@ static int select_common(cudaStream_t st, const void* q, int nq, int64_t q_row_s
   NKV_REQUIRE(((uintptr_t)q & 15) == 0 && ((uintptr_t)reps & 15) == 0 && (q_head_stride % 8) == 0 &&
                   (q_row_stride % 8) == 0,
               "select: q/reps must be 16-byte aligned with strides multiple of 8 elements");
-  p = SelectParams{};
+  p = SelectParams{};  // (xs_P = 0: no peer exchange)
   p.q = (const __nv_bfloat16*)q;
   p.q_row_stride = q_row_stride;
   p.q_head_stride = q_head_stride;
@@ -490,12 +502,25 @@ namespace nkv {
 int select_scores(cudaStream_t st, const void* q, int64_t q_row_stride, int64_t q_head_stride, int hq, int hkv,
                   int head_dim, const void* reps, int r, int max_blocks, int nblocks, const int32_t* protected_ids,
                   int n_protected, int k, void* workspace, size_t workspace_bytes, const float** scores,
-                  float* out_block_scores) {
+                  float* out_block_scores, const PeerArgs* peer) {
   SelectParams p;
   int rc = select_common(st, q, 1, q_row_stride, q_head_stride, hq, hkv, head_dim, reps, r, max_blocks, nblocks,
                          protected_ids, n_protected, k, workspace, workspace_bytes, 0, p);
   if (rc) return rc;
   p.score_only = 1;
+  if (peer) {
+    NKV_REQUIRE(peer->P >= 1 && peer->P <= NKV_MAX_PEERS && peer->rank >= 0 && peer->rank < peer->P && peer->exch &&
+                    nblocks <= peer->cap,
+                "select_scores: bad peer exchange (P=%d, rank=%d, cap=%d)", peer->P, peer->rank, peer->cap);
+    p.xs_P = peer->P;
+    p.xs_rank = peer->rank;
+    p.xs_cap = peer->cap;
+    p.xs_epoch = (const uint32_t*)peer->exch[peer->rank];
+    for (int i = 0; i < peer->P; ++i) {
+      NKV_REQUIRE(peer->exch[i] && ((uintptr_t)peer->exch[i] & 15) == 0, "select_scores: exchange %d missing", i);
+      p.xs_peer[i] = (u64*)((char*)peer->exch[i] + peer_xs_offset());
+    }
+  }
   p.out_block_scores = out_block_scores;
   *scores = p.scores;
   return launch_select(st, p, hq / hkv);

@@ -991,6 +991,46 @@ class M12LayerRuntime:
              prot.data_ptr(), nprot, self._bscores.data_ptr(), ws.data_ptr(), ws.numel())
         return self._bscores[:nb]
 
+    def shard_scores(self, q: torch.Tensor, exchanges, n_ranks: int, rank: int) -> None:
+        """Scoring half of a KV-head-sharded decode step with the exchange in
+        the kernels: this layer's masked block scores go, tagged with the step,
+        into every rank's exchange buffer (``exchanges``: the ctypes array of
+        the ranks' buffers, nkv_shard_scores)."""
+        cfg = self.cfg
+        if q.ndim == 2:
+            q = q.unsqueeze(0)
+        q = _aligned(q)
+        nb = self.nblocks_filled
+        prot, nprot = self._protected_dev(nb)
+        ws = self._select_ws(1)
+        call("nkv_shard_scores", _stream(self.device), q.data_ptr(), q.stride(0), q.stride(1), cfg.num_heads,
+             cfg.num_kv_heads, cfg.head_dim, self.reps_gpu.data_ptr(), cfg.r, self.max_blocks, nb,
+             prot.data_ptr(), nprot, C.cast(exchanges, C.c_void_p), n_ranks, rank, ws.data_ptr(), ws.numel())
+
+    def decode_shard(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, exchanges, n_ranks: int, rank: int,
+                     out_full: torch.Tensor) -> torch.Tensor:
+        """The rest of a KV-head-sharded decode step after shard_scores on
+        every rank: ranks the max over ranks of the exchanged scores, attends
+        this layer's heads, writes their rows of ``out_full`` [1, Hq_all, D]
+        and exchanges rows with the other ranks inside the kernel
+        (nkv_shard_attend); returns ``out_full``."""
+        cfg = self.cfg
+        assert q.shape[0] == 1 and k.shape[0] == 1
+        assert out_full.is_contiguous() and out_full.shape[-2] == cfg.num_heads * n_ranks
+        kk = self._budget(self._decode_requested)
+        d, _, head_new = self._decode_fill(q, k, v, kk)
+        a = _lib.AttendArgs.from_buffer_copy(d.attend)
+        a.out = out_full.data_ptr() + rank * cfg.num_heads * cfg.head_dim * 2
+        a.out_row_stride, a.out_head_stride = cfg.num_heads * n_ranks * cfg.head_dim, cfg.head_dim
+        a.block_ids, a.n_sel, a.overlap_select = self._ids.data_ptr(), kk, 1
+        call("nkv_shard_attend", _stream(self.device), C.byref(a), C.cast(exchanges, C.c_void_p), n_ranks, rank,
+             self.max_blocks, self.nblocks_filled, self._ids.data_ptr(), self._topk_scores.data_ptr(),
+             out_full.data_ptr())
+        self._ring_head = head_new
+        self.valid_len += 1
+        self._last_ids_dev, self._last_ids_host = self._ids_view, None
+        return out_full
+
     def decode_ranked(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                       scores: torch.Tensor) -> torch.Tensor:
         """The rest of a decode step given the block scores of every KV head

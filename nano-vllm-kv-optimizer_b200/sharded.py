@@ -1,18 +1,29 @@
 """KV-head sharding of the sparse path over the GPUs of one node.
 
-Each rank of a ``torch.distributed`` process group (one GPU per rank, NCCL)
-holds the history, representatives, sink and recent window of its share of
-the KV heads (rank i owns KV heads [i*Hkv/P, (i+1)*Hkv/P) and their query
-heads) and runs the per-layer kernels on them.  A decode step exchanges two
-things over NVLink:
+Each rank of a ``torch.distributed`` process group (one GPU per rank) holds
+the history, representatives, sink and recent window of its share of the KV
+heads (rank i owns KV heads [i*Hkv/P, (i+1)*Hkv/P) and their query heads) and
+runs the per-layer kernels on them.  A decode step exchanges two things over
+NVLink:
 
 1. block selection is global in the reference: a block's score is the maximum
    over every query head (m12_runtime.py:999-1003).  Each rank scores its own
-   heads; one MAX all-reduce of the fp32 block scores ([nblocks], 2 KB at 32K)
-   gives every rank the global scores, from which its attention kernel ranks
-   the same Top-K as a single GPU would;
-2. the per-rank attention outputs [1, Hq/P, D] are all-gathered into
-   [1, Hq, D] (the all-gather before o_proj).
+   heads; the maximum over ranks of the fp32 block scores gives every rank the
+   global scores, from which its attention kernel ranks the same Top-K as a
+   single GPU would;
+2. the per-rank attention outputs [1, Hq/P, D] are gathered into [1, Hq, D]
+   (the all-gather before o_proj).
+
+Two forms of the exchange:
+
+- ``exchange="peer"`` (the default where every pair of GPUs has peer access):
+  inside the kernels, through per-layer exchange buffers that every rank maps
+  (CUDA IPC).  The scoring kernel writes its scores as step-tagged 8-byte words
+  into every rank's buffer; the attention kernel polls them, ranks the max,
+  attends, pushes its output rows to the other ranks the same way and pulls
+  theirs before it ends.  No collective library call on the data path.
+- ``exchange="nccl"``: a MAX all-reduce of the scores ([nblocks], 2 KB at 32K)
+  and an all-gather of the outputs (NCCL), around the same two kernels.
 
 Prefill needs no exchange for the store (each rank stores its heads' K/V);
 the segmented prefill attention of a later chunk selects with query segment
@@ -20,11 +31,13 @@ means whose scores reduce the same way.
 """
 from __future__ import annotations
 
+import ctypes as C
 import dataclasses
 
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from .m12_runtime import M12Config, M12LayerRuntime
 
 
@@ -36,7 +49,9 @@ class KVHeadShardedLayer:
     ``_store_kv``, ``block_scores_dev`` and ``decode_ranked``.
     """
 
-    def __init__(self, layer_id: int, cfg: M12Config, group=None, runtime_factory=None):
+    def __init__(self, layer_id: int, cfg: M12Config, group=None, runtime_factory=None, exchange: str = "auto"):
+        if exchange not in ("auto", "peer", "nccl"):
+            raise ValueError(f"exchange must be 'auto', 'peer' or 'nccl', not {exchange!r}")
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -49,6 +64,11 @@ class KVHeadShardedLayer:
         self.cfg = cfg
         self.local_cfg = dataclasses.replace(cfg, num_heads=self.hq, num_kv_heads=self.hkv)
         self.rt = (runtime_factory or M12LayerRuntime)(layer_id, self.local_cfg)
+        self.exchange = "nccl" if (self.world == 1 or exchange == "nccl" or runtime_factory is not None) else exchange
+        self._exch = None      # ctypes array of the ranks' exchange buffers (peer form)
+        self._exch_cap = 0     # block capacity they were made for
+        self._own = None       # this rank's buffer
+        self._opened = []      # the peers' buffers opened here
 
     # this rank's heads of full-width tensors [T, heads, D]
     def _kv(self, x: torch.Tensor) -> torch.Tensor:
@@ -72,10 +92,70 @@ class KVHeadShardedLayer:
         """Append a chunk of history (the store half of prefill)."""
         self.rt._store_kv(self._kv(k), self._kv(v))
 
+    # ---- peer exchange buffers (collective: every rank calls at the same point) ----
+    def _peer_ok(self) -> bool:
+        """Whether every rank's GPU can access every other's memory."""
+        dev = torch.cuda.current_device() if self.rt.device.index is None else self.rt.device.index
+        devs = [None] * self.world
+        dist.all_gather_object(devs, dev, group=self.group)
+        ok = all(a == b or torch.cuda.can_device_access_peer(dev, b) for a in [dev] for b in devs)
+        oks = [None] * self.world
+        dist.all_gather_object(oks, bool(ok), group=self.group)
+        return all(oks)
+
+    def _ensure_exchange(self) -> None:
+        cap = self.rt.max_blocks
+        if self._exch is not None and cap <= self._exch_cap:
+            return
+        if self.exchange == "auto":
+            self.exchange = "peer" if self._peer_ok() else "nccl"
+            if self.exchange == "nccl":
+                return
+        self.close()
+        lib = _lib.load()
+        nbytes = lib.nkv_shard_exchange_bytes(self.world, cap, self.cfg.num_heads)
+        own = C.c_void_p()
+        handle = C.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+        _lib.call("nkv_peer_alloc", nbytes, C.byref(own), handle)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=self.group)
+        ptrs = (C.c_void_p * self.world)()
+        for r, hb in enumerate(handles):
+            if r == self.rank:
+                ptrs[r] = own.value
+                continue
+            p = C.c_void_p()
+            _lib.call("nkv_peer_open", C.create_string_buffer(hb, _lib.IPC_HANDLE_BYTES), C.byref(p))
+            ptrs[r] = p.value
+            self._opened.append(p.value)
+        self._own, self._exch, self._exch_cap = own.value, ptrs, cap
+        # no rank writes into a peer's buffer before every rank has opened it
+        dist.barrier(group=self.group)
+
+    def close(self) -> None:
+        """Release the peer exchange buffers (collective where they exist)."""
+        if self._exch is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)  # no peer still writes into them
+        lib = _lib.load()
+        for p in self._opened:
+            lib.nkv_peer_close(C.c_void_p(p))
+        if self._own:
+            lib.nkv_peer_free(C.c_void_p(self._own))
+        self._exch, self._own, self._opened, self._exch_cap = None, None, [], 0
+
     def decode(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, device=None) -> torch.Tensor:
         """One decode step for full-width q [1, Hq, D], k/v [1, Hkv, D] (every
         rank gets the same inputs, as with a replicated model); returns the
         full-width output [1, Hq, D] on every rank."""
+        if self.world > 1 and self.exchange != "nccl":
+            self._ensure_exchange()
+        if self.world > 1 and self.exchange == "peer":
+            out = torch.empty(1, self.cfg.num_heads, self.cfg.head_dim, dtype=q.dtype, device=q.device)
+            self.rt.shard_scores(self._q(q), self._exch, self.world, self.rank)
+            return self.rt.decode_shard(self._q(q), self._kv(k), self._kv(v), self._exch, self.world, self.rank,
+                                        out)
         scores = self.rt.block_scores_dev(self._q(q))
         if self.world > 1:
             dist.all_reduce(scores, op=dist.ReduceOp.MAX, group=self.group)
