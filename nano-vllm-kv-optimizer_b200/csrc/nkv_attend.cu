@@ -797,86 +797,6 @@ __device__ __forceinline__ void issue_piece(const DecodeMaps& tm, int src, int y
   }
 }
 
-// Top 32 of n fp32 block scores, ranked by the keys of nkv_select (score
-// descending, then block id ascending): each of the NW warps sorts its
-// 32-score chunks (bitonic, 64-bit keys) into a running list, skipping chunks
-// that cannot enter it, then the warp lists merge pairwise.  Returns with
-// lists[0..31] = ranks 0..31 (all threads must call).  n <= NW * 32 * MAXC.
-template <int NW, int MAXC>
-__device__ void rank_top32_vals(const float (&v)[MAXC], int n, u64* lists);
-template <int NW, int MAXC>
-__device__ void rank_top32(const float* __restrict__ scores, int n, u64* lists) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float v[MAXC];
-#pragma unroll
-  for (int c = 0; c < MAXC; ++c) {
-    const int i = (warp + c * NW) * 32 + lane;
-    v[c] = i < n ? __ldcg(scores + i) : -INFINITY;
-  }
-  rank_top32_vals<NW, MAXC>(v, n, lists);
-}
-// rank_top32 over the max across ranks of the tagged scores in this rank's
-// exchange buffer: every (rank, block) word of the thread is loaded, then the
-// ones not yet carrying this step's tag are polled again (bounded, then
-// ERR_WAIT_TIMEOUT and the stale value).
-template <int NW, int MAXC>
-__device__ void rank_top32_peer(const AttendParams& p, uint32_t ep, u64* lists) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint32_t tag = step_tag(ep);
-  const u64* xs = p.xp_scores + (long long)(ep & 1u) * p.xp_P * p.xp_cap;
-  float v[MAXC];
-#pragma unroll
-  for (int c = 0; c < MAXC; ++c) v[c] = -INFINITY;
-  for (int r = 0; r < p.xp_P; ++r) {
-    unsigned pending = 0u;
-#pragma unroll
-    for (int c = 0; c < MAXC; ++c)
-      if ((warp + c * NW) * 32 + lane < p.rank_n) pending |= 1u << c;
-    const long long t0 = clock64();
-    while (pending) {
-#pragma unroll
-      for (int c = 0; c < MAXC; ++c) {
-        if (!((pending >> c) & 1u)) continue;
-        const u64 w = ld_peer_u64(xs + (long long)r * p.xp_cap + (warp + c * NW) * 32 + lane);
-        if ((uint32_t)(w >> 32) == tag) {
-          v[c] = fmaxf(v[c], f32_unorder((uint32_t)w));
-          pending &= ~(1u << c);
-        }
-      }
-      if (pending && clock64() - t0 > PEER_WAIT_CYCLES) {
-        if (p.err) atomicExch(p.err, ERR_WAIT_TIMEOUT);
-        break;
-      }
-    }
-  }
-  rank_top32_vals<NW, MAXC>(v, p.rank_n, lists);
-}
-template <int NW, int MAXC>
-__device__ void rank_top32_vals(const float (&v)[MAXC], int n, u64* lists) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  u64 run = 0ull;  // 0 is below every real key
-#pragma unroll 1
-  for (int c = 0; c < MAXC; ++c) {
-    const int base = (warp + c * NW) * 32;
-    if (base >= n) break;
-    const int i = base + lane;
-    float x = v[0];
-#pragma unroll
-    for (int cc = 1; cc < MAXC; ++cc) x = cc == c ? v[cc] : x;
-    const u64 key = i < n ? make_key(x, (uint32_t)i) : 0ull;
-    const uint32_t run_min = (uint32_t)(shfl64(run, 31) >> 32);
-    if (__reduce_max_sync(FULL, (uint32_t)(key >> 32)) >= run_min) run = warp_merge_desc(run, warp_sort_desc(key));
-  }
-  lists[warp * 32 + lane] = run;
-  __syncthreads();
-#pragma unroll
-  for (int st = 1; st < NW; st <<= 1) {
-    if ((warp % (2 * st)) == 0 && warp + st < NW)
-      lists[warp * 32 + lane] = warp_merge_desc(lists[warp * 32 + lane], lists[(warp + st) * 32 + lane]);
-    __syncthreads();
-  }
-}
-constexpr int RANK_MAXC = 8;  // ranked decode: nblocks <= 8 warps x 32 x 8 = 2048
 
 // ---------------------------------------------------------------------------
 // One-launch decode step: scoring and selection inside the attention grid.
@@ -992,53 +912,26 @@ __device__ void fs_score_publish(const AttendParams& p, int cta, uint32_t tag, u
 
 constexpr int FS_CAND_MAX = 256;  // candidates ranked by counting (more: extraction rounds)
 
-// Top n_sel of the rank_n published keys, in rank order (score descending,
-// then block id ascending: nkv_select's order), into s_sel as make_key keys.
-// Thread t holds keys t, t + NT, ...: it polls them until they carry `tag`
-// (bounded: ~0.2 s of SM clock, then ERR_WAIT_TIMEOUT).
+// Top k (<= 32) of n orderable 32-bit scores (f32_order) held in registers,
+// in rank order (score descending, then block id ascending: nkv_select's
+// order), into s_sel[0, k) as make_key keys.  Thread t holds the scores of
+// blocks t, t + NT, ... in u[0], u[1], ... (bit e of `live`: u[e] is a block).
 //  1. threshold: every warp finds its 4th largest distinct score (4 warp max
 //     reductions); theta = the smallest over the warps, so at least 4 x NW
-//     keys score >= theta and the top n_sel (<= 32) are among them (theta = 0,
-//     every key, when fewer than n_sel keys can be guaranteed that way);
+//     keys score >= theta and the top k (<= 32) are among them (theta = 0,
+//     every key, when fewer than k keys can be guaranteed that way);
 //  2. the keys >= theta are compacted into shared memory (warp ballots);
 //  3. each candidate's rank = the number of larger candidate keys; ranks below
-//     n_sel land in s_sel[rank].
-// With more than FS_CAND_MAX candidates (flat or tied scores) the top n_sel
-// are extracted one per round (block-wide max of the remaining keys) instead.
-// All threads of the CTA must call.
+//     k land in s_sel[rank].
+// With more than FS_CAND_MAX candidates (flat or tied scores) the top k are
+// extracted one per round (block-wide max of the remaining keys) instead.
+// All threads of the CTA must call; s_sel is valid after the call.
 template <int NW>
-__device__ void fs_select(const AttendParams& p, uint32_t tag, u64* s_sel, u64* s_cand, unsigned* s_misc,
-                          [[maybe_unused]] int* trc) {
+__device__ void topk_threshold(const uint32_t (&u)[FS_MAXE], unsigned live, int n, int k, u64* s_sel,
+                               u64* s_cand, unsigned* s_misc, [[maybe_unused]] int* trc) {
   constexpr int NT = NW * 32;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int n = p.rank_n, k = p.n_sel;
   const int E = (n + NT - 1) / NT;
-  uint32_t u[FS_MAXE];
-  unsigned live = 0;
-#pragma unroll
-  for (int e = 0; e < FS_MAXE; ++e) {
-    u[e] = 0u;
-    if (e < E && tid + e * NT < n) live |= 1u << e;
-  }
-  unsigned pending = live;
-  const long long t_start = clock64();
-  while (pending) {
-#pragma unroll
-    for (int e = 0; e < FS_MAXE; ++e) {
-      if ((pending >> e) & 1u) {
-        const unsigned long long v = ld_relaxed_u64(p.fs_keys + tid + e * NT);
-        if ((uint32_t)(v >> 32) == tag) {
-          u[e] = (uint32_t)v;
-          pending &= ~(1u << e);
-        }
-      }
-    }
-    if (pending && clock64() - t_start > 400000000ll) {
-      if (p.err) atomicExch(p.err, ERR_WAIT_TIMEOUT);
-      break;
-    }
-  }
-  NKV_STAMP(trc, 40);
   // 1. per-warp 4th largest distinct score
   uint32_t prev = 0xffffffffu, th = 0u;
   bool more = true;
@@ -1139,6 +1032,109 @@ __device__ void fs_select(const AttendParams& p, uint32_t tag, u64* s_sel, u64* 
   }
   NKV_STAMP(trc, 41);
   __syncthreads();
+}
+
+// Top n_sel of the rank_n published keys, in rank order, into s_sel
+// (topk_threshold).  Thread t holds keys t, t + NT, ...: it polls them until
+// they carry `tag` (bounded: ~0.2 s of SM clock, then ERR_WAIT_TIMEOUT).
+// All threads of the CTA must call.
+template <int NW>
+__device__ void fs_select(const AttendParams& p, uint32_t tag, u64* s_sel, u64* s_cand, unsigned* s_misc,
+                          [[maybe_unused]] int* trc) {
+  constexpr int NT = NW * 32;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n = p.rank_n, k = p.n_sel;
+  const int E = (n + NT - 1) / NT;
+  uint32_t u[FS_MAXE];
+  unsigned live = 0;
+#pragma unroll
+  for (int e = 0; e < FS_MAXE; ++e) {
+    u[e] = 0u;
+    if (e < E && tid + e * NT < n) live |= 1u << e;
+  }
+  unsigned pending = live;
+  const long long t_start = clock64();
+  while (pending) {
+#pragma unroll
+    for (int e = 0; e < FS_MAXE; ++e) {
+      if ((pending >> e) & 1u) {
+        const unsigned long long v = ld_relaxed_u64(p.fs_keys + tid + e * NT);
+        if ((uint32_t)(v >> 32) == tag) {
+          u[e] = (uint32_t)v;
+          pending &= ~(1u << e);
+        }
+      }
+    }
+    if (pending && clock64() - t_start > 400000000ll) {
+      if (p.err) atomicExch(p.err, ERR_WAIT_TIMEOUT);
+      break;
+    }
+  }
+  NKV_STAMP(trc, 40);
+  topk_threshold<NW>(u, live, n, k, s_sel, s_cand, s_misc, trc);
+}
+
+// Ranked decode: the top k (<= 32) of the n fp32 block scores written by the
+// scoring grid, into s_sel (topk_threshold).  All threads of the CTA must call.
+template <int NW>
+__device__ void rank_topk(const float* __restrict__ scores, int n, int k, u64* s_sel, u64* s_cand,
+                          unsigned* s_misc, int* trc) {
+  constexpr int NT = NW * 32;
+  const int tid = threadIdx.x;
+  uint32_t u[FS_MAXE];
+  unsigned live = 0u;
+#pragma unroll
+  for (int e = 0; e < FS_MAXE; ++e) {
+    const int i = tid + e * NT;
+    u[e] = 0u;
+    if (i < n) {
+      u[e] = f32_order(__ldcg(scores + i));
+      live |= 1u << e;
+    }
+  }
+  topk_threshold<NW>(u, live, n, k, s_sel, s_cand, s_misc, trc);
+}
+// rank_topk over the max across ranks of the tagged scores in this rank's
+// exchange buffer: every (rank, block) word of the thread is loaded, then the
+// ones not yet carrying this step's tag are polled again (bounded, then
+// ERR_WAIT_TIMEOUT and the stale value).
+template <int NW>
+__device__ void rank_topk_peer(const AttendParams& p, uint32_t ep, u64* s_sel, u64* s_cand, unsigned* s_misc,
+                               int* trc) {
+  constexpr int NT = NW * 32;
+  const int tid = threadIdx.x;
+  const uint32_t tag = step_tag(ep);
+  const u64* xs = p.xp_scores + (long long)(ep & 1u) * p.xp_P * p.xp_cap;
+  float v[FS_MAXE];
+  unsigned live = 0u;
+#pragma unroll
+  for (int e = 0; e < FS_MAXE; ++e) {
+    v[e] = -INFINITY;
+    if (tid + e * NT < p.rank_n) live |= 1u << e;
+  }
+  for (int r = 0; r < p.xp_P; ++r) {
+    unsigned pending = live;
+    const long long t0 = clock64();
+    while (pending) {
+#pragma unroll
+      for (int e = 0; e < FS_MAXE; ++e) {
+        if (!((pending >> e) & 1u)) continue;
+        const u64 w = ld_peer_u64(xs + (long long)r * p.xp_cap + tid + e * NT);
+        if ((uint32_t)(w >> 32) == tag) {
+          v[e] = fmaxf(v[e], f32_unorder((uint32_t)w));
+          pending &= ~(1u << e);
+        }
+      }
+      if (pending && clock64() - t0 > PEER_WAIT_CYCLES) {
+        if (p.err) atomicExch(p.err, ERR_WAIT_TIMEOUT);
+        break;
+      }
+    }
+  }
+  uint32_t u[FS_MAXE];
+#pragma unroll
+  for (int e = 0; e < FS_MAXE; ++e) u[e] = ((live >> e) & 1u) ? f32_order(v[e]) : 0u;
+  topk_threshold<NW>(u, live, p.rank_n, p.n_sel, s_sel, s_cand, s_misc, trc);
 }
 
 // The launch is done with its keys once every CTA has arrived here: the last
@@ -1445,15 +1441,14 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
     // publishes the ids) rank the block scores themselves (with a peer
     // exchange: the max over ranks of the scores in the exchange buffer)
     if (nslots > 0 || (split == 0 && h == 0)) {
-      __shared__ u64 s_rank[NW * 32];
       if (p.xp_P)
-        rank_top32_peer<NW, RANK_MAXC>(p, xp_ep, s_rank);
+        rank_topk_peer<NW>(p, xp_ep, s_sel, s_cand, s_misc, trc);
       else
-        rank_top32<NW, RANK_MAXC>(p.rank_scores, p.rank_n, s_rank);
-      if (tid < nslots) s_ids[tid] = (long long)key_id(s_rank[slot0 + tid]);
+        rank_topk<NW>(p.rank_scores, p.rank_n, p.n_sel, s_sel, s_cand, s_misc, trc);
+      if (tid < nslots) s_ids[tid] = (long long)key_id(s_sel[slot0 + tid]);
       if (split == 0 && h == 0 && tid < p.n_sel) {
-        p.rank_out[tid] = (long long)key_id(s_rank[tid]);
-        if (p.rank_out_scores) p.rank_out_scores[tid] = key_score(s_rank[tid]);
+        p.rank_out[tid] = (long long)key_id(s_sel[tid]);
+        if (p.rank_out_scores) p.rank_out_scores[tid] = key_score(s_sel[tid]);
       }
     }
   } else if (tid < nslots) {
@@ -2041,7 +2036,8 @@ int attend_ranked(nkv_stream_t stream, const nkv_attend_args* a, const float* sc
   }
   NKV_REQUIRE(a->n_sel >= 1 && a->n_sel <= 32 && a->n_sel <= nblocks, "attend_ranked: k=%d out of [1, 32]",
               a->n_sel);
-  NKV_SUPPORTED(nblocks <= 8 * 32 * RANK_MAXC, "attend_ranked: %d blocks exceed the in-kernel ranking", nblocks);
+  NKV_SUPPORTED(nblocks <= FS_MAXE * NKV_DECODE_WARPS * 32, "attend_ranked: %d blocks exceed the in-kernel ranking",
+                nblocks);
   RankArgs r{scores, nblocks, out_ids, out_scores, peer, out_full, nullptr, 0, 0, nullptr, 0, nullptr};
   return attend_impl(stream, a, &r);
 }

@@ -384,12 +384,127 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel(SelectParams p) {
   if (threadIdx.x == 0) *p.out_count = U;
 }
 
+// Score-only form (the decode step's scoring grid, ranked by the attention
+// CTAs): a lighter grid of at most one 256-thread CTA per SM, so that the
+// attention CTAs launched after it (programmatic dependent launch) are
+// resident beside it and run their prologue while it scores.  CTA c owns
+// blocks [c * bpc, (c + 1) * bpc) for every KV head; warp w scores heads w,
+// w + 8, ...; per head the warp takes its blocks SC_UPW at a time with every
+// representative load of the group issued before the arithmetic (one DRAM
+// round trip per group).  Lane layout and summation order are unit_score's,
+// so the scores are bit-identical to select_kernel's.
+constexpr int SC_THREADS = 256;
+constexpr int SC_WARPS = SC_THREADS / 32;
+constexpr int SC_UPW = 4;       // (head, block) units per warp in flight
+constexpr int SC_BPC_MAX = 64;  // blocks per CTA
+
+template <int G>
+__global__ void __launch_bounds__(SC_THREADS) score_kernel(SelectParams p) {
+  __shared__ float part[SC_WARPS][SC_BPC_MAX];
+  __shared__ unsigned char s_prot[SC_BPC_MAX];
+  pdl_launch_dependents();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j = lane >> 3, c = lane & 7;
+  const int b0 = blockIdx.x * p.bpc;
+  const int nb = min(p.bpc, p.nblocks - b0);
+  for (int i = threadIdx.x; i < SC_WARPS * SC_BPC_MAX; i += SC_THREADS) (&part[0][0])[i] = -INFINITY;
+  for (int i = threadIdx.x; i < SC_BPC_MAX; i += SC_THREADS) s_prot[i] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < p.n_protected; i += SC_THREADS) {
+    const int b = __ldg(p.protected_ids + i) - b0;
+    if (b >= 0 && b < nb) s_prot[b] = 1;
+  }
+  const bool jvalid = j < p.r;
+  for (int h = warp; h < p.hkv; h += SC_WARPS) {
+    // this lane's 16-dim slice of the head's G query rows
+    uint4 qa[G], qb[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const __nv_bfloat16* qs = p.q + (long long)(h * G + g) * p.q_head_stride + c * 16;
+      if (!NKV_INB(p.err, 51, qs - p.q, 16, p.ext_q)) qs = p.q;
+      qa[g] = __ldg(reinterpret_cast<const uint4*>(qs));
+      qb[g] = __ldg(reinterpret_cast<const uint4*>(qs + 8));
+    }
+    for (int u0 = 0; u0 < nb; u0 += SC_UPW) {
+      uint4 ra[SC_UPW], rb[SC_UPW];
+#pragma unroll
+      for (int u = 0; u < SC_UPW; ++u) {
+        ra[u] = rb[u] = make_uint4(0u, 0u, 0u, 0u);
+        const long long off = (((long long)h * p.max_blocks + b0 + u0 + u) * p.r + j) * NKV_D + c * 16;
+        if (u0 + u < nb && jvalid && NKV_INB(p.err, 50, off, 16, p.ext_reps)) {
+          ra[u] = __ldg(reinterpret_cast<const uint4*>(p.reps + off));
+          rb[u] = __ldg(reinterpret_cast<const uint4*>(p.reps + off + 8));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < SC_UPW; ++u) {
+        float rv[16];
+        unpack8(ra[u], rv);
+        unpack8(rb[u], rv + 8);
+        float best = -INFINITY;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          float qv[16];
+          unpack8(qa[g], qv);
+          unpack8(qb[g], qv + 8);
+          float sc = 0.f;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) sc = fmaf(qv[i], rv[i], sc);
+          sc += __shfl_xor_sync(FULL, sc, 1);
+          sc += __shfl_xor_sync(FULL, sc, 2);
+          sc += __shfl_xor_sync(FULL, sc, 4);
+          if (jvalid) best = fmaxf(best, sc);
+        }
+        best = fmaxf(best, __shfl_xor_sync(FULL, best, 8));
+        best = fmaxf(best, __shfl_xor_sync(FULL, best, 16));
+        if (lane == 0 && u0 + u < nb) part[warp][u0 + u] = fmaxf(part[warp][u0 + u], best);
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < nb) {
+    const int b = b0 + threadIdx.x;
+    float m = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < SC_WARPS; ++w) m = fmaxf(m, part[w][threadIdx.x]);
+    if (s_prot[threadIdx.x]) m = -INFINITY;
+    p.scores[b] = m;
+    if (p.out_block_scores) p.out_block_scores[b] = m;
+    if (p.xs_P) {
+      const uint32_t ep = ld_peer_u32(p.xs_epoch);
+      const u64 w = ((u64)step_tag(ep) << 32) | f32_order(m);
+      const long long at = ((long long)(ep & 1u) * p.xs_P + p.xs_rank) * p.xs_cap + b;
+      for (int r = 0; r < p.xs_P; ++r) st_peer_u64(p.xs_peer[r] + at, w);
+    }
+  }
+}
+
 }  // namespace nkv
 
 using namespace nkv;
 
+static int launch_score(cudaStream_t st, SelectParams& p, int G) {
+  const int sms = sm_count();
+  const int per = (p.nblocks + sms - 1) / sms;
+  p.bpc = (per + SC_UPW - 1) / SC_UPW * SC_UPW;
+  const int grid = (p.nblocks + p.bpc - 1) / p.bpc;
+  switch (G) {
+    case 1: score_kernel<1><<<grid, SC_THREADS, 0, st>>>(p); break;
+    case 2: score_kernel<2><<<grid, SC_THREADS, 0, st>>>(p); break;
+    case 4: score_kernel<4><<<grid, SC_THREADS, 0, st>>>(p); break;
+    default:
+      set_error("score: unsupported G=%d", G);
+      return NKV_ERR_UNSUPPORTED;
+  }
+  return check_launch("score");
+}
+
 static int launch_select(cudaStream_t st, SelectParams& p, int G) {
   const int sms = sm_count();
+  // score-only, one query row, r <= 4, G <= 4: the lighter scoring grid
+  if (p.score_only && !p.per_query && p.nq == 1 && p.r <= 4 && G <= 4 &&
+      (p.nblocks + sms - 1) / sms <= SC_BPC_MAX && knob("NKV_SCORE_GRID", 1))
+    return launch_score(st, p, G);
   // one (head, block) unit per warp when the grid fits in one wave (<= 4 CTAs/SM)
   int bpc = (p.nblocks + 4 * sms - 1) / (4 * sms);
   const int unit_bpc = SEL_WARPS / (p.hkv < SEL_WARPS ? p.hkv : SEL_WARPS);
