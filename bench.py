@@ -306,6 +306,47 @@ def prefill_measure(nkv, dev, iters=5):
                          "frac": round(tf / peak, 4), "peak_kind": kind}}
 
 
+# kernel (5), store + representatives, per 4096-token chunk: read the chunk's
+# K and V, write them into the block store, write the blocks' r
+# representatives (+ int16 indices) and the last RECENT tokens into the ring
+ST_T = 4096
+ST_BYTES = (2 * ST_T * HKV * D * 2 + 2 * ST_T * HKV * D * 2 + (ST_T // B) * HKV * R_REPS * (D * 2 + 2)
+            + 2 * min(ST_T, RECENT) * HKV * D * 2)
+ST_ROT = 8  # distinct input chunks and store regions: 8 x 32 MiB > L2
+
+
+def store_measure(nkv, dev, iters=16):
+    """Kernel (5) on 4096-token chunks, rotating over ST_ROT inputs and store
+    regions (their bytes exceed L2, so every launch reads and writes HBM)."""
+    g = torch.Generator(device=dev).manual_seed(5151)
+    rt = nkv.M12LayerRuntime(0, nkv.M12Config(max_model_len=ST_ROT * ST_T + 4096, device=dev))
+    rt.reserve_blocks(ST_ROT * ST_T // B)
+    ks = [torch.randn(ST_T, HKV, D, generator=g, device=dev).bfloat16() for _ in range(ST_ROT)]
+    vs = [torch.randn(ST_T, HKV, D, generator=g, device=dev).bfloat16() for _ in range(ST_ROT)]
+    rt._store_kv(ks[0], vs[0])  # first chunk: store, sink and ring set up
+
+    def run(i):
+        j = i % ST_ROT
+        rt._launch_store(ks[j], vs[j], j * (ST_T // B), ring_pos0=0)
+    for i in range(ST_ROT):
+        run(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(iters):
+        run(i)
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / iters
+    peak, kind = peaks()
+    gbs = ST_BYTES / (us * 1e-6) / 1e9
+    del rt
+    return {"workload": "store + reps of a 4096-token chunk (bf16 block store, r=4), 8 rotating chunks > L2",
+            "us_per_chunk": round(us, 2), "bytes_per_chunk": ST_BYTES,
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "peak_kind": kind}}
+
+
 class Clocks:
     """nvidia-smi sampling during the timed region."""
 
@@ -401,6 +442,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true", help="skip the kernel (4) measurement")
     ap.add_argument("--no-offload", action="store_true", help="skip the host-offload decode measurement")
     ap.add_argument("--no-sharded", action="store_true", help="skip the KV-head-sharded measurement (N > 1)")
+    ap.add_argument("--store-only", action="store_true",
+                    help="run only the kernel (5) store measurement and print its record (profiling)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -434,6 +477,9 @@ def main():
         return
 
     nkv = __import__("importlib").import_module(PKG)
+    if args.store_only:
+        print(json.dumps({"store": store_measure(nkv, torch.device("cuda", 0))}))
+        return
     if world > 1:
         import torch.distributed as dist
         from datetime import timedelta
@@ -537,12 +583,32 @@ def main():
         host_us = (time.perf_counter() - h0) * 1e6 / (e2e_steps * L)  # host issue time per layer
         e1.record(stream)
         e1.synchronize()
+    e2e_eager_ms = e0.elapsed_time(e1) / e2e_steps
+    # the same end-to-end step through DecodeGraph: the per-step copies as
+    # above, the layers' decode replayed from one CUDA graph whose recent
+    # windows advance on the device with every replay
+    dg = nkv.DecodeGraph(layers, views, stream=stream)
+    with torch.cuda.stream(stream):
+        def e2e_graph_step():
+            xdev.copy_(hqkv, non_blocking=True)
+            ho.copy_(dg.replay(), non_blocking=True)
+        for _ in range(2):
+            e2e_graph_step()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        h0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            e2e_graph_step()
+        graph_host_us = (time.perf_counter() - h0) * 1e6 / (e2e_steps * L)
+        e1.record(stream)
+        e1.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
     if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
+        t = torch.tensor([e2e_ms, e2e_eager_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+        e2e_ms, e2e_eager_ms = float(t[0].item()), float(t[1].item())
     e2e_value = e2e_ms * 1000.0 / (L * world)
+    e2e_eager_value = e2e_eager_ms * 1000.0 / (L * world)
 
     line = None
     prefill = offload = sharded = None
@@ -553,6 +619,7 @@ def main():
             prefill = prefill_measure(nkv, dev)
     if rank == 0 and not args.no_offload:
         offload = offload_measure(nkv, dev)
+    store = store_measure(nkv, dev) if rank == 0 else None
     if rank == 0:
         # the CPU baseline is timed at N = 1 only (with N > 1 other ranks share the host)
         cpu_us, n_cpu = cpu_reference(args.cpu_steps, 3, threads) if world == 1 else (None, 0)
@@ -572,19 +639,25 @@ def main():
             "cpu_baseline": None if cpu_us is None else {
                 "value": round(cpu_us, 1), "unit": UNIT, "cores": threads, "kind": "port",
                 "sample": f"{n_cpu} decode calls of one 32K layer state (median)"},
-            "e2e": {"value": round(e2e_value, 4), "unit": UNIT, "host_us_per_layer": round(host_us, 2),
+            "e2e": {"value": round(e2e_value, 4), "unit": UNIT, "api": "DecodeGraph.replay (all layers)",
+                    "host_us_per_layer": round(graph_host_us, 2),
                     "h2d_bytes_per_step": L * (HQ + 2 * HKV) * D * 2,
                     "d2h_bytes_per_step": L * HQ * D * 2},
+            "e2e_eager": {"value": round(e2e_eager_value, 4), "unit": UNIT,
+                          "api": "M12LayerRuntime.decode per layer", "host_us_per_layer": round(host_us, 2),
+                          "h2d_bytes_per_step": L * (HQ + 2 * HKV) * D * 2,
+                          "d2h_bytes_per_step": L * HQ * D * 2},
             "gpu_launches": 2 * L * args.steps,
             "attend_launch": {"cluster": attend_cfg[0], "splits_per_head": attend_cfg[1],
                               "keys_per_cta": attend_cfg[2]},
             "clocks": clocks,
             "prefill": prefill,
             "offload": offload,
+            "store": store,
             "kv_head_sharded": sharded,
         }
         print(json.dumps(line))
-    del graph, g_att
+    del graph, g_att, dg
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

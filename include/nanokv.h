@@ -199,6 +199,18 @@ typedef struct {
   float* out_topk_scores; /* [k] or NULL */
   void* select_workspace;
   size_t select_workspace_bytes;
+  /* Optional device int32 [2], 8-byte aligned: {ring head, 0}.  NULL: the
+   * recent window is attend.ring_start / ring_len / ring_write_pos as given.
+   * Otherwise the step reads the head from the device instead of
+   * attend.ring_start / ring_write_pos (current token written at slot head,
+   * window = the ring_len slots after it) and advances it by one, so a CUDA
+   * graph of decode steps replays with the window moving on every replay.
+   * Needs a full window (ring_len == ring_cap - 1) and the two-launch form
+   * (the one-launch form and NKV_DECODE_FUSED=0 return NKV_ERR_UNSUPPORTED).
+   * Word 1 counts the CTAs that have read the head and must start at 0.
+   * Replaces the host-side shift of the recent window of
+   * M12LayerRuntime.decode (m12_runtime.py:1166-1172) for graph replay. */
+  int32_t* ring_head;
 } nkv_decode_args;
 int nkv_decode_step(nkv_stream_t stream, const nkv_decode_args* args);
 /* How the calling thread's last nkv_decode_step ran: 1 one launch, 2 a

@@ -16,9 +16,12 @@ from .m12_runtime import (
     prefill_query_summaries,
     prefill_recent_slice,
 )
+from .decode_graph import DecodeGraph, DeviceRingHeads
 from .sharded import KVHeadShardedLayer
 
 __all__ = [
+    "DecodeGraph",
+    "DeviceRingHeads",
     "KVHeadShardedLayer",
     "M12Config",
     "M12LayerRuntime",

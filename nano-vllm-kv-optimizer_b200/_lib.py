@@ -60,6 +60,7 @@ class DecodeArgs(C.Structure):
         ("protected_ids", c_vp), ("n_protected", c_int), ("k", c_int),
         ("out_ids", c_vp), ("out_topk_scores", c_vp),
         ("select_workspace", c_vp), ("select_workspace_bytes", C.c_size_t),
+        ("ring_head", c_vp),
     ]
 
 

@@ -98,6 +98,11 @@ struct AttendParams {
   // decode kernel, ranked mode: the CTAs rank these block scores (written by
   // the preceding scoring grid) themselves instead of reading ids
   const float* rank_scores;
+  // decode kernel, device-resident ring head (graph replay): ring_dyn[0] is
+  // the ring slot of logical recent slot 0 (the slot the current token is
+  // written to), ring_dyn[1] counts arriving CTAs; the last CTA to arrive
+  // advances the head.  Null: ring_start / ring_write_pos as given.
+  int* ring_dyn;
   int rank_n;
   long long* rank_out;     // the ranked ids, written by CTA (0, 0)
   float* rank_out_scores;  // their scores (optional)
@@ -812,6 +817,11 @@ __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long
   asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
   return v;
 }
+__device__ __forceinline__ int ld_acquire_s32(const int* a) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+  return v;
+}
 __device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned* a) {
   unsigned v;
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
@@ -1154,7 +1164,7 @@ __device__ __forceinline__ void fs_arrive(const AttendParams& p) {
 // V scale; token scheme: per-token bf16 scales).
 __device__ void thread_rows(const AttendParams& p, int h, int pos0, int len, int row0, unsigned char* kt,
                             unsigned char* vt, int NR, const long long* s_ids, int slot0, int selEnd, int sinkEnd,
-                            int ringEnd) {
+                            int ringEnd, int ring_start) {
   const int B = p.B;
   if (pos0 < selEnd && p.kind != NKV_STORE_BF16) {
     const signed char* kst = reinterpret_cast<const signed char*>(p.k_store);
@@ -1215,7 +1225,7 @@ __device__ void thread_rows(const AttendParams& p, int h, int pos0, int len, int
       vsrc = p.sink_v;
       ext = p.ext_sink;
     } else if (pos < ringEnd) {
-      int phys = p.ring_start + (pos - sinkEnd);
+      int phys = ring_start + (pos - sinkEnd);
       if (phys >= p.ring_cap) phys -= p.ring_cap;
       o = ((long long)h * p.ring_cap + phys) * NKV_D;
       ksrc = p.ring_k;
@@ -1288,6 +1298,24 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
   [[maybe_unused]] int* trc = nullptr;
 #endif
   NKV_STAMP(trc, 48);
+  // recent ring: explicit (arguments) or device-resident (graph replay; the
+  // head is read before any use and the last CTA to arrive advances it)
+  int ring_start = p.ring_start, ring_wpos = p.ring_write_pos;
+  if (p.ring_dyn) {
+    __shared__ int s_head;
+    if (tid == 0) {
+      const int hd = ld_acquire_s32(p.ring_dyn);
+      s_head = hd;
+      if (atomicAdd(reinterpret_cast<unsigned*>(p.ring_dyn + 1), 1u) == gridDim.x * gridDim.y - 1u) {
+        p.ring_dyn[1] = 0;
+        p.ring_dyn[0] = hd + 1 == p.ring_cap ? 0 : hd + 1;
+      }
+    }
+    __syncthreads();
+    ring_wpos = s_head;
+    ring_start = s_head + p.ring_cap - p.ring_len;
+    if (ring_start >= p.ring_cap) ring_start -= p.ring_cap;
+  }
   // peer exchange: this step's epoch (advanced only after every CTA read it)
   const uint32_t xp_ep = p.xp_P ? ld_peer_u32(p.xp_sync) : 0u;
   // one-launch step: this launch's tag (the epoch load overlaps the prologue)
@@ -1321,7 +1349,7 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
       type = (p.tma_mask & 1) ? PT_SEL : PT_THREADS;
     } else {
       const int k = tid - nslots;  // 0 sink, 1 ring before the wrap, 2 ring after it, 3 current
-      const int wrap = min(ringEnd, sinkEnd + (p.ring_cap - p.ring_start));
+      const int wrap = min(ringEnd, sinkEnd + (p.ring_cap - ring_start));
       const int e0 = clampk(selEnd), e1 = clampk(sinkEnd), e2 = clampk(wrap), e3 = clampk(ringEnd);
       row = e0 - t0;
       if (k >= 1) row += (e1 - e0 + 7) & ~7;
@@ -1395,27 +1423,28 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
     if (type == PT_SINK) {
       y0 = h * p.sink_cap + (pos0 - selEnd);
     } else {
-      int phys = p.ring_start + (pos0 - sinkEnd);
+      int phys = ring_start + (pos0 - sinkEnd);
       if (phys >= p.ring_cap) phys -= p.ring_cap;
       y0 = h * p.ring_cap + phys;
     }
     issue_piece(tm, type, y0, plen[i], prow[i], kt, vt, NR, &kbar[i], &vbar[i], lane);
   }
   // decode: append the current token to the recent ring (a slot no CTA reads)
-  if (split == 0 && p.ring_write_pos >= 0 && tid >= 64 && tid < 96 &&
-      NKV_INB(p.err, 40, ((long long)h * p.ring_cap + p.ring_write_pos) * NKV_D, NKV_D, p.ext_ring) &&
+  if (split == 0 && ring_wpos >= 0 && tid >= 64 && tid < 96 &&
+      NKV_INB(p.err, 40, ((long long)h * p.ring_cap + ring_wpos) * NKV_D, NKV_D, p.ext_ring) &&
       NKV_INB(p.err, 41, h * p.cur_head, NKV_D, p.ext_cur)) {
     const int c = tid & 15;
     const bool isv = (tid & 16) != 0;
     const __nv_bfloat16* src = (isv ? p.cur_v : p.cur_k) + h * p.cur_head + c * 8;
-    __nv_bfloat16* dst = (isv ? p.ring_v : p.ring_k) + ((long long)h * p.ring_cap + p.ring_write_pos) * NKV_D + c * 8;
+    __nv_bfloat16* dst = (isv ? p.ring_v : p.ring_k) + ((long long)h * p.ring_cap + ring_wpos) * NKV_D + c * 8;
     *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
   }
   // thread-loaded pieces outside the selected segment
   for (unsigned long long m = thr_pieces; m; m &= m - 1) {
     const int i = __ffsll((long long)m) - 1;
     if (t0 + plo[i] >= selEnd)
-      thread_rows(p, h, t0 + plo[i], plen[i], prow[i], kt, vt, NR, s_ids, slot0, selEnd, sinkEnd, ringEnd);
+      thread_rows(p, h, t0 + plo[i], plen[i], prow[i], kt, vt, NR, s_ids, slot0, selEnd, sinkEnd, ringEnd,
+                  ring_start);
   }
   NKV_STAMP(trc, 62);
   if (p.overlap) pdl_wait();  // block ids (or scores) are complete past this point
@@ -1480,7 +1509,8 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
   for (unsigned long long m = thr_pieces; m; m &= m - 1) {
     const int i = __ffsll((long long)m) - 1;
     if (t0 + plo[i] < selEnd)
-      thread_rows(p, h, t0 + plo[i], plen[i], prow[i], kt, vt, NR, s_ids, slot0, selEnd, sinkEnd, ringEnd);
+      thread_rows(p, h, t0 + plo[i], plen[i], prow[i], kt, vt, NR, s_ids, slot0, selEnd, sinkEnd, ringEnd,
+                  ring_start);
   }
   __syncthreads();  // thread-loaded rows visible
   NKV_STAMP(trc, 50);
@@ -2010,6 +2040,7 @@ struct RankArgs {
   const int32_t* prot;
   int nprot;
   void* sel_ws;  // select workspace: epoch at +16, arrivals at +20, keys at +256
+  int32_t* ring_head;  // device-resident recent-ring head [head, arrivals] (decode kernel) or null
 };
 static bool g_fs_unavailable = false;  // the cooperative cluster launch was refused once
 
@@ -2021,7 +2052,7 @@ extern "C" int nkv_attend(nkv_stream_t stream, const nkv_attend_args* a) {
 
 namespace nkv {
 int attend_ranked(nkv_stream_t stream, const nkv_attend_args* a, const float* scores, int nblocks,
-                  int64_t* out_ids, float* out_scores, const PeerArgs* peer, void* out_full) {
+                  int64_t* out_ids, float* out_scores, const PeerArgs* peer, void* out_full, int32_t* ring_head) {
   NKV_REQUIRE(a && a->nq == 1 && (scores || peer) && out_ids, "attend_ranked: needs one query, scores and out_ids");
   if (peer) {
     NKV_REQUIRE(peer->P >= 1 && peer->P <= NKV_MAX_PEERS && peer->rank >= 0 && peer->rank < peer->P && peer->exch &&
@@ -2038,7 +2069,16 @@ int attend_ranked(nkv_stream_t stream, const nkv_attend_args* a, const float* sc
               a->n_sel);
   NKV_SUPPORTED(nblocks <= FS_MAXE * NKV_DECODE_WARPS * 32, "attend_ranked: %d blocks exceed the in-kernel ranking",
                 nblocks);
-  RankArgs r{scores, nblocks, out_ids, out_scores, peer, out_full, nullptr, 0, 0, nullptr, 0, nullptr};
+  if (ring_head) {
+    // graph replay: every replay appends one token at the device-resident head,
+    // so the window length must already be at its fixed size
+    NKV_REQUIRE(((uintptr_t)ring_head & 7) == 0 && a->n_cur == 1 && a->ring_cap >= 1 && a->ring_write_pos >= 0 &&
+                    a->ring_len == a->ring_cap - 1 && a->ring_k && a->ring_v,
+                "attend_ranked: a device ring head needs a full recent window (ring_len %d, cap %d) and one "
+                "current token",
+                a->ring_len, a->ring_cap);
+  }
+  RankArgs r{scores, nblocks, out_ids, out_scores, peer, out_full, nullptr, 0, 0, nullptr, 0, nullptr, ring_head};
   return attend_impl(stream, a, &r);
 }
 
@@ -2187,6 +2227,7 @@ static int attend_impl(nkv_stream_t stream, const nkv_attend_args* a, const Rank
   p.rank_n = rank ? rank->nblocks : 0;
   p.rank_out = rank ? (long long*)rank->out_ids : nullptr;
   p.rank_out_scores = rank ? rank->out_scores : nullptr;
+  p.ring_dyn = rank ? rank->ring_head : nullptr;
   const bool one_launch = rank && !rank->scores && !rank->peer;
   p.fs_reps = one_launch ? (const __nv_bfloat16*)rank->reps : nullptr;
   p.fs_r = one_launch ? rank->r : 0;

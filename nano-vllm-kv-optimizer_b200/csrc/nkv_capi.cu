@@ -90,7 +90,7 @@ extern "C" int nkv_decode_step(nkv_stream_t stream, const nkv_decode_args* a) {
   // on B200 at 32K it measured 16.7 us per layer against 14.9 us for the two
   // launches below (its in-CTA scoring and selection take longer than the
   // scoring grid and the launch it saves).
-  if (nkv::knob("NKV_DECODE_ONE", 0) != 0) {
+  if (nkv::knob("NKV_DECODE_ONE", 0) != 0 && !a->ring_head) {
     nkv_attend_args b = t;
     b.block_ids = a->out_ids;
     b.n_sel = a->k;
@@ -117,8 +117,10 @@ extern "C" int nkv_decode_step(nkv_stream_t stream, const nkv_decode_args* a) {
     b.n_sel = a->k;
     b.overlap_select = nkv::knob("NKV_PDL", 1) != 0 ? 1 : 0;  // NKV_PDL=0: plain stream order (measurement)
     g_decode_form = 2;
-    return nkv::attend_ranked(stream, &b, scores, a->nblocks, a->out_ids, a->out_topk_scores);
+    return nkv::attend_ranked(stream, &b, scores, a->nblocks, a->out_ids, a->out_topk_scores, nullptr, nullptr,
+                              a->ring_head);
   }
+  NKV_SUPPORTED(!a->ring_head, "decode_step: a device ring head needs the two-launch form (k <= 32, nblocks <= 2048)");
   int rc = nkv_select(stream, t.q, 1, t.q_row_stride, t.q_head_stride, t.hq, t.hkv, t.head_dim, a->reps, a->r,
                       a->reps_blocks, a->nblocks, a->protected_ids, a->n_protected, a->k, a->out_ids,
                       a->out_topk_scores, nullptr, a->select_workspace, a->select_workspace_bytes);

@@ -117,8 +117,11 @@ int select_scores(cudaStream_t st, const void* q, int64_t q_row_stride, int64_t 
 // attend_ranked: nkv_attend for one query whose CTAs rank the block scores of
 // a preceding select_scores themselves (top args->n_sel), after waiting for it.
 // The ranked ids (and scores, when out_scores != NULL) are written to out_ids.
+// With ring_head != NULL the recent ring's head is device-resident (see
+// nkv_decode_args.ring_head).
 int attend_ranked(nkv_stream_t stream, const nkv_attend_args* args, const float* scores, int nblocks,
-                  int64_t* out_ids, float* out_scores, const PeerArgs* peer = nullptr, void* out_full = nullptr);
+                  int64_t* out_ids, float* out_scores, const PeerArgs* peer = nullptr, void* out_full = nullptr,
+                  int32_t* ring_head = nullptr);
 // attend_step: the whole decode step (scoring of every block, protection,
 // top args->n_sel selection, attention) as one cooperative cluster launch.
 // The keys it publishes live in the select workspace, which must start at

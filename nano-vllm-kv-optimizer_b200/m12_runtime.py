@@ -317,6 +317,11 @@ class M12LayerRuntime:
         self._att_ws = None
         self._qwin = None
         self._qwin_count = 0
+        # device address of a device-resident ring head ({head, arrivals}
+        # int32), set only while a DeviceRingHeads recording captures this
+        # layer's decode
+        self._ring_dev_ptr = 0
+        self._ring_ptr_in_args = 0
 
         # ---- state ---------------------------------------------------------------
         self.valid_len = 0
@@ -921,6 +926,7 @@ class M12LayerRuntime:
         d.select_workspace, d.select_workspace_bytes = sws.data_ptr(), sws.numel()
         a.out_row_stride, a.out_head_stride = cfg.num_heads * cfg.head_dim, cfg.head_dim
         self._dstrides = None  # (q strides, cur strides) last written into the args
+        self._ring_ptr_in_args = 0  # ring_head last written into the args
         self._daddr = C.addressof(d)
         key = (self.nblocks_filled, self.cpu_blocks_cap, self._store_ptrs, kk, id(self._ids),
                id(self.k_scale), id(self.v_scale_cpu), id(self._k_tok_scale), id(self._sel_ws),
@@ -962,6 +968,8 @@ class M12LayerRuntime:
     def _decode_fast(self, q, k, v, kk):
         """The plain decode step as one native call (nkv_decode_step)."""
         d, out, head_new = self._decode_fill(q, k, v, kk)
+        if self._ring_ptr_in_args != self._ring_dev_ptr:
+            d.ring_head = self._ring_ptr_in_args = self._ring_dev_ptr
         rc = self._step_fn(_stream_fast(self._dev_index), self._daddr)
         if rc != _lib.NKV_OK:
             call("nkv_decode_step", _stream(q.device), C.byref(d))  # raises with the message
