@@ -325,19 +325,27 @@ def store_measure(nkv, dev, iters=16):
     vs = [torch.randn(ST_T, HKV, D, generator=g, device=dev).bfloat16() for _ in range(ST_ROT)]
     rt._store_kv(ks[0], vs[0])  # first chunk: store, sink and ring set up
 
-    def run(i):
-        j = i % ST_ROT
-        rt._launch_store(ks[j], vs[j], j * (ST_T // B), ring_pos0=0)
-    for i in range(ST_ROT):
-        run(i)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(iters):
-        run(i)
-    e1.record()
-    e1.synchronize()
-    us = e0.elapsed_time(e1) * 1000.0 / iters
+    def run_all():
+        for j in range(ST_ROT):
+            rt._launch_store(ks[j], vs[j], j * (ST_T // B), ring_pos0=0)
+    run_all()  # eager once (kernel attributes), then the ST_ROT launches from a graph:
+    torch.cuda.synchronize()  # the kernel's time, not the host's issue time
+    st = torch.cuda.Stream(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=st):
+        run_all()
+    reps = max(1, iters // ST_ROT)
+    with torch.cuda.stream(st):
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(st)
+        e1.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / (reps * ST_ROT)
+    del graph
     peak, kind = peaks()
     gbs = ST_BYTES / (us * 1e-6) / 1e9
     del rt

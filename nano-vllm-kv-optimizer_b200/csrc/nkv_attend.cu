@@ -103,6 +103,7 @@ struct AttendParams {
   // written to), ring_dyn[1] counts arriving CTAs; the last CTA to arrive
   // advances the head.  Null: ring_start / ring_write_pos as given.
   int* ring_dyn;
+  int sel_thr_every;  // decode kernel: 0, or every n-th selected piece loaded by the threads
   int rank_n;
   long long* rank_out;     // the ranked ids, written by CTA (0, 0)
   float* rank_out_scores;  // their scores (optional)
@@ -1298,23 +1299,32 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
   [[maybe_unused]] int* trc = nullptr;
 #endif
   NKV_STAMP(trc, 48);
-  // recent ring: explicit (arguments) or device-resident (graph replay; the
-  // head is read before any use and the last CTA to arrive advances it)
+  // recent ring: explicit (arguments) or device-resident (graph replay).  With
+  // a device head only the CTAs holding ring keys or the current token read
+  // it (splits from sinkEnd / tps on: the others keep it off their prologue);
+  // the last of those readers to arrive advances it, and the CTA holding the
+  // current token writes it into the ring.
   int ring_start = p.ring_start, ring_wpos = p.ring_write_pos;
+  const bool ring_writer = p.ring_dyn ? split == (int)gridDim.x - 1 : split == 0;
   if (p.ring_dyn) {
-    __shared__ int s_head;
-    if (tid == 0) {
-      const int hd = ld_acquire_s32(p.ring_dyn);
-      s_head = hd;
-      if (atomicAdd(reinterpret_cast<unsigned*>(p.ring_dyn + 1), 1u) == gridDim.x * gridDim.y - 1u) {
-        p.ring_dyn[1] = 0;
-        p.ring_dyn[0] = hd + 1 == p.ring_cap ? 0 : hd + 1;
+    ring_wpos = -1;
+    const int first_reader = sinkEnd / p.tps;
+    if (split >= first_reader) {
+      __shared__ int s_head;
+      if (tid == 0) {
+        const int hd = ld_acquire_s32(p.ring_dyn);
+        s_head = hd;
+        const unsigned readers = (gridDim.x - (unsigned)first_reader) * gridDim.y;
+        if (atomicAdd(reinterpret_cast<unsigned*>(p.ring_dyn + 1), 1u) == readers - 1u) {
+          p.ring_dyn[1] = 0;
+          p.ring_dyn[0] = hd + 1 == p.ring_cap ? 0 : hd + 1;
+        }
       }
+      __syncthreads();
+      ring_wpos = s_head;
+      ring_start = s_head + p.ring_cap - p.ring_len;
+      if (ring_start >= p.ring_cap) ring_start -= p.ring_cap;
     }
-    __syncthreads();
-    ring_wpos = s_head;
-    ring_start = s_head + p.ring_cap - p.ring_len;
-    if (ring_start >= p.ring_cap) ring_start -= p.ring_cap;
   }
   // peer exchange: this step's epoch (advanced only after every CTA read it)
   const uint32_t xp_ep = p.xp_P ? ld_peer_u32(p.xp_sync) : 0u;
@@ -1347,6 +1357,9 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
       b = min(min(t1, selEnd), (slot0 + tid + 1) * B);
       row = a - t0;
       type = (p.tma_mask & 1) ? PT_SEL : PT_THREADS;
+      // every sel_thr_every-th selected piece by the threads (16-byte loads)
+      // beside the TMA boxes of the others: two load paths into the SM
+      if (p.sel_thr_every > 0 && tid % p.sel_thr_every == p.sel_thr_every - 1) type = PT_THREADS;
     } else {
       const int k = tid - nslots;  // 0 sink, 1 ring before the wrap, 2 ring after it, 3 current
       const int wrap = min(ringEnd, sinkEnd + (p.ring_cap - ring_start));
@@ -1430,7 +1443,7 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
     issue_piece(tm, type, y0, plen[i], prow[i], kt, vt, NR, &kbar[i], &vbar[i], lane);
   }
   // decode: append the current token to the recent ring (a slot no CTA reads)
-  if (split == 0 && ring_wpos >= 0 && tid >= 64 && tid < 96 &&
+  if (ring_writer && ring_wpos >= 0 && tid >= 64 && tid < 96 &&
       NKV_INB(p.err, 40, ((long long)h * p.ring_cap + ring_wpos) * NKV_D, NKV_D, p.ext_ring) &&
       NKV_INB(p.err, 41, h * p.cur_head, NKV_D, p.ext_cur)) {
     const int c = tid & 15;
@@ -1488,6 +1501,7 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
   }
   __syncthreads();
   NKV_STAMP(trc, 49);
+  NKV_STAMP(trc, 30);
   // selected blocks: TMA boxes (piece i issued by warp i % NW), or the threads
   // (int8, host-resident)
   for (int i = warp; i < np; i += NW) {
@@ -1496,6 +1510,7 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
     long long id = s_ids[(pos0 >> p.log2B) - slot0];
     if (id < 0) id = 0;  // masked in the scores
     const int y0 = (int)((id * p.hkv + h) * B + (pos0 & (B - 1)));
+    if (i == 0) NKV_STAMP(trc, 31);
     issue_piece(tm, PT_SEL, y0, plen[i], prow[i], kt, vt, NR, &kbar[i], &vbar[i], lane);
     if (i == 0) NKV_STAMP(trc, 42);
   }
@@ -2228,6 +2243,7 @@ static int attend_impl(nkv_stream_t stream, const nkv_attend_args* a, const Rank
   p.rank_out = rank ? (long long*)rank->out_ids : nullptr;
   p.rank_out_scores = rank ? rank->out_scores : nullptr;
   p.ring_dyn = rank ? rank->ring_head : nullptr;
+  p.sel_thr_every = env_int("NKV_SEL_THREADS", 0);
   const bool one_launch = rank && !rank->scores && !rank->peer;
   p.fs_reps = one_launch ? (const __nv_bfloat16*)rank->reps : nullptr;
   p.fs_r = one_launch ? rank->r : 0;

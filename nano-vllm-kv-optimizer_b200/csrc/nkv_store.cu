@@ -2,10 +2,14 @@
 // small helpers around it (K channel scale, query-segment means, and the dense
 // paged-cache row scatter that twins the reference's Triton store_kvcache).
 //
-// Store: one CTA per (block, kv head).  The 64 x 128 bf16 key tile is staged in
-// shared memory (16 KiB), written to the block store (bf16 or int8), and the r
-// representatives are chosen in-CTA exactly as the reference does
-// (m12_runtime.py:354-395):
+// Store: one CTA per (block, kv head).  One pass over the chunk's rows writes
+// the bf16 block store, sink and recent-ring rows from the registers and
+// stages the 64 x 128 key tile in shared memory (the value tile too for the
+// int8 kinds, whose scales need the whole tile).  The key directions are
+// computed once into shared memory (fp32, 32 KiB) and every pass of the
+// representative choice reads them; per warp four tokens are reduced at a
+// time (interleaved butterflies).  The r representatives are chosen in-CTA
+// exactly as the reference does (m12_runtime.py:354-395):
 //   dir_t   = k_t / max(|k_t|, 1e-12)                 (true division, as F.normalize)
 //   mean    = sum_t dir_t / B ;  mdir = mean / max(|mean|, 1e-12)
 //   pick_0  = first argmax_t dir_t . mdir
@@ -61,10 +65,12 @@ __device__ __forceinline__ signed char q8(float x, float s) {
 __global__ void __launch_bounds__(ST_THREADS) store_kernel(StoreParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int B = p.B;
-  __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(smem);           // [B][D]
-  __nv_bfloat16* vs = ks + B * NKV_D;                                    // [B][D]
-  float* nrm = reinterpret_cast<float*>(vs + B * NKV_D);                 // [B]
-  float* crit = nrm + ST_MAXB;                                           // [B]
+  // V is staged only for the int8 store kinds (its scales need the whole tile)
+  const bool stage_v = p.k_store != nullptr && p.store_kind != NKV_STORE_BF16;
+  __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(smem);           // [B][D] raw keys
+  float* dir = reinterpret_cast<float*>(ks + B * NKV_D);                 // [B][D] k_t / |k_t|
+  __nv_bfloat16* vs = reinterpret_cast<__nv_bfloat16*>(dir + B * NKV_D); // [B][D] (int8 kinds)
+  float* crit = reinterpret_cast<float*>(vs + (stage_v ? B * NKV_D : 0)); // [B]
   float* worst = crit + ST_MAXB;                                         // [B]
   float* mdir = worst + ST_MAXB;                                         // [D]
   float* red = mdir + NKV_D;                                             // [8 warps]
@@ -74,8 +80,12 @@ __global__ void __launch_bounds__(ST_THREADS) store_kernel(StoreParams p) {
   const int bl = blockIdx.x, h = blockIdx.y;
   const int blk = p.start_block + bl;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const long long tile = ((long long)blk * p.hkv + h) * B;  // row index into the store
+  const bool bf16_store = p.k_store != nullptr && p.store_kind == NKV_STORE_BF16;
 
-  // ---- stage K and V tiles (zero padding past T) ---------------------------
+  // ---- one pass over the chunk's rows: stage K (and V for int8 kinds); the
+  // bf16 block store (zero rows past T), sink and recent-ring rows are written
+  // straight from the registers ------------------------------------------------
   for (int i = tid; i < B * (NKV_D / 8); i += ST_THREADS) {
     const int t = i / (NKV_D / 8), c = i % (NKV_D / 8);
     const int gt = bl * B + t;
@@ -85,21 +95,30 @@ __global__ void __launch_bounds__(ST_THREADS) store_kernel(StoreParams p) {
       vv = *reinterpret_cast<const uint4*>(p.v + gt * p.v_row + h * p.v_head + c * 8);
     }
     reinterpret_cast<uint4*>(ks)[i] = kv;
-    reinterpret_cast<uint4*>(vs)[i] = vv;
+    if (stage_v) reinterpret_cast<uint4*>(vs)[i] = vv;
+    if (bf16_store) {
+      reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.k_store) + tile * NKV_D)[i] = kv;
+      reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.v_store) + tile * NKV_D)[i] = vv;
+    }
+    if (gt < p.T) {
+      if (gt < p.sink_write) {
+        const long long o = ((long long)h * p.sink_cap + gt) * NKV_D + c * 8;
+        *reinterpret_cast<uint4*>(p.sink_k + o) = kv;
+        *reinterpret_cast<uint4*>(p.sink_v + o) = vv;
+      }
+      if (gt >= p.ring_first && p.ring_cap > 0) {
+        const int slot = (int)(((long long)p.ring_pos0 + gt) % p.ring_cap);
+        const long long o = ((long long)h * p.ring_cap + slot) * NKV_D + c * 8;
+        *reinterpret_cast<uint4*>(p.ring_k + o) = kv;
+        *reinterpret_cast<uint4*>(p.ring_v + o) = vv;
+      }
+    }
   }
   __syncthreads();
 
-  const long long tile = ((long long)blk * p.hkv + h) * B;  // row index into the store
-  // ---- block store ---------------------------------------------------------
-  if (p.k_store == nullptr) {
-    // representatives only
-  } else if (p.store_kind == NKV_STORE_BF16) {
-    uint4* ko = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.k_store) + tile * NKV_D);
-    uint4* vo = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.v_store) + tile * NKV_D);
-    for (int i = tid; i < B * (NKV_D / 8); i += ST_THREADS) {
-      ko[i] = reinterpret_cast<uint4*>(ks)[i];
-      vo[i] = reinterpret_cast<uint4*>(vs)[i];
-    }
+  // ---- int8 block store ------------------------------------------------------
+  if (!stage_v) {
+    // bf16 store (written above) or representatives only
   } else if (p.store_kind == NKV_STORE_INT8_REF) {
     // V block scale: max |v| over the block's tokens and dims
     float m = 0.f;
@@ -160,41 +179,38 @@ __global__ void __launch_bounds__(ST_THREADS) store_kernel(StoreParams p) {
     }
   }
 
-  // ---- sink and recent-ring rows (bf16) --------------------------------------
-  for (int i = tid; i < B * (NKV_D / 8); i += ST_THREADS) {
-    const int t = i / (NKV_D / 8), c = i % (NKV_D / 8);
-    const int gt = bl * B + t;
-    if (gt >= p.T) continue;
-    if (gt < p.sink_write) {
-      const long long o = ((long long)h * p.sink_cap + gt) * NKV_D + c * 8;
-      *reinterpret_cast<uint4*>(p.sink_k + o) = reinterpret_cast<uint4*>(ks)[i];
-      *reinterpret_cast<uint4*>(p.sink_v + o) = reinterpret_cast<uint4*>(vs)[i];
-    }
-    if (gt >= p.ring_first && p.ring_cap > 0) {
-      const int slot = (int)(((long long)p.ring_pos0 + gt) % p.ring_cap);
-      const long long o = ((long long)h * p.ring_cap + slot) * NKV_D + c * 8;
-      *reinterpret_cast<uint4*>(p.ring_k + o) = reinterpret_cast<uint4*>(ks)[i];
-      *reinterpret_cast<uint4*>(p.ring_v + o) = reinterpret_cast<uint4*>(vs)[i];
-    }
-  }
-
   // ---- representatives ---------------------------------------------------------
-  // token norms: warp w handles tokens w, w+8, ...; lane holds 4 dims
-  for (int t = warp; t < B; t += ST_THREADS / 32) {
-    float s = 0.f;
+  // directions dir_t = k_t / max(|k_t|, 1e-12), once: warp w handles tokens
+  // w, w + 8, ... four at a time (interleaved reductions); lane holds 4 dims
+  for (int t0 = warp; t0 < B; t0 += 4 * (ST_THREADS / 32)) {
+    float x[4][4], s[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float x = __bfloat162float(ks[t * NKV_D + lane * 4 + i]);
-      s = fmaf(x, x, s);
+    for (int j = 0; j < 4; ++j) {
+      const int t = t0 + j * (ST_THREADS / 32);
+      s[j] = 0.f;
+      const uint2 w = t < B ? *reinterpret_cast<const uint2*>(ks + t * NKV_D + lane * 4) : make_uint2(0u, 0u);
+      x[j][0] = bf_lo(w.x); x[j][1] = bf_hi(w.x); x[j][2] = bf_lo(w.y); x[j][3] = bf_hi(w.y);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) s[j] = fmaf(x[j][i], x[j][i], s[j]);
     }
-    s = warp_sum(s);
-    if (lane == 0) nrm[t] = fmaxf(sqrtf(s), 1e-12f);
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s[j] += __shfl_xor_sync(FULL, s[j], m);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int t = t0 + j * (ST_THREADS / 32);
+      if (t >= B) break;
+      const float n = fmaxf(sqrtf(s[j]), 1e-12f);
+      *reinterpret_cast<float4*>(dir + t * NKV_D + lane * 4) =
+          make_float4(__fdiv_rn(x[j][0], n), __fdiv_rn(x[j][1], n), __fdiv_rn(x[j][2], n), __fdiv_rn(x[j][3], n));
+    }
   }
   __syncthreads();
   // mean direction: thread d sums dir_t[d] over tokens
   if (tid < NKV_D) {
     float s = 0.f;
-    for (int t = 0; t < B; ++t) s += __fdiv_rn(__bfloat162float(ks[t * NKV_D + tid]), nrm[t]);
+    for (int t = 0; t < B; ++t) s += dir[t * NKV_D + tid];
     mdir[tid] = __fdiv_rn(s, (float)B);
   }
   __syncthreads();
@@ -210,35 +226,39 @@ __global__ void __launch_bounds__(ST_THREADS) store_kernel(StoreParams p) {
   __syncthreads();
 
   for (int step = 0; step < p.r; ++step) {
-    // criterion per token
-    for (int t = warp; t < B; t += ST_THREADS / 32) {
-      float s = 0.f;
-      if (step == 0) {
+    // criterion per token: dir_t . mdir (step 0), dir_t . dir_pick (later)
+    const float4 ref = *reinterpret_cast<const float4*>((step == 0 ? mdir : dir + picks[step - 1] * NKV_D) +
+                                                        lane * 4);
+    for (int t0 = warp; t0 < B; t0 += 4 * (ST_THREADS / 32)) {
+      float s[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int d = lane * 4 + i;
-          s = fmaf(__fdiv_rn(__bfloat162float(ks[t * NKV_D + d]), nrm[t]), mdir[d], s);
-        }
-      } else {
-        const int pk = picks[step - 1];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int d = lane * 4 + i;
-          const float a = __fdiv_rn(__bfloat162float(ks[t * NKV_D + d]), nrm[t]);
-          const float b = __fdiv_rn(__bfloat162float(ks[pk * NKV_D + d]), nrm[pk]);
-          s = fmaf(a, b, s);
-        }
+      for (int j = 0; j < 4; ++j) {
+        const int t = t0 + j * (ST_THREADS / 32);
+        const float4 a = t < B ? *reinterpret_cast<const float4*>(dir + t * NKV_D + lane * 4)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        s[j] = fmaf(a.x, ref.x, 0.f);
+        s[j] = fmaf(a.y, ref.y, s[j]);
+        s[j] = fmaf(a.z, ref.z, s[j]);
+        s[j] = fmaf(a.w, ref.w, s[j]);
       }
-      s = warp_sum(s);
+#pragma unroll
+      for (int m = 16; m > 0; m >>= 1)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) s[j] += __shfl_xor_sync(FULL, s[j], m);
       if (lane == 0) {
-        if (step == 0) {
-          crit[t] = s;
-        } else {
-          const float w = step == 1 ? s : fmaxf(worst[t], s);
-          worst[t] = w;
-          bool taken = false;
-          for (int q = 0; q < step; ++q) taken |= (picks[q] == t);
-          crit[t] = taken ? 2.0f : fmaxf(w, 0.f);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int t = t0 + j * (ST_THREADS / 32);
+          if (t >= B) break;
+          if (step == 0) {
+            crit[t] = s[j];
+          } else {
+            const float w = step == 1 ? s[j] : fmaxf(worst[t], s[j]);
+            worst[t] = w;
+            bool taken = false;
+            for (int q = 0; q < step; ++q) taken |= (picks[q] == t);
+            crit[t] = taken ? 2.0f : fmaxf(w, 0.f);
+          }
         }
       }
     }
@@ -423,7 +443,10 @@ extern "C" int nkv_store_chunk(nkv_stream_t stream, const nkv_store_args* a) {
   p.ring_cap = a->ring_cap > 0 ? a->ring_cap : 0;
   p.ring_pos0 = a->ring_pos0;
   p.ring_first = a->ring_first;
-  const size_t smem = 2 * (size_t)a->block_size * NKV_D * 2 + (3 * ST_MAXB + NKV_D + 8) * 4;
+  // K tile (bf16) + directions (fp32) + V tile (bf16, int8 kinds) + per-token and per-dim scratch
+  const bool stage_v = a->k_store != nullptr && a->store_kind != NKV_STORE_BF16;
+  const size_t tile_b = (size_t)a->block_size * NKV_D;
+  const size_t smem = tile_b * 2 + tile_b * 4 + (stage_v ? tile_b * 2 : 0) + (2 * ST_MAXB + NKV_D + 8) * 4;
   if (ensure_smem(store_kernel, smem, "store_chunk")) return NKV_ERR_CUDA;
   dim3 grid(nb, a->hkv);
   store_kernel<<<grid, ST_THREADS, smem, (cudaStream_t)stream>>>(p);
