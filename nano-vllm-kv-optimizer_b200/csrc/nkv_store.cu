@@ -86,31 +86,45 @@ __global__ void __launch_bounds__(ST_THREADS) store_kernel(StoreParams p) {
   // ---- one pass over the chunk's rows: stage K (and V for int8 kinds); the
   // bf16 block store (zero rows past T), sink and recent-ring rows are written
   // straight from the registers ------------------------------------------------
-  for (int i = tid; i < B * (NKV_D / 8); i += ST_THREADS) {
-    const int t = i / (NKV_D / 8), c = i % (NKV_D / 8);
-    const int gt = bl * B + t;
-    uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-    if (gt < p.T) {
-      kv = *reinterpret_cast<const uint4*>(p.k + gt * p.k_row + h * p.k_head + c * 8);
-      vv = *reinterpret_cast<const uint4*>(p.v + gt * p.v_row + h * p.v_head + c * 8);
-    }
-    reinterpret_cast<uint4*>(ks)[i] = kv;
-    if (stage_v) reinterpret_cast<uint4*>(vs)[i] = vv;
-    if (bf16_store) {
-      reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.k_store) + tile * NKV_D)[i] = kv;
-      reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.v_store) + tile * NKV_D)[i] = vv;
-    }
-    if (gt < p.T) {
-      if (gt < p.sink_write) {
-        const long long o = ((long long)h * p.sink_cap + gt) * NKV_D + c * 8;
-        *reinterpret_cast<uint4*>(p.sink_k + o) = kv;
-        *reinterpret_cast<uint4*>(p.sink_v + o) = vv;
+  // Loads of ST_BATCH rows per thread are all issued before their stores (the
+  // compiler may not move a load above a store to another global pointer).
+  constexpr int ST_BATCH = 4;
+  for (int base = 0; base < B * (NKV_D / 8); base += ST_BATCH * ST_THREADS) {
+    uint4 kr[ST_BATCH], vr[ST_BATCH];
+#pragma unroll
+    for (int j = 0; j < ST_BATCH; ++j) {
+      const int i = base + j * ST_THREADS + tid;
+      const int gt = bl * B + i / (NKV_D / 8), c = i % (NKV_D / 8);
+      kr[j] = vr[j] = make_uint4(0, 0, 0, 0);
+      if (i < B * (NKV_D / 8) && gt < p.T) {
+        kr[j] = __ldg(reinterpret_cast<const uint4*>(p.k + gt * p.k_row + h * p.k_head + c * 8));
+        vr[j] = __ldg(reinterpret_cast<const uint4*>(p.v + gt * p.v_row + h * p.v_head + c * 8));
       }
-      if (gt >= p.ring_first && p.ring_cap > 0) {
-        const int slot = (int)(((long long)p.ring_pos0 + gt) % p.ring_cap);
-        const long long o = ((long long)h * p.ring_cap + slot) * NKV_D + c * 8;
-        *reinterpret_cast<uint4*>(p.ring_k + o) = kv;
-        *reinterpret_cast<uint4*>(p.ring_v + o) = vv;
+    }
+#pragma unroll
+    for (int j = 0; j < ST_BATCH; ++j) {
+      const int i = base + j * ST_THREADS + tid;
+      if (i >= B * (NKV_D / 8)) break;
+      const int gt = bl * B + i / (NKV_D / 8), c = i % (NKV_D / 8);
+      const uint4 kv = kr[j], vv = vr[j];
+      reinterpret_cast<uint4*>(ks)[i] = kv;
+      if (stage_v) reinterpret_cast<uint4*>(vs)[i] = vv;
+      if (bf16_store) {
+        reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.k_store) + tile * NKV_D)[i] = kv;
+        reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.v_store) + tile * NKV_D)[i] = vv;
+      }
+      if (gt < p.T) {
+        if (gt < p.sink_write) {
+          const long long o = ((long long)h * p.sink_cap + gt) * NKV_D + c * 8;
+          *reinterpret_cast<uint4*>(p.sink_k + o) = kv;
+          *reinterpret_cast<uint4*>(p.sink_v + o) = vv;
+        }
+        if (gt >= p.ring_first && p.ring_cap > 0) {
+          const int slot = (p.ring_pos0 + gt) % p.ring_cap;
+          const long long o = ((long long)h * p.ring_cap + slot) * NKV_D + c * 8;
+          *reinterpret_cast<uint4*>(p.ring_k + o) = kv;
+          *reinterpret_cast<uint4*>(p.ring_v + o) = vv;
+        }
       }
     }
   }
@@ -180,46 +194,54 @@ __global__ void __launch_bounds__(ST_THREADS) store_kernel(StoreParams p) {
   }
 
   // ---- representatives ---------------------------------------------------------
-  // directions dir_t = k_t / max(|k_t|, 1e-12), once: warp w handles tokens
-  // w, w + 8, ... four at a time (interleaved reductions); lane holds 4 dims
-  for (int t0 = warp; t0 < B; t0 += 4 * (ST_THREADS / 32)) {
-    float x[4][4], s[4];
+  // Four threads per token (t = tid / 4 + 64 g; quarter qd = tid % 4 holds dims
+  // [32 qd, 32 qd + 32)), so a token's dot product is 32 fmas and two shuffles.
+  // dir_t = k_t / max(|k_t|, 1e-12) is computed once into shared memory, its
+  // 16-byte chunks XOR-swizzled within each quarter by (qd, row parity): the 8
+  // lanes of a shared-memory phase then touch 8 different bank groups.  mdir
+  // uses the same layout with row parity 0.
+  const int qd = tid & 3;
+  for (int tb = 0; tb < B; tb += ST_THREADS / 4) {
+    const int t = tb + (tid >> 2);
+    if (t >= B) break;  // warp-uniform (B is a multiple of 8)
+    const int sw = qd | ((t & 1) << 2);
+    float x[32];
+    float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int t = t0 + j * (ST_THREADS / 32);
-      s[j] = 0.f;
-      const uint2 w = t < B ? *reinterpret_cast<const uint2*>(ks + t * NKV_D + lane * 4) : make_uint2(0u, 0u);
-      x[j][0] = bf_lo(w.x); x[j][1] = bf_hi(w.x); x[j][2] = bf_lo(w.y); x[j][3] = bf_hi(w.y);
+    for (int c = 0; c < 4; ++c) {
+      unpack8(*reinterpret_cast<const uint4*>(ks + t * NKV_D + qd * 32 + c * 8), x + c * 8);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) s[j] = fmaf(x[j][i], x[j][i], s[j]);
+      for (int e = 0; e < 8; ++e) ss = fmaf(x[c * 8 + e], x[c * 8 + e], ss);
     }
+    ss += __shfl_xor_sync(FULL, ss, 1);
+    ss += __shfl_xor_sync(FULL, ss, 2);
+    const float n = fmaxf(sqrtf(ss), 1e-12f);
 #pragma unroll
-    for (int m = 16; m > 0; m >>= 1)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) s[j] += __shfl_xor_sync(FULL, s[j], m);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int t = t0 + j * (ST_THREADS / 32);
-      if (t >= B) break;
-      const float n = fmaxf(sqrtf(s[j]), 1e-12f);
-      *reinterpret_cast<float4*>(dir + t * NKV_D + lane * 4) =
-          make_float4(__fdiv_rn(x[j][0], n), __fdiv_rn(x[j][1], n), __fdiv_rn(x[j][2], n), __fdiv_rn(x[j][3], n));
-    }
+    for (int i = 0; i < 8; ++i)
+      *reinterpret_cast<float4*>(dir + t * NKV_D + qd * 32 + ((i ^ sw) << 2)) =
+          make_float4(__fdiv_rn(x[i * 4 + 0], n), __fdiv_rn(x[i * 4 + 1], n), __fdiv_rn(x[i * 4 + 2], n),
+                      __fdiv_rn(x[i * 4 + 3], n));
   }
   __syncthreads();
-  // mean direction: thread d sums dir_t[d] over tokens
-  if (tid < NKV_D) {
-    float s = 0.f;
-    for (int t = 0; t < B; ++t) s += dir[t * NKV_D + tid];
-    mdir[tid] = __fdiv_rn(s, (float)B);
+  // mean direction: thread (d, half) sums dir_t[d] over half of the tokens
+  {
+    const int d = tid & (NKV_D - 1), hf = tid >> 7;  // ST_THREADS == 2 * NKV_D
+    const int dq = d >> 5, di = (d >> 2) & 7, de = d & 3;
+    const int off0 = dq * 32 + ((di ^ dq) << 2) + de, off1 = dq * 32 + ((di ^ (dq | 4)) << 2) + de;
+    const int h0 = hf * (B / 2), h1 = h0 + B / 2;
+    float sm = 0.f;
+    for (int t = h0; t < h1; ++t) sm += dir[t * NKV_D + ((t & 1) ? off1 : off0)];
+    crit[tid] = sm;  // (crit and worst as scratch: 256 floats)
+    __syncthreads();
+    if (tid < NKV_D) mdir[off0] = __fdiv_rn(crit[tid] + crit[tid + NKV_D], (float)B);
   }
   __syncthreads();
-  if (warp == 0) {
-    float s = 0.f;
+  if (warp == 0) {  // normalise mdir (elementwise: layout-agnostic)
+    float sq = 0.f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) s = fmaf(mdir[lane * 4 + i], mdir[lane * 4 + i], s);
-    s = warp_sum(s);
-    const float n = fmaxf(sqrtf(s), 1e-12f);
+    for (int i = 0; i < 4; ++i) sq = fmaf(mdir[lane * 4 + i], mdir[lane * 4 + i], sq);
+    sq = warp_sum(sq);
+    const float n = fmaxf(sqrtf(sq), 1e-12f);
 #pragma unroll
     for (int i = 0; i < 4; ++i) mdir[lane * 4 + i] = __fdiv_rn(mdir[lane * 4 + i], n);
   }
@@ -227,38 +249,34 @@ __global__ void __launch_bounds__(ST_THREADS) store_kernel(StoreParams p) {
 
   for (int step = 0; step < p.r; ++step) {
     // criterion per token: dir_t . mdir (step 0), dir_t . dir_pick (later)
-    const float4 ref = *reinterpret_cast<const float4*>((step == 0 ? mdir : dir + picks[step - 1] * NKV_D) +
-                                                        lane * 4);
-    for (int t0 = warp; t0 < B; t0 += 4 * (ST_THREADS / 32)) {
-      float s[4];
+    const int pk = step == 0 ? 0 : picks[step - 1];
+    const float* ref = step == 0 ? mdir : dir + pk * NKV_D;
+    const int rsw = qd | ((pk & 1) << 2);  // mdir: row parity 0
+    for (int tb = 0; tb < B; tb += ST_THREADS / 4) {
+      const int t = tb + (tid >> 2);
+      if (t >= B) break;  // warp-uniform
+      const int sw = qd | ((t & 1) << 2);
+      float sc = 0.f;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int t = t0 + j * (ST_THREADS / 32);
-        const float4 a = t < B ? *reinterpret_cast<const float4*>(dir + t * NKV_D + lane * 4)
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
-        s[j] = fmaf(a.x, ref.x, 0.f);
-        s[j] = fmaf(a.y, ref.y, s[j]);
-        s[j] = fmaf(a.z, ref.z, s[j]);
-        s[j] = fmaf(a.w, ref.w, s[j]);
+      for (int i = 0; i < 8; ++i) {
+        const float4 a4 = *reinterpret_cast<const float4*>(dir + t * NKV_D + qd * 32 + ((i ^ sw) << 2));
+        const float4 r4 = *reinterpret_cast<const float4*>(ref + qd * 32 + ((i ^ rsw) << 2));
+        sc = fmaf(a4.x, r4.x, sc);
+        sc = fmaf(a4.y, r4.y, sc);
+        sc = fmaf(a4.z, r4.z, sc);
+        sc = fmaf(a4.w, r4.w, sc);
       }
-#pragma unroll
-      for (int m = 16; m > 0; m >>= 1)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) s[j] += __shfl_xor_sync(FULL, s[j], m);
-      if (lane == 0) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int t = t0 + j * (ST_THREADS / 32);
-          if (t >= B) break;
-          if (step == 0) {
-            crit[t] = s[j];
-          } else {
-            const float w = step == 1 ? s[j] : fmaxf(worst[t], s[j]);
-            worst[t] = w;
-            bool taken = false;
-            for (int q = 0; q < step; ++q) taken |= (picks[q] == t);
-            crit[t] = taken ? 2.0f : fmaxf(w, 0.f);
-          }
+      sc += __shfl_xor_sync(FULL, sc, 1);
+      sc += __shfl_xor_sync(FULL, sc, 2);
+      if (qd == 0) {
+        if (step == 0) {
+          crit[t] = sc;
+        } else {
+          const float w = step == 1 ? sc : fmaxf(worst[t], sc);
+          worst[t] = w;
+          bool taken = false;
+          for (int q = 0; q < step; ++q) taken |= (picks[q] == t);
+          crit[t] = taken ? 2.0f : fmaxf(w, 0.f);
         }
       }
     }
