@@ -338,6 +338,12 @@ int nkv_ring_append(nkv_stream_t stream, const void* k, const void* v, int T, in
                     int64_t k_head_stride, int64_t v_row_stride, int64_t v_head_stride, int hkv,
                     int head_dim, void* ring_k, void* ring_v, int ring_cap, int ring_pos0);
 
+/* Self-test of the division the store kernel uses for the key directions
+ * (a correctly rounded reciprocal and one fma correction instead of a divide
+ * per element): out[i] = a[i] / b[i] for b[i] > 0 normal and a finite quotient,
+ * to be compared with the division operator.  No counterpart in the reference. */
+int nkv_selftest_div(nkv_stream_t stream, const float* a, const float* b, float* out, int n);
+
 /* Per-(kv head, channel) K scale of the reference int8 scheme, from one chunk:
  * scale[h][d] = max(max_t |k[t][h][d]|, 1e-8) / 127   (m12_runtime.py:463-465). */
 int nkv_k_channel_scale(nkv_stream_t stream, const void* k, int T, int64_t row_stride,

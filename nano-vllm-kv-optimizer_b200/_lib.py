@@ -119,6 +119,7 @@ SIGNATURES = {
     "nkv_k_channel_scale": (c_int, [c_vp, c_vp, c_int, c_i64, c_i64, c_int, c_int, c_vp]),
     "nkv_query_summaries": (c_int, [c_vp, c_vp, c_int, c_i64, c_i64, c_int, c_int, c_int, c_vp]),
     "nkv_store_kvcache": (c_int, [c_vp, c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_int, c_int]),
+    "nkv_selftest_div": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int]),
 }
 
 _lib = None

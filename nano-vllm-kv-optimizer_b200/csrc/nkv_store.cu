@@ -55,6 +55,20 @@ __device__ __forceinline__ float warp_max(float x) {
   return x;
 }
 
+// x / n, correctly rounded, given y = RN(1/n) (n a positive normal float):
+// q0 = RN(x * y) is within an ulp of x / n, the remainder r = x - q0 * n is
+// exact in one fma, and RN(q0 + r * y) is the correctly rounded quotient
+// (Markstein, "Computation of elementary functions on the IBM RISC System/6000
+// processor", IBM J. Res. Dev. 34(1), 1990).  The argument needs a quotient
+// in the normal range: tiny quotients (and zeros, for the sign) take the
+// division itself.  Checked against the division operator by nkv_selftest_div.
+__device__ __forceinline__ float div_rcp(float x, float n, float y) {
+  const float q0 = x * y;
+  if (fabsf(q0) < 0x1p-100f) return __fdiv_rn(x, n);
+  const float r = fmaf(-q0, n, x);
+  return fmaf(r, y, q0);
+}
+
 // quantize one float with a given scale, reference rounding (half to even)
 __device__ __forceinline__ signed char q8(float x, float s) {
   float y = rintf(__fdiv_rn(x, s));
@@ -216,11 +230,12 @@ __global__ void __launch_bounds__(ST_THREADS) store_kernel(StoreParams p) {
     ss += __shfl_xor_sync(FULL, ss, 1);
     ss += __shfl_xor_sync(FULL, ss, 2);
     const float n = fmaxf(sqrtf(ss), 1e-12f);
+    const float y = __frcp_rn(n);
 #pragma unroll
     for (int i = 0; i < 8; ++i)
       *reinterpret_cast<float4*>(dir + t * NKV_D + qd * 32 + ((i ^ sw) << 2)) =
-          make_float4(__fdiv_rn(x[i * 4 + 0], n), __fdiv_rn(x[i * 4 + 1], n), __fdiv_rn(x[i * 4 + 2], n),
-                      __fdiv_rn(x[i * 4 + 3], n));
+          make_float4(div_rcp(x[i * 4 + 0], n, y), div_rcp(x[i * 4 + 1], n, y), div_rcp(x[i * 4 + 2], n, y),
+                      div_rcp(x[i * 4 + 3], n, y));
   }
   __syncthreads();
   // mean direction: thread (d, half) sums dir_t[d] over half of the tokens
@@ -501,4 +516,22 @@ extern "C" int nkv_store_kvcache(nkv_stream_t stream, const void* key, int64_t k
       (const __nv_bfloat16*)key, key_stride, (const __nv_bfloat16*)value, value_stride,
       (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, (const long long*)slot_mapping, row_elems);
   return check_launch("store_kvcache");
+}
+
+// ---------------------------------------------------------------------------
+// Self-test of div_rcp: out[i] = a[i] / b[i] by the store kernel's division
+// (b[i] > 0 normal).  Tests compare it with the division operator.
+// ---------------------------------------------------------------------------
+namespace nkv {
+__global__ void selftest_div_kernel(const float* a, const float* b, float* out, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = div_rcp(a[i], b[i], __frcp_rn(b[i]));
+}
+}  // namespace nkv
+
+extern "C" int nkv_selftest_div(nkv_stream_t stream, const float* a, const float* b, float* out, int n) {
+  NKV_REQUIRE(a && b && out && n >= 0, "selftest_div: bad arguments");
+  if (n == 0) return NKV_OK;
+  nkv::selftest_div_kernel<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(a, b, out, n);
+  return nkv::check_launch("selftest_div");
 }

@@ -94,6 +94,29 @@ def test_select_per_query_matches_oracle():
 # ----------------------------------------------------------------------------
 # kernel (5): store + representatives
 # ----------------------------------------------------------------------------
+def test_store_division_is_correctly_rounded():
+    """The store kernel divides each key by its norm with a reciprocal and one
+    fma correction; it must equal the IEEE division bit for bit (the division
+    operator on the device), signs of zero included, over positive normal
+    divisors and finite quotients (key elements over norms lie in [-1, 1])."""
+    nkv = pkg()
+    g = torch.Generator().manual_seed(11)
+    n = 1 << 20
+    a = torch.cat([torch.randn(n, generator=g).bfloat16().float(),                    # key elements
+                   torch.randn(n, generator=g) * 2.0 ** torch.randint(-30, 30, (n,), generator=g).float(),
+                   torch.tensor([0.0, -0.0, 1e-38, -3e-39, 65504.0, 1.0, -1.0])])
+    b = torch.cat([torch.rand(n, generator=g) * 30 + 1e-3,                              # norms
+                   torch.rand(n, generator=g).clamp_min(1e-6) * 2.0 ** torch.randint(-30, 30, (n,), generator=g).float(),
+                   torch.tensor([1e-12, 1e-12, 1.0, 3.0, 7.0, 1e-12, 1e-12])])
+    ad, bd = a.to(DEV), b.to(DEV)
+    out = torch.empty_like(ad)
+    nkv._lib.call("nkv_selftest_div", torch.cuda.current_stream().cuda_stream, ad.data_ptr(), bd.data_ptr(),
+                  out.data_ptr(), ad.numel())
+    want = ad / bd
+    torch.cuda.synchronize()
+    assert torch.equal(out.view(torch.int32), want.view(torch.int32))
+
+
 @pytest.mark.parametrize("T,start", [(4096, 0), (333, 5), (64, 0), (2, 1)])
 def test_store_and_reps_match_oracle(T, start):
     nkv = pkg()
