@@ -91,7 +91,6 @@ struct AttendParams {
   int overlap;  // 1: wait for the preceding (select) grid before touching ids
   int cluster;  // 1: the splits of a head form one thread-block cluster (DSMEM merge)
   int log2B;    // block_size is a power of two
-  int stop;     // checked builds only: end the decode kernel after phase `stop` (timing probes)
   // decode kernel: tile rows per K (or V) tile, bytes of the K-tile region,
   // segments TMA may read (1 selected blocks, 2 sink, 4 ring: bf16 in device memory)
   int tile_rows, region_k, tma_mask;
@@ -1542,13 +1541,6 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
   for (int i = pa; i <= pb; ++i)
     if (ptype[i] <= PT_RING) mbar_wait_poll(&kbar[i], 0, p.err);
   NKV_STAMP(trc, 51);
-#ifdef NKV_CHECKED
-  if (p.stop == 1) {
-    for (int i = pa; i <= pb; ++i)
-      if (ptype[i] <= PT_RING) mbar_wait_poll(&vbar[i], 0, p.err);
-    return;
-  }
-#endif
 
   // slices hold at most 48 keys (tps <= 384 over 8 warps, rounded to 8)
   constexpr int MAXT = AT_TPS_MAX_CLUSTER / (8 * NW);  // n-tiles of 8 keys per warp slice
@@ -1624,9 +1616,6 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
   for (int i = pa; i <= pb; ++i)
     if (ptype[i] <= PT_RING) mbar_wait_poll(&vbar[i], 0, p.err);
   NKV_STAMP(trc, 53);
-#ifdef NKV_CHECKED
-  if (p.stop == 2) { if (lane == 0 && mloc == 1.2345f) p.out[0] = __float2bfloat16(lloc); return; }
-#endif
 
   // O += P V: k-steps of 16 keys (two n-tiles of scores), 16 n-tiles of 8 dims
   float ofr[16][4];
@@ -1670,9 +1659,6 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
   }
   __syncthreads();  // warp partials complete; every warp is done with the V tile
   NKV_STAMP(trc, 54);
-#ifdef NKV_CHECKED
-  if (p.stop == 3) return;
-#endif
 
   // ---- merge the warp slices into the CTA partial -----------------------------------
   float* dst_o = p.cluster ? po : p.part_o + (((long long)h * p.splits + split) * G) * NKV_D;
@@ -1708,9 +1694,6 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
     }
   }
   NKV_STAMP(trc, 55);
-#ifdef NKV_CHECKED
-  if (p.stop == 4) return;
-#endif
   if (p.cluster) {
     combine_cluster<G>(p, h, pm, pl, po, xp_ep);  // begins and ends with a cluster barrier
     if (p.xp_P && split == 0) peer_pull_arrive<G>(p, h, xp_ep);
@@ -2237,7 +2220,6 @@ static int attend_impl(nkv_stream_t stream, const nkv_attend_args* a, const Rank
   p.cluster = C > 0 ? 1 : 0;
   // NKV_ATTEND_MERGE: 0 = workspace merge, 1 = cluster merge where it fits
   if (env_int("NKV_ATTEND_MERGE", 1) == 0) p.cluster = 0;
-  p.stop = env_int("NKV_DEBUG_STOP", 0);
   p.rank_scores = rank ? rank->scores : nullptr;
   p.rank_n = rank ? rank->nblocks : 0;
   p.rank_out = rank ? (long long*)rank->out_ids : nullptr;
