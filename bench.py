@@ -10,7 +10,9 @@ hold ~2.7 GB and a step touches ~540 MB, more than L2 (126 MB), so no L2 flush
 is needed between steps.  Inputs are synthetic (seeded N(0,1)).
 
 Metric: device time per layer decode, whole job: step_time / (L * n_gpus) in
-microseconds (lower is better).  With N GPUs each rank decodes its own
+microseconds (lower is better); the step is replayed through DecodeGraph (the
+36 layers' decode recorded once, the recent windows advancing on the device
+with every replay, as in a decode loop).  With N GPUs each rank decodes its own
 independent sequence (replicas; weak scaling, no collective on the data path).
 
 ``--impl reference`` times the reference algorithm's CPU implementation (the
@@ -511,11 +513,9 @@ def main():
     stream.synchronize()
     attend_cfg = nkv._lib.attend_last_config()
 
-    # whole step (select + attend for every layer) captured in one CUDA graph
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        for li, rt in enumerate(layers):
-            rt.decode(qs[li], ks[li], vs[li], dev)
+    # whole step (select + attend for every layer) recorded once and replayed
+    # per token with the recent windows advancing on the device (DecodeGraph)
+    graph = nkv.DecodeGraph(layers, [(qs[li], ks[li], vs[li]) for li in range(L)], stream=stream)
     # kernel (2) alone over the same ids, for the roofline of the dominant kernel
     ids_saved = [rt._ids[:TOPK].clone() for rt in layers]
     g_att = torch.cuda.CUDAGraph()
