@@ -47,7 +47,7 @@ ATTEND_BYTES = ATTEND_TOKENS * HKV * D * 2 * 2 + (HQ * D * 2) * 2 + HKV * D * 2 
 SELECT_BYTES = (CTX // B) * HKV * R_REPS * D * 2 + HQ * D * 2
 STEP_BYTES = ATTEND_BYTES + SELECT_BYTES
 # DRAM bytes of one attend launch measured by ncu (profiles/decode_kernel_l4.md)
-ATTEND_TRAFFIC = 10826240
+ATTEND_TRAFFIC = 10851328
 # segmented prefill operator: a 4096-token chunk after a
 # 28672-token history; visible (query, key) pairs per head x 32 heads x 4 D
 PF_CHUNK, PF_HIST = 4096, 28672
