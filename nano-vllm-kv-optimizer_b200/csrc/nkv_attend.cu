@@ -817,9 +817,9 @@ __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long
   asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
   return v;
 }
-__device__ __forceinline__ int ld_acquire_s32(const int* a) {
+__device__ __forceinline__ int ld_relaxed_s32(const int* a) {
   int v;
-  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+  asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
   return v;
 }
 __device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned* a) {
@@ -1309,16 +1309,11 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
     ring_wpos = -1;
     const int first_reader = sinkEnd / p.tps;
     if (split >= first_reader) {
+      // (the arrival that lets the last reader advance the head comes after
+      // the prologue, once the head is in use: its round trip stays off the
+      // CTA's first barrier)
       __shared__ int s_head;
-      if (tid == 0) {
-        const int hd = ld_acquire_s32(p.ring_dyn);
-        s_head = hd;
-        const unsigned readers = (gridDim.x - (unsigned)first_reader) * gridDim.y;
-        if (atomicAdd(reinterpret_cast<unsigned*>(p.ring_dyn + 1), 1u) == readers - 1u) {
-          p.ring_dyn[1] = 0;
-          p.ring_dyn[0] = hd + 1 == p.ring_cap ? 0 : hd + 1;
-        }
-      }
+      if (tid == 0) s_head = ld_relaxed_s32(p.ring_dyn);
       __syncthreads();
       ring_wpos = s_head;
       ring_start = s_head + p.ring_cap - p.ring_len;
@@ -1457,6 +1452,15 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
     if (t0 + plo[i] >= selEnd)
       thread_rows(p, h, t0 + plo[i], plen[i], prow[i], kt, vt, NR, s_ids, slot0, selEnd, sinkEnd, ringEnd,
                   ring_start);
+  }
+  if (p.ring_dyn && tid == 0 && split >= sinkEnd / p.tps) {
+    // device ring head: this CTA has read it (ring_wpos holds it); the last of
+    // the readers to arrive advances it for the next step
+    const unsigned readers = (gridDim.x - (unsigned)(sinkEnd / p.tps)) * gridDim.y;
+    if (atomicAdd(reinterpret_cast<unsigned*>(p.ring_dyn + 1), 1u) == readers - 1u) {
+      p.ring_dyn[1] = 0;
+      p.ring_dyn[0] = ring_wpos + 1 == p.ring_cap ? 0 : ring_wpos + 1;
+    }
   }
   NKV_STAMP(trc, 62);
   if (p.overlap) pdl_wait();  // block ids (or scores) are complete past this point
