@@ -1298,6 +1298,10 @@ __global__ void __launch_bounds__(DK<G>::THREADS) decode_kernel(const AttendPara
   [[maybe_unused]] int* trc = nullptr;
 #endif
   NKV_STAMP(trc, 48);
+  // a kernel launched after this one with programmatic dependent launch (the
+  // next layer's scoring grid) may become resident now; it waits for this
+  // grid's completion before reading anything
+  if (!FS) pdl_launch_dependents();
   // recent ring: explicit (arguments) or device-resident (graph replay).  With
   // a device head only the CTAs holding ring keys or the current token read
   // it (splits from sinkEnd / tps on: the others keep it off their prologue);

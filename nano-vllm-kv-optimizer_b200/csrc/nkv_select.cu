@@ -402,6 +402,11 @@ template <int G>
 __global__ void __launch_bounds__(SC_THREADS) score_kernel(SelectParams p) {
   __shared__ float part[SC_WARPS][SC_BPC_MAX];
   __shared__ unsigned char s_prot[SC_BPC_MAX];
+  // launched with programmatic dependent launch: the CTAs may be resident
+  // before the preceding kernel has finished, so wait for it before any read,
+  // and release the dependent attention grid only then (its prologue reads q
+  // and the current token, which the preceding kernel may produce)
+  pdl_wait();
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int j = lane >> 3, c = lane & 7;
@@ -488,13 +493,29 @@ static int launch_score(cudaStream_t st, SelectParams& p, int G) {
   const int per = (p.nblocks + sms - 1) / sms;
   p.bpc = (per + SC_UPW - 1) / SC_UPW * SC_UPW;
   const int grid = (p.nblocks + p.bpc - 1) / p.bpc;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = knob("NKV_SCORE_PDL", 1) != 0 ? 1 : 0;
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(grid);
+  lc.blockDim = dim3(SC_THREADS);
+  lc.dynamicSmemBytes = 0;
+  lc.stream = st;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  cudaError_t e;
   switch (G) {
-    case 1: score_kernel<1><<<grid, SC_THREADS, 0, st>>>(p); break;
-    case 2: score_kernel<2><<<grid, SC_THREADS, 0, st>>>(p); break;
-    case 4: score_kernel<4><<<grid, SC_THREADS, 0, st>>>(p); break;
+    case 1: e = cudaLaunchKernelEx(&lc, score_kernel<1>, p); break;
+    case 2: e = cudaLaunchKernelEx(&lc, score_kernel<2>, p); break;
+    case 4: e = cudaLaunchKernelEx(&lc, score_kernel<4>, p); break;
     default:
       set_error("score: unsupported G=%d", G);
       return NKV_ERR_UNSUPPORTED;
+  }
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("score: launch failed: %s", cudaGetErrorString(e));
+    return NKV_ERR_CUDA;
   }
   return check_launch("score");
 }
