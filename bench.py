@@ -454,6 +454,8 @@ def main():
     ap.add_argument("--no-sharded", action="store_true", help="skip the KV-head-sharded measurement (N > 1)")
     ap.add_argument("--store-only", action="store_true",
                     help="run only the kernel (5) store measurement and print its record (profiling)")
+    ap.add_argument("--offload-only", action="store_true",
+                    help="run only the host-offload decode measurement and print its record (profiling)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -489,6 +491,9 @@ def main():
     nkv = __import__("importlib").import_module(PKG)
     if args.store_only:
         print(json.dumps({"store": store_measure(nkv, torch.device("cuda", 0))}))
+        return
+    if args.offload_only:
+        print(json.dumps({"offload": offload_measure(nkv, torch.device("cuda", 0))}))
         return
     if world > 1:
         import torch.distributed as dist
