@@ -77,7 +77,9 @@ class DeviceRingHeads:
         self._ring[:, 0].copy_(torch.tensor(self._heads, dtype=torch.int32))
 
     @contextmanager
-    def recording(self):
+    def recording(self, outputs=None):
+        """``outputs[i]`` (optional): the [1, Hq, D] tensor layer i's recorded
+        decode writes its output into, instead of a new tensor."""
         layers = self.layers
         saved = [(rt.valid_len, rt._ring_head, rt._last_ids_dev, rt._last_ids_host, rt.timings,
                   rt.cfg.check_finite_outputs) for rt in layers]
@@ -85,10 +87,16 @@ class DeviceRingHeads:
             for i, rt in enumerate(layers):
                 rt._ring_dev_ptr = self._ring[i].data_ptr()
                 rt.cfg.check_finite_outputs = False  # a host synchronisation: not recordable
+                if outputs is not None:
+                    o = outputs[i]
+                    assert (o.is_contiguous() and o.dtype == torch.bfloat16 and o.device == rt.device
+                            and tuple(o.shape) == (1, rt.cfg.num_heads, rt.cfg.head_dim))
+                    rt._out_override = o
             yield self
         finally:
             for rt, sv in zip(layers, saved):
                 rt._ring_dev_ptr = 0
+                rt._out_override = None
                 (rt.valid_len, rt._ring_head, rt._last_ids_dev, rt._last_ids_host, rt.timings,
                  rt.cfg.check_finite_outputs) = sv
 
@@ -121,8 +129,8 @@ class DecodeGraph:
 
     ``inputs[i] = (q, k, v)`` are layer i's device inputs ([1, Hq, D],
     [1, Hkv, D], [1, Hkv, D] bf16), read by every replay.  ``outputs[i]`` is
-    layer i's [1, Hq, D] output, and with ``stack=True`` ``out`` is all of
-    them as one [L, 1, Hq, D] tensor written inside the graph.
+    layer i's [1, Hq, D] output; with ``stack=True`` they are the rows of
+    ``out`` ([L, 1, Hq, D]), which the layers' decode steps write directly.
     """
 
     def __init__(self, layers: list[M12LayerRuntime], inputs, stream: torch.cuda.Stream | None = None,
@@ -136,9 +144,15 @@ class DecodeGraph:
         self.layers = self.heads.layers
         self.inputs = list(inputs)
         self.graph = torch.cuda.CUDAGraph()
-        with self.heads.recording(), torch.cuda.graph(self.graph, stream=stream):
+        # stacked: every layer's decode writes its row of `out` directly
+        self.out = None
+        if stack:
+            hq, d = layers[0].cfg.num_heads, layers[0].cfg.head_dim
+            assert all(rt.cfg.num_heads == hq and rt.cfg.head_dim == d for rt in layers)
+            self.out = torch.empty(len(layers), 1, hq, d, dtype=torch.bfloat16, device=dev)
+        rows = list(self.out) if stack else None
+        with self.heads.recording(rows), torch.cuda.graph(self.graph, stream=stream):
             self.outputs = [rt.decode(q, k, v, dev) for rt, (q, k, v) in zip(layers, inputs)]
-            self.out = torch.stack(self.outputs) if stack else None
 
     def replay(self):
         """Decode one token through every layer; returns ``out`` (or ``outputs``)."""

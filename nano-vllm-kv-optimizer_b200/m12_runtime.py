@@ -322,6 +322,9 @@ class M12LayerRuntime:
         # layer's decode
         self._ring_dev_ptr = 0
         self._ring_ptr_in_args = 0
+        # output tensor of the next fast decode calls instead of a new one (set
+        # only while a DeviceRingHeads recording writes into stacked outputs)
+        self._out_override = None
 
         # ---- state ---------------------------------------------------------------
         self.valid_len = 0
@@ -951,7 +954,9 @@ class M12LayerRuntime:
         if ks != vs or ks[-1] != 1 or ks[1] % 8 or kp % 16 or vp % 16:
             k, v = k.contiguous(), v.contiguous()
             ks, kp, vp = k.stride(), k.data_ptr(), v.data_ptr()
-        out = torch.empty(1, cfg.num_heads, cfg.head_dim, dtype=q.dtype, device=q.device)
+        out = self._out_override
+        if out is None:
+            out = torch.empty(1, cfg.num_heads, cfg.head_dim, dtype=q.dtype, device=q.device)
         a.q, a.cur_k, a.cur_v, a.out = qp, kp, vp, out.data_ptr()
         strides = (qs[0], qs[1], ks[0], ks[1])
         if strides != self._dstrides:

@@ -78,6 +78,7 @@ def test_graph_replay_matches_eager(hist, top_k, recent):
         for li in range(L):
             assert torch.equal(out[li], want[li]), f"step {step} layer {li}"
             assert torch.equal(dg.outputs[li], want[li])
+            assert dg.outputs[li].data_ptr() == dg.out[li].data_ptr()  # written in place, no stack copy
             _same_state(ga[li], eb[li])
 
 

@@ -16,7 +16,8 @@ def _layer(i, valid_len=1000, head=5, R=512, S=64, nb=16):
     return types.SimpleNamespace(
         layer_id=i, cfg=cfg, device=torch.device("cpu"), _fast_ok=True, record_q=False, record_ids=False,
         _k_store=object(), _dargs=object(), valid_len=valid_len, nblocks_filled=nb, _ring_head=head,
-        _ids_view="ids", _last_ids_dev=None, _last_ids_host=[1], timings={}, _ring_dev_ptr=0)
+        _ids_view="ids", _last_ids_dev=None, _last_ids_host=[1], timings={}, _ring_dev_ptr=0,
+        _out_override=None)
 
 
 def test_heads_advance_wrap_and_resync():
