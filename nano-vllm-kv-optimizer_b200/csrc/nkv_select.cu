@@ -393,6 +393,11 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel(SelectParams p) {
 // representative load of the group issued before the arithmetic (one DRAM
 // round trip per group).  Lane layout and summation order are unit_score's,
 // so the scores are bit-identical to select_kernel's.
+// Bulk prefetch of `bytes` (a multiple of 16, 16-byte aligned) into L2.
+__device__ __forceinline__ void prefetch_l2_range(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 constexpr int SC_THREADS = 256;
 constexpr int SC_WARPS = SC_THREADS / 32;
 constexpr int SC_UPW = 4;       // (head, block) units per warp in flight
@@ -402,16 +407,22 @@ template <int G>
 __global__ void __launch_bounds__(SC_THREADS) score_kernel(SelectParams p) {
   __shared__ float part[SC_WARPS][SC_BPC_MAX];
   __shared__ unsigned char s_prot[SC_BPC_MAX];
-  // launched with programmatic dependent launch: the CTAs may be resident
-  // before the preceding kernel has finished, so wait for it before any read,
-  // and release the dependent attention grid only then (its prologue reads q
-  // and the current token, which the preceding kernel may produce)
-  pdl_wait();
-  pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int j = lane >> 3, c = lane & 7;
   const int b0 = blockIdx.x * p.bpc;
   const int nb = min(p.bpc, p.nblocks - b0);
+  // launched with programmatic dependent launch: the CTAs may be resident
+  // before the preceding kernel has finished.  Meanwhile each warp prefetches
+  // its heads' representative rows into L2 (a prefetch reads nothing into the
+  // SM, so it cannot see data older than what the loads below will); every
+  // read waits for the preceding kernel, and the dependent attention grid is
+  // released only then (its prologue reads q and the current token, which the
+  // preceding kernel may produce)
+  if (lane == 0 && nb > 0)
+    for (int h = warp; h < p.hkv; h += SC_WARPS)
+      prefetch_l2_range(p.reps + ((long long)h * p.max_blocks + b0) * p.r * NKV_D, (uint32_t)(nb * p.r * NKV_D * 2));
+  pdl_wait();
+  pdl_launch_dependents();
   for (int i = threadIdx.x; i < SC_WARPS * SC_BPC_MAX; i += SC_THREADS) (&part[0][0])[i] = -INFINITY;
   for (int i = threadIdx.x; i < SC_BPC_MAX; i += SC_THREADS) s_prot[i] = 0;
   __syncthreads();
