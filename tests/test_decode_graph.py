@@ -41,12 +41,18 @@ def _same_state(a, b):
     assert a.last_block_ids.tolist() == b.last_block_ids.tolist()
 
 
-@pytest.mark.parametrize("hist,top_k,recent", [(2048, 8, 512), (8192, 32, 512), (3000, 16, 64)])
-def test_graph_replay_matches_eager(hist, top_k, recent):
+@pytest.mark.parametrize("hist,top_k,recent,extra", [
+    (2048, 8, 512, {}),
+    (8192, 32, 512, {}),
+    (3000, 16, 64, {}),
+    # int8 history (per-token scales) in mapped pinned host memory: the offload decode
+    (4096, 32, 512, {"quant_history": True, "quant_scheme": "token", "kv_residency": "host"}),
+])
+def test_graph_replay_matches_eager(hist, top_k, recent, extra):
     nkv = pkg()
     L = 3
-    ga = _stack(L, hist, seed=hist + top_k, top_k_blocks=top_k, recent_tokens=recent)
-    eb = _stack(L, hist, seed=hist + top_k, top_k_blocks=top_k, recent_tokens=recent)
+    ga = _stack(L, hist, seed=hist + top_k, top_k_blocks=top_k, recent_tokens=recent, **extra)
+    eb = _stack(L, hist, seed=hist + top_k, top_k_blocks=top_k, recent_tokens=recent, **extra)
     g = torch.Generator().manual_seed(7)
     # one eager token on both stacks (sets up workspaces outside the capture)
     for (q, k, v), a, b in zip(_token(g, L), ga, eb):
