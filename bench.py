@@ -15,8 +15,11 @@ microseconds (lower is better); the step is replayed through DecodeGraph (the
 with every replay, as in a decode loop).  With N GPUs each rank decodes its own
 independent sequence (replicas; weak scaling, no collective on the data path).
 
-``--impl reference`` times the reference algorithm's CPU implementation (the
-oracle port of m12_runtime.py's torch path) on the host cores instead.
+``--impl reference`` times the reference's own CPU implementation on the host
+cores instead: its ``M12LayerRuntime.decode`` (torch, from the reference package
+installed under ``baseline/_ref``, run through the CPU device shim in
+``oracle/ref_shim.py``), with the oracle port's time beside it (the port is the
+reference arm when the package is absent).
 """
 from __future__ import annotations
 
@@ -38,6 +41,7 @@ HQ, HKV, D, B, R_REPS = 32, 8, 128, 64, 4
 TOPK, SINK, RECENT = 32, 64, 512
 CTX = 32768
 LAYERS = 36
+NSETS = 8  # distinct decode inputs in rotation (the selection changes every step)
 METRIC = "sparse decode attn us/layer @32K ctx"
 UNIT = "us/layer"
 
@@ -46,7 +50,7 @@ ATTEND_TOKENS = TOPK * B + SINK + RECENT                 # 2624 keys per kv head
 ATTEND_BYTES = ATTEND_TOKENS * HKV * D * 2 * 2 + (HQ * D * 2) * 2 + HKV * D * 2 * 2
 SELECT_BYTES = (CTX // B) * HKV * R_REPS * D * 2 + HQ * D * 2
 STEP_BYTES = ATTEND_BYTES + SELECT_BYTES
-# DRAM bytes of one attend launch measured by ncu (profiles/decode_kernel_l4.md)
+# DRAM bytes of one attend launch, recorded from an ncu capture of this kernel
 ATTEND_TRAFFIC = 10851328
 # segmented prefill operator: a 4096-token chunk after a
 # 28672-token history; visible (query, key) pairs per head x 32 heads x 4 D
@@ -418,7 +422,8 @@ def build_layers(nkv, dev, n_layers, seed):
 
 
 def cpu_reference(steps, warmup, threads):
-    """The reference algorithm's CPU path (oracle port) on one 32K layer state."""
+    """The reference algorithm's CPU path restated (oracle port) on one 32K
+    layer state: median decode call time in microseconds."""
     from oracle import m12_oracle as orc
 
     torch.set_num_threads(threads)
@@ -439,6 +444,66 @@ def cpu_reference(steps, warmup, threads):
         if i >= warmup:
             times.append(dt)
     return statistics.median(times) * 1e6, len(times)
+
+
+def reference_own(steps, warmup, threads, verify_iters=5):
+    """The reference's own torch code on the host cores: its M12LayerRuntime
+    (installed under baseline/_ref, run through the CPU device shim) decoding
+    one 32K layer state (median of `steps` calls after `warmup`), and its
+    6-query lossless verify at 28672 history (median of `verify_iters` calls,
+    each followed by rollback_verified so the state is unchanged).  Returns
+    None when the reference package is not installed."""
+    from oracle import ref_shim
+
+    if not ref_shim.reference_available():
+        return None
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(7)
+    rt = ref_shim.RefRuntime(max_model_len=CTX + 4096)
+    for c in range(CTX // 4096):
+        k = torch.randn(4096, HKV, D, generator=g).bfloat16()
+        v = torch.randn(4096, HKV, D, generator=g).bfloat16()
+        if c == 0:
+            rt.prefill_first(None, k, v)
+        else:
+            rt._store_kv(k, v)
+    times = []
+    cpu = torch.device("cpu")
+    for i in range(warmup + steps):
+        q = torch.randn(1, HQ, D, generator=g).bfloat16()
+        k = torch.randn(1, HKV, D, generator=g).bfloat16()
+        v = torch.randn(1, HKV, D, generator=g).bfloat16()
+        t = time.perf_counter()
+        rt.decode(q, k, v, cpu)
+        dt = time.perf_counter() - t
+        if i >= warmup:
+            times.append(dt)
+    decode_us = statistics.median(times) * 1e6
+    del rt
+    # BASELINE config 4, multi-token variant: 5 draft tokens + 1 at 28672
+    rv = ref_shim.RefRuntime(max_model_len=PF_HIST + 4096, verify_union_blocks=6 * TOPK)
+    for c in range(PF_HIST // 4096):
+        k = torch.randn(4096, HKV, D, generator=g).bfloat16()
+        v = torch.randn(4096, HKV, D, generator=g).bfloat16()
+        if c == 0:
+            rv.prefill_first(None, k, v)
+        else:
+            rv._store_kv(k, v)
+    rv.rt.verify_mode = True
+    rv.rt.verify_lossless = True
+    vt = []
+    for i in range(1 + verify_iters):
+        q = torch.randn(6, HQ, D, generator=g).bfloat16()
+        k = torch.randn(6, HKV, D, generator=g).bfloat16()
+        v = torch.randn(6, HKV, D, generator=g).bfloat16()
+        t = time.perf_counter()
+        rv.verify_tokens(q, k, v, cpu)
+        dt = time.perf_counter() - t
+        rv.rollback_verified()
+        if i >= 1:
+            vt.append(dt)
+    return {"decode_us": decode_us, "decode_calls": len(times),
+            "verify6_us": statistics.median(vt) * 1e6, "verify_calls": len(vt)}
 
 
 def main():
@@ -476,15 +541,25 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        us, n = cpu_reference(max(3, args.steps if args.steps < 30 else 20), max(3, args.warmup),
-                              threads)
-        line = {"impl": "reference", "metric": METRIC, "value": us, "unit": UNIT, "n_gpus": args.gpus,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": us * args.layers / 1000.0,
+        n_steps = max(3, min(args.steps, 20) if args.steps < 20 else 20)
+        own = reference_own(max(20, n_steps), max(3, args.warmup), threads)
+        port_us, n_port = cpu_reference(n_steps, max(3, args.warmup), threads)
+        if own is not None:
+            us, kind = own["decode_us"], "reference"
+            sample = (f"{own['decode_calls']} decode calls of one 32K layer state through the reference's "
+                      f"own M12LayerRuntime (torch, CPU device shim), median")
+        else:
+            us, kind = port_us, "port"
+            sample = f"{n_port} decode calls of one 32K layer state (oracle port), median"
+        line = {"impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": UNIT,
+                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(us * args.layers / 1000.0, 3),
                 "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic", "config": config,
-                "cpu_baseline": {"value": us, "unit": UNIT, "cores": threads, "kind": "port",
-                                 "sample": f"{n} decode calls of one 32K layer state (median)"},
-                "e2e": {"value": us, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+                "cpu_baseline": {"value": round(us, 1), "unit": UNIT, "cores": threads, "kind": kind,
+                                 "sample": sample, "port_value": round(port_us, 1),
+                                 "verify6_us_at_28672": None if own is None else round(own["verify6_us"], 1)},
+                "e2e": {"value": round(us, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
         return
 
@@ -505,10 +580,20 @@ def main():
     L = args.layers
     layers = build_layers(nkv, dev, L, seed=1234 + rank)
 
+    # NSETS distinct q/k/v sets per layer; step s decodes set s % NSETS, copied
+    # into a persistent staging buffer whose per-layer views are the decode
+    # inputs (as a model's qkv projection output would be), so the selection
+    # changes from step to step
+    QKV = (HQ + 2 * HKV) * D
     gq = torch.Generator(device=dev).manual_seed(99 + rank)
-    qs = torch.randn(L, 1, HQ, D, generator=gq, device=dev).bfloat16()
-    ks = torch.randn(L, 1, HKV, D, generator=gq, device=dev).bfloat16()
-    vs = torch.randn(L, 1, HKV, D, generator=gq, device=dev).bfloat16()
+    xsets = torch.randn(NSETS, L, QKV, generator=gq, device=dev).bfloat16()
+    xdev = torch.empty(L, QKV, dtype=torch.bfloat16, device=dev)
+    xdev.copy_(xsets[0])
+    views = [(xdev[li, :HQ * D].view(1, HQ, D), xdev[li, HQ * D:(HQ + HKV) * D].view(1, HKV, D),
+              xdev[li, (HQ + HKV) * D:].view(1, HKV, D)) for li in range(L)]
+    qs = [vw[0] for vw in views]
+    ks = [vw[1] for vw in views]
+    vs = [vw[2] for vw in views]
 
     stream = torch.cuda.Stream(dev)
     # warm the kernels once eagerly (workspace allocation happens here)
@@ -520,7 +605,7 @@ def main():
 
     # whole step (select + attend for every layer) recorded once and replayed
     # per token with the recent windows advancing on the device (DecodeGraph)
-    graph = nkv.DecodeGraph(layers, [(qs[li], ks[li], vs[li]) for li in range(L)], stream=stream)
+    graph = nkv.DecodeGraph(layers, views, stream=stream)
     # kernel (2) alone over the same ids, for the roofline of the dominant kernel
     ids_saved = [rt._ids[:TOPK].clone() for rt in layers]
     g_att = torch.cuda.CUDAGraph()
@@ -531,24 +616,40 @@ def main():
             rt._attend(qs[li], ids_saved[li], TOPK, sink_len, start, n, ks[li], vs[li],
                        ring_write_pos=w)
 
-    def timed(g, iters):
+    def timed(g, iters, rotate=True):
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
             ev0.record(stream)
-            for _ in range(iters):
+            for i in range(iters):
+                if rotate:
+                    xdev.copy_(xsets[i % NSETS], non_blocking=True)
                 g.replay()
             ev1.record(stream)
         ev1.synchronize()
         return ev0.elapsed_time(ev1)
 
-    for _ in range(max(3, args.warmup)):
-        graph.replay()
+    def timed_copies(iters):
+        """The per-step input copies alone (reported beside the step time)."""
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for i in range(iters):
+                xdev.copy_(xsets[i % NSETS], non_blocking=True)
+            ev1.record(stream)
+        ev1.synchronize()
+        return ev0.elapsed_time(ev1)
+
+    with torch.cuda.stream(stream):
+        for i in range(max(3, args.warmup)):
+            xdev.copy_(xsets[i % NSETS], non_blocking=True)
+            graph.replay()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     clk = Clocks(local) if rank == 0 else None
     ms = timed(graph, args.steps)
+    ms_copy = timed_copies(args.steps)
     torch.cuda.synchronize()
     if world > 1:
         t = torch.tensor([ms], device=dev)
@@ -562,27 +663,27 @@ def main():
     # dominant kernel (attend) timed alone
     for _ in range(3):
         g_att.replay()
-    att_ms = timed(g_att, args.steps) / args.steps
+    att_ms = timed(g_att, args.steps, rotate=False) / args.steps
     att_us = att_ms * 1000.0 / L
     peak, peak_kind = peaks()
     achieved = ATTEND_BYTES / (att_us * 1e-6) / 1e9
     step_gbs = STEP_BYTES / (ms_per_step * 1000.0 / L * 1e-6) / 1e9
 
     # end to end through the public API: the step's q/k/v for every layer
-    # copied from pinned host memory in one transfer, eager rt.decode per
-    # layer, the step's outputs gathered and copied back in one transfer
-    QKV = (HQ + 2 * HKV) * D
-    hqkv = torch.randn(L, QKV).bfloat16().pin_memory()
+    # copied from pinned host memory in one transfer (NSETS distinct sets in
+    # rotation), eager rt.decode per layer, the step's outputs gathered and
+    # copied back in one transfer
+    hsets = torch.randn(NSETS, L, QKV, generator=torch.Generator().manual_seed(199 + rank)).bfloat16().pin_memory()
     ho = torch.empty(L, 1, HQ, D, dtype=torch.bfloat16).pin_memory()
     e2e_steps = max(3, min(args.steps, 20))
-    # a persistent device staging buffer for the step's inputs; each layer's
-    # q, k, v are fixed views of it (as a model's qkv projection output would be)
-    xdev = torch.empty(L, QKV, dtype=torch.bfloat16, device=dev)
-    views = [(xdev[li, :HQ * D].view(1, HQ, D), xdev[li, HQ * D:(HQ + HKV) * D].view(1, HKV, D),
-              xdev[li, (HQ + HKV) * D:].view(1, HKV, D)) for li in range(L)]
+    e2e_i = [0]
+
+    def next_host_set():
+        e2e_i[0] += 1
+        return hsets[e2e_i[0] % NSETS]
     with torch.cuda.stream(stream):
         def e2e_step():
-            xdev.copy_(hqkv, non_blocking=True)
+            xdev.copy_(next_host_set(), non_blocking=True)
             outs = [rt.decode(q, k, v, dev) for rt, (q, k, v) in zip(layers, views)]
             ho.copy_(torch.stack(outs), non_blocking=True)
         for _ in range(2):
@@ -600,10 +701,10 @@ def main():
     # the same end-to-end step through DecodeGraph: the per-step copies as
     # above, the layers' decode replayed from one CUDA graph whose recent
     # windows advance on the device with every replay
-    dg = nkv.DecodeGraph(layers, views, stream=stream)
+    dg = graph
     with torch.cuda.stream(stream):
         def e2e_graph_step():
-            xdev.copy_(hqkv, non_blocking=True)
+            xdev.copy_(next_host_set(), non_blocking=True)
             ho.copy_(dg.replay(), non_blocking=True)
         for _ in range(2):
             e2e_graph_step()
@@ -635,7 +736,10 @@ def main():
     store = store_measure(nkv, dev) if rank == 0 else None
     if rank == 0:
         # the CPU baseline is timed at N = 1 only (with N > 1 other ranks share the host)
-        cpu_us, n_cpu = cpu_reference(args.cpu_steps, 3, threads) if world == 1 else (None, 0)
+        own = port = None
+        if world == 1:
+            own = reference_own(args.cpu_steps, 3, threads)
+            port = cpu_reference(args.cpu_steps, 3, threads)
         line = {
             "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
@@ -647,11 +751,16 @@ def main():
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "us_per_launch": round(att_us, 3), "bytes_per_launch": ATTEND_BYTES,
                          "traffic": ATTEND_TRAFFIC,
-                         "traffic_source": "ncu dram__bytes_read+write of one launch, "
-                                           "profiles/decode_kernel_l4.md"},
-            "cpu_baseline": None if cpu_us is None else {
-                "value": round(cpu_us, 1), "unit": UNIT, "cores": threads, "kind": "port",
-                "sample": f"{n_cpu} decode calls of one 32K layer state (median)"},
+                         "traffic_source": "recorded constant: ncu dram__bytes_read+write of one launch "
+                                           "of this kernel, from a separate capture (not measured in this run)"},
+            "cpu_baseline": None if port is None else {
+                "value": round(own["decode_us"] if own else port[0], 1), "unit": UNIT, "cores": threads,
+                "kind": "reference" if own else "port",
+                "sample": (f"{own['decode_calls']} decode calls of one 32K layer state through the reference's own "
+                           "M12LayerRuntime (torch, CPU device shim), median") if own else
+                          f"{port[1]} decode calls of one 32K layer state (oracle port), median",
+                "port_value": round(port[0], 1),
+                "verify6_us_at_28672": round(own["verify6_us"], 1) if own else None},
             "e2e": {"value": round(e2e_value, 4), "unit": UNIT, "api": "DecodeGraph.replay (all layers)",
                     "host_us_per_layer": round(graph_host_us, 2),
                     "h2d_bytes_per_step": L * (HQ + 2 * HKV) * D * 2,

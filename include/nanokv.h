@@ -162,14 +162,27 @@ int nkv_attend_last_config(int* cluster, int* splits, int* keys_per_cta);
  * The workspace is a scratch array of NKV_ATTEND_STATIC_SCRATCH_BYTES inside
  * the library, one per device; args->workspace and workspace_bytes are
  * ignored, and a call whose nkv_attend_workspace_bytes exceeds the scratch
- * fails with NKV_ERR_ARG.  The first call on a device looks the scratch up
- * (cudaGetSymbolAddress, which may load the module there): make it before any
- * stream capture.  Each call clears the scratch's error word and merge
- * counters with cudaMemsetAsync on `stream` and ignores overlap_select.
- * Calls on one device share the scratch, so calls that can overlap in time
- * (several streams or host threads) race; serialise them. */
-#define NKV_ATTEND_STATIC_SCRATCH_BYTES (8u << 20)
+ * fails with NKV_ERR_ARG.  At the reference geometry (hkv 8, hq 32, one query)
+ * that is at most 8048 keys per call: Top-32 of 64-token blocks with a 64-token
+ * sink, a 512-token recent window and the current token (2625 keys) fits, and
+ * so does any selection of up to 116 such blocks.  The first call on a device
+ * looks the scratch up (cudaGetSymbolAddress, which may load the module
+ * there): make it before any stream capture.  The address is cached per device
+ * ordinal for the life of the process, so it does not survive a
+ * cudaDeviceReset of that device.  Each call clears the scratch's error word
+ * and merge counters with cudaMemsetAsync on `stream` and ignores
+ * overlap_select.  Calls on one device share the scratch, so calls that can
+ * overlap in time (several streams or host threads) race; serialise them. */
+#define NKV_ATTEND_STATIC_SCRATCH_BYTES ((size_t)8 << 20)
 int nkv_attend_static(nkv_stream_t stream, const nkv_attend_args* args);
+
+/* The error word of the static scratch on the current device, which the
+ * kernels of nkv_attend_static write (a bounded wait that ran out, a block id
+ * outside the store).  Same contract as nkv_check on a caller workspace:
+ * synchronous on `stream`, NKV_OK when clear, NKV_ERR_DEVICE (and cleared)
+ * otherwise.  The next nkv_attend_static call clears the word, so check after
+ * each call whose result matters.  No counterpart in the reference. */
+int nkv_attend_static_check(nkv_stream_t stream);
 
 /* One decode step of a layer: nkv_select over the layer's representatives
  * for the single query, then nkv_attend of that query over the selected

@@ -97,6 +97,7 @@ SIGNATURES = {
     "nkv_attend": (c_int, [c_vp, C.POINTER(AttendArgs)]),
     "nkv_attend_last_config": (c_int, [C.POINTER(c_int), C.POINTER(c_int), C.POINTER(c_int)]),
     "nkv_attend_static": (c_int, [c_vp, C.POINTER(AttendArgs)]),
+    "nkv_attend_static_check": (c_int, [c_vp]),
     "nkv_decode_step": (c_int, [c_vp, C.POINTER(DecodeArgs)]),
     "nkv_decode_last_form": (c_int, []),
     "nkv_reload_env": (None, []),

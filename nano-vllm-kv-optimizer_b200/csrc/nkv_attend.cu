@@ -2460,11 +2460,40 @@ extern "C" int nkv_attend_last_config(int* cluster, int* splits, int* keys_per_c
 // nkv_attend path with the scratch as its workspace.  Because that memset sits
 // between a preceding selection and the attention, overlap_select is ignored.
 // All calls on one device share the scratch: calls that may run at the same
-// time (other streams, other host threads) race on it.
+// time (other streams, other host threads) race on it.  The error word the
+// kernels write stays readable through nkv_attend_static_check until the next
+// call clears it.  The scratch address is cached per device ordinal for the
+// life of the process.
 // ---------------------------------------------------------------------------
 static __device__ __align__(256) unsigned char g_attend_scratch[NKV_ATTEND_STATIC_SCRATCH_BYTES];
 static std::mutex g_attend_scratch_mu;
-static void* g_attend_scratch_ptr[64];  // per device ordinal
+static void* g_attend_scratch_ptr[64];  // per device ordinal, for the life of the process
+
+// Device address of the scratch on the current device (looked up once per
+// device, then cached).
+static int attend_scratch(const char* who, void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    set_error("%s: no usable current device (%s)", who, cudaGetErrorString(e));
+    return NKV_ERR_CUDA;
+  }
+  std::lock_guard<std::mutex> lock(g_attend_scratch_mu);
+  void* ws = g_attend_scratch_ptr[dev];
+  if (!ws) {
+    e = cudaGetSymbolAddress(&ws, g_attend_scratch);
+    if (e != cudaSuccess || !ws) {
+      cudaGetLastError();
+      set_error("%s: cudaGetSymbolAddress of the scratch failed on device %d: %s", who, dev,
+                cudaGetErrorString(e));
+      return NKV_ERR_CUDA;
+    }
+    g_attend_scratch_ptr[dev] = ws;
+  }
+  *out = ws;
+  return NKV_OK;
+}
 
 extern "C" int nkv_attend_static(nkv_stream_t stream, const nkv_attend_args* a) {
   NKV_REQUIRE(a, "attend_static: null args");
@@ -2478,28 +2507,10 @@ extern "C" int nkv_attend_static(nkv_stream_t stream, const nkv_attend_args* a) 
               "attend_static: this call needs %zu bytes of workspace but the static scratch holds %zu "
               "(fewer keys, heads or queries per call, or nkv_attend with a caller workspace)",
               need, (size_t)NKV_ATTEND_STATIC_SCRATCH_BYTES);
-  int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= 64) {
-    cudaGetLastError();
-    set_error("attend_static: no usable current device (%s)", cudaGetErrorString(e));
-    return NKV_ERR_CUDA;
-  }
   void* ws = nullptr;
-  {
-    std::lock_guard<std::mutex> lock(g_attend_scratch_mu);
-    ws = g_attend_scratch_ptr[dev];
-    if (!ws) {
-      e = cudaGetSymbolAddress(&ws, g_attend_scratch);
-      if (e != cudaSuccess || !ws) {
-        cudaGetLastError();
-        set_error("attend_static: cudaGetSymbolAddress of the scratch failed on device %d: %s", dev,
-                  cudaGetErrorString(e));
-        return NKV_ERR_CUDA;
-      }
-      g_attend_scratch_ptr[dev] = ws;
-    }
-  }
+  int rc = attend_scratch("attend_static", &ws);
+  if (rc != NKV_OK) return rc;
+  cudaError_t e;
   // error word (256 B) + per-head counters, as laid out by the attend workspace
   const size_t zero_bytes = 256 + ((size_t)(a->hkv * 4 + 255) / 256) * 256;
   e = cudaMemsetAsync(ws, 0, zero_bytes, (cudaStream_t)stream);
@@ -2513,4 +2524,14 @@ extern "C" int nkv_attend_static(nkv_stream_t stream, const nkv_attend_args* a) 
   b.workspace_bytes = NKV_ATTEND_STATIC_SCRATCH_BYTES;
   b.overlap_select = 0;
   return nkv_attend(stream, &b);
+}
+
+// The error word of the static scratch on the current device: the same
+// contract as nkv_check on a caller workspace (synchronous on `stream`,
+// NKV_ERR_DEVICE and cleared when a kernel recorded an error).
+extern "C" int nkv_attend_static_check(nkv_stream_t stream) {
+  void* ws = nullptr;
+  int rc = attend_scratch("attend_static_check", &ws);
+  if (rc != NKV_OK) return rc;
+  return nkv_check(stream, ws);
 }

@@ -1,12 +1,18 @@
-"""Run the reference's own M12 runtime on the CPU (golden-fixture generation only).
+"""Run the reference's own M12 runtime on the CPU.
+
+TEST INFRASTRUCTURE ONLY: used by ``tests/golden/make_golden.py`` (fixture
+generation) and by ``bench.py --impl reference`` (the reference arm, which times
+the reference's own ``M12LayerRuntime.decode`` on the host cores).  The product
+package never imports it.
 
 The reference (`nanovllm/sparse/m12_runtime.py`) hard-codes ``device="cuda"`` and
 ``pin_memory=True`` in its buffer allocations (m12_runtime.py:192-246).  This shim
 rewrites those two arguments for ``torch.empty/zeros/full/tensor`` while the
 reference object is built and called, so its torch code runs unmodified on the host.
 
-Used only by ``make_golden.py`` in the container that holds the reference checkout;
-nothing on a GPU box imports it.
+The reference is found at ``$NKV_REFERENCE_ROOT`` when that is set, else in
+``baseline/_ref`` under the repository root (the reference package installed
+there with ``pip install --no-deps --target baseline/_ref``).
 """
 from __future__ import annotations
 
@@ -16,7 +22,13 @@ import sys
 
 import torch
 
-REFERENCE_ROOT = os.environ.get("NKV_REFERENCE_ROOT", "/root/reference")
+_REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REFERENCE_ROOT = os.environ.get("NKV_REFERENCE_ROOT") or os.path.join(_REPO, "baseline", "_ref")
+
+
+def reference_available() -> bool:
+    return os.path.isfile(os.path.join(REFERENCE_ROOT, "nanovllm", "sparse", "m12_runtime.py"))
+
 
 _PATCHED = ("empty", "zeros", "full", "tensor", "arange", "ones")
 
@@ -48,7 +60,9 @@ def cpu_device_shim():
 
 
 def import_reference():
-    """Import the reference's runtime module (read-only checkout)."""
+    """Import the reference's runtime module."""
+    if not reference_available():
+        raise ImportError(f"reference package not found under {REFERENCE_ROOT}")
     if REFERENCE_ROOT not in sys.path:
         sys.path.insert(0, REFERENCE_ROOT)
     import nanovllm.sparse.m12_runtime as m12  # noqa: E402

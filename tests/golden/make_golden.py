@@ -1,10 +1,11 @@
 """Generate the committed golden fixtures by running the REFERENCE runtime on CPU.
 
-Run in a container that holds the reference checkout (read-only):
+Run where the reference package is importable (``baseline/_ref``, or the
+checkout named by ``$NKV_REFERENCE_ROOT``):
 
     python tests/golden/make_golden.py [--check-oracle]
 
-For each case in ``cases.py`` the reference ``M12LayerRuntime`` (via ``ref_shim``)
+For each case in ``cases.py`` the reference ``M12LayerRuntime`` (via ``oracle/ref_shim.py``)
 is driven through the case's script on seeded inputs.  The fixture stores, per
 step: the selected block ids (reference ``last_block_ids``), the representative
 token indices recovered from the reference's ``reps_gpu``, and the attention
@@ -21,8 +22,9 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 from cases import CASES, HKV, HQ, D, qkv, sample_rows  # noqa: E402
-from ref_shim import RefRuntime  # noqa: E402
+from oracle.ref_shim import RefRuntime  # noqa: E402
 
 
 def rep_indices(reps: torch.Tensor, k_blocks: torch.Tensor) -> torch.Tensor:

@@ -33,6 +33,16 @@ def test_workspace_queries_are_host_only():
     assert lib.nkv_attend_workspace_bytes(8, 32, 1, 2624) > 0
 
 
+def test_static_scratch_limit_at_reference_geometry():
+    """The largest key count nkv_attend_static takes at hkv 8 / hq 32 / one
+    query is the one the header states (8048 keys)."""
+    lib = pkg()._lib.load()
+    cap = 8 << 20
+    assert lib.nkv_attend_workspace_bytes(8, 32, 1, 8048) <= cap
+    assert lib.nkv_attend_workspace_bytes(8, 32, 1, 8049) > cap
+    assert lib.nkv_attend_workspace_bytes(8, 32, 1, 116 * 64 + 64 + 512 + 1) <= cap
+
+
 def test_argument_errors_need_no_gpu():
     nkv = pkg()
     lib = nkv._lib

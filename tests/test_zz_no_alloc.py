@@ -4,7 +4,10 @@
 Both run the same kernels on the same arguments; the outputs must agree within
 the GPU parity tolerance (max-abs 2e-2 / rel 1e-2) on two calls in a row, for
 the single-query decode kernel with either split merge and for the multi-query
-kernel.  A call whose workspace would not fit the scratch is refused.
+kernel.  A call whose workspace would not fit the scratch is refused, and an
+error the kernels record in the scratch (here: a block id outside the store,
+which the kernels' bounds check replaces by block 0 and reports) is readable
+through nkv_attend_static_check.
 """
 import ctypes as C
 import os
@@ -111,3 +114,31 @@ def test_static_scratch_rejects_oversize():
     rc = lib.nkv_attend_static(torch.cuda.current_stream().cuda_stream, C.byref(b))
     assert rc == nkv._lib.NKV_ERR_ARG
     assert "static scratch" in lib.nkv_last_error().decode()
+
+
+def test_static_scratch_error_word_is_readable():
+    nkv = pkg()
+    rt = _layer(nkv, 7)
+    ref, args, keep = _attend_args(nkv, rt, 1, 13)
+    lib = nkv._lib.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    _static(nkv, args, ref)
+    assert lib.nkv_attend_static_check(stream) == 0, lib.nkv_last_error().decode()
+    # slot 3 names a block beyond the store's capacity: the kernel's id check
+    # records the error and loads block 0 in its place
+    bad_ids = keep[3].clone()
+    bad_ids[3] = rt.cpu_blocks_cap + 7
+    b = nkv._lib.AttendArgs.from_buffer_copy(args)
+    b.block_ids = bad_ids.data_ptr()
+    out = torch.empty_like(ref)
+    b.out = out.data_ptr()
+    b.workspace, b.workspace_bytes = None, 0
+    assert lib.nkv_attend_static(stream, C.byref(b)) == 0, lib.nkv_last_error().decode()
+    assert lib.nkv_attend_static_check(stream) == nkv._lib.NKV_ERR_DEVICE
+    assert "out of range" in lib.nkv_last_error().decode()
+    # reading the word cleared it
+    assert lib.nkv_attend_static_check(stream) == 0
+    # and the next good call reports nothing
+    got = _static(nkv, args, ref)
+    assert lib.nkv_attend_static_check(stream) == 0
+    torch.testing.assert_close(got.float().cpu(), ref.float().cpu(), atol=ATOL, rtol=RTOL)
