@@ -278,6 +278,33 @@ class OracleConfig:
     quant_history: bool = False
     prefill_query_segments: int = 1
     gather_sort: bool = False
+    # decode selection variants (reference M12Config fields, m12_runtime.py:110-121)
+    dynamic_top_k: bool = False
+    dynamic_top_k_mass: float = 0.90
+    decode_relative_a: float | None = None
+    decode_relative_max_blocks: int = 48
+    decode_relative_union: bool = False
+    decode_query_window: int = 1
+
+
+def relative_select(scores: torch.Tensor, nblocks: int, protected, k: int, a: float, scale: float,
+                    max_blocks: int, union: bool) -> torch.Tensor:
+    """Relative-threshold decode selection.  Reference m12_runtime.py:1015-1031:
+    candidates are the best ``min(max_blocks, avail)`` blocks; keep those whose
+    masked score is within ln(a)/scale of the best (with ``union``, also every
+    candidate ranked below k); if none qualifies, the first k."""
+    avail = nblocks - len([p for p in protected if p < nblocks])
+    threshold = float(scores.amax()) + math.log(a) / scale
+    cap = min(max_blocks, max(1, avail))
+    order = rank_blocks(scores)
+    cand = order[:cap]
+    above = scores[cand] >= threshold
+    if union:
+        above = above | (torch.arange(cand.numel()) < k)
+    keep = cand[above]
+    if keep.numel() == 0:
+        keep = order[:k]
+    return keep.clone()
 
 
 @dataclass
@@ -305,6 +332,7 @@ class OracleLayer:
     own_ids: torch.Tensor | None = None           # selection before any override
     force_ids: torch.Tensor | None = None         # test hook: ids to use for the next step
     pending: tuple | None = None
+    q_window: list = field(default_factory=list)  # decode routing queries (decode_query_window > 1)
 
     def __post_init__(self):
         c = self.cfg
@@ -465,12 +493,43 @@ class OracleLayer:
         self.pending = None
 
     # -- decode (m12_runtime.py:1141-1346) ------------------------------------
+    def _decode_select(self, q_route):
+        """Decode block choice with the configured variant (reference
+        m12_runtime.py:1193-1198 -> _gpu_select :959-1055)."""
+        c = self.cfg
+        req = c.top_k_blocks if c.decode_top_k_blocks is None else c.decode_top_k_blocks
+        s = mask_protected(block_scores(q_route.unsqueeze(0), self.reps, self.nblocks),
+                           self.protected, self.nblocks)
+        k = select_k(self.nblocks, self.protected, req)
+        if c.decode_relative_a is not None:
+            ids = relative_select(s, self.nblocks, self.protected, k, c.decode_relative_a, c.scale,
+                                  c.decode_relative_max_blocks, c.decode_relative_union)
+        else:
+            ids = rank_blocks(s)[:k].clone()
+            if c.dynamic_top_k and k == req:
+                ids = ids[:dynamic_budget(s[ids], req, c.dynamic_top_k_mass)]
+        if c.gather_sort and ids.numel() > 1:
+            ids = ids.sort().values
+        return self._adopt(ids, s)
+
+    def _routing_query(self, q):
+        """Mean of the last decode_query_window queries (reference :1181-1190)."""
+        c = self.cfg
+        if c.decode_query_window <= 1:
+            return q[0]
+        self.q_window.append(q[0])
+        while len(self.q_window) > c.decode_query_window:
+            self.q_window.pop(0)
+        if len(self.q_window) == 1:
+            return self.q_window[0]
+        return torch.stack(self.q_window, dim=0).mean(dim=0)
+
     def decode(self, q, k, v):
         c = self.cfg
         # shift-left-and-append on the full R-slot window (m12_runtime.py:1169-1172)
         self.recent_k = torch.cat([self.recent_k[1:], k[:1]])
         self.recent_v = torch.cat([self.recent_v[1:], v[:1]])
-        ids = self._select(q[0], c.decode_top_k_blocks)
+        ids = self._decode_select(self._routing_query(q))
         hk, hv = self.gather(ids)
         sink_len = min(c.sink_tokens, self.valid_len)
         rlen = min(c.recent_tokens, self.valid_len + 1)

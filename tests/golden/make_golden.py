@@ -41,18 +41,21 @@ def rep_indices(reps: torch.Tensor, k_blocks: torch.Tensor) -> torch.Tensor:
 
 def run_case(name: str, spec: dict) -> dict:
     gen = torch.Generator().manual_seed(spec["seed"])
-    rt = RefRuntime(max_model_len=16384, **spec["cfg"])
+    rt = RefRuntime(max_model_len=max(16384, spec.get("max_model_len", 0)), **spec["cfg"])
     B = rt.cfg.block_size
     steps = []
     all_k = []
     for op in spec["script"]:
         rec = {"op": op}
-        if op[0] in ("first", "chunk"):
+        if op[0] in ("first", "chunk", "store"):
             t = op[1]
             q, k, v = qkv(gen, t)
             start = rt.rt.nblocks_filled
             if op[0] == "first":
                 rt.prefill_first(q, k, v)
+                o = None
+            elif op[0] == "store":
+                rt._store_kv(k, v)
                 o = None
             else:
                 o = rt.prefill_chunk(q, k, v, torch.device("cpu"))

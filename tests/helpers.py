@@ -74,12 +74,14 @@ class OracleReplay:
                 # outputs stay comparable; own_ids keeps the oracle's own pick
                 if op[0] != "verify" or not op[2]:
                     L.force_ids = self.golden["steps"][i]["ids"]
-            if op[0] in ("first", "chunk"):
+            if op[0] in ("first", "chunk", "store"):
                 q, k, v = qkv(self.gen, op[1])
                 out["inputs"] = (q, k, v)
                 start = L.nblocks
                 if op[0] == "first":
                     out["o"] = L.prefill_first(q, k, v)
+                elif op[0] == "store":
+                    L.store(k, v)
                 else:
                     out["o"] = L.prefill_chunk(q, k, v)
                     out["ids"], out["scores"] = L.last_ids, L.last_scores

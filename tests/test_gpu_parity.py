@@ -172,6 +172,7 @@ def test_store_kvcache_twin():
 def _runtime_for(name, **extra):
     nkv = pkg()
     cfg = dict(CASES[name]["cfg"])
+    cfg.setdefault("max_model_len", max(16384, CASES[name].get("max_model_len", 0)))
     cfg.update(extra)
     return nkv.M12LayerRuntime(0, _cfg(**cfg))
 
@@ -192,13 +193,16 @@ def _replay(name, rt, skip_chunks=False):
     for step, op in enumerate(spec["script"]):
         g = golden["steps"][step]
         out = {"op": op, "golden": g}
-        if op[0] in ("first", "chunk", "decode", "verify"):
+        if op[0] in ("first", "chunk", "store", "decode", "verify"):
             q, k, v = qkv(gen, 1 if op[0] == "decode" else op[1])
             qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
         if op[0] == "first":
             rt.prefill_first(qd, kd, vd)
             layer.store(k, v)
             layer.prefill_len = rt.prefill_len
+        elif op[0] == "store":
+            rt._store_kv(kd, vd)
+            layer.store(k, v)
         elif op[0] == "chunk":
             if skip_chunks:
                 rt._store_kv(kd, vd)
@@ -246,7 +250,8 @@ def _check_step(s):
             _close(got, g["o"])
 
 
-@pytest.mark.parametrize("name", ["decode_c1", "short"])
+@pytest.mark.parametrize("name", ["decode_c1", "short", "relative", "relative_union", "dynamic", "qwindow",
+                                  "verify28k"])
 def test_runtime_decode_matches_oracle_and_reference(name):
     rt = _runtime_for(name)
     for s in _replay(name, rt):
@@ -284,6 +289,30 @@ def test_decode_32k_matches_oracle():
         rt._store_kv(k.to(DEV), v.to(DEV))
     layer.valid_len = rt.valid_len
     assert rt.nblocks_filled == 512 and sorted(rt.protected_blocks) == sorted(layer.protected)
+    for _ in range(3):
+        q, k, v = qkv(g, 1)
+        got = rt.decode(q.to(DEV), k.to(DEV), v.to(DEV), DEV)
+        layer.force_ids = rt.last_block_ids
+        want = layer.decode(q, k, v)
+        ok, why = ids_match_modulo_ties(rt.last_block_ids, layer.own_ids, layer.last_scores)
+        assert ok, why
+        _close(got, want)
+
+
+def test_decode_128k_matches_oracle():
+    """Long-context geometry (BASELINE config 5's operator): 131072-token
+    history (2048 blocks, Top-32 of 2039 unprotected), sink 64, recent 512."""
+    nkv = pkg()
+    g = torch.Generator().manual_seed(131072)
+    layer = orc.OracleLayer(orc.OracleConfig())
+    rt = nkv.M12LayerRuntime(0, _cfg(max_model_len=131072 + 4096))
+    for _ in range(32):
+        q, k, v = qkv(g, 4096)
+        layer.store(k, v)
+        layer.prefill_len = max(layer.prefill_len, 1)
+        rt._store_kv(k.to(DEV), v.to(DEV))
+    layer.valid_len = rt.valid_len
+    assert rt.nblocks_filled == 2048 and sorted(rt.protected_blocks) == sorted(layer.protected)
     for _ in range(3):
         q, k, v = qkv(g, 1)
         got = rt.decode(q.to(DEV), k.to(DEV), v.to(DEV), DEV)
