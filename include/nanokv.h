@@ -376,6 +376,35 @@ int nkv_store_kvcache(nkv_stream_t stream, const void* key, int64_t key_stride,
                       const void* value, int64_t value_stride, void* k_cache, void* v_cache,
                       const int64_t* slot_mapping, int n, int row_elems);
 
+/* ------------------------------------------------------------------------ */
+/* The callers either side of the sparse path in a Qwen3 decoder layer (the
+ * full-model harness).  bf16 rows, fp32 arithmetic, no host synchronisation. */
+
+/* Per-head RMSNorm of q and k followed by the rotary embedding, in place on the
+ * fused qkv projection output [T][(hq + 2*hkv) * head_dim] (row_stride elements
+ * apart): for every token t and q/k head, x <- bf16(bf16(x * rsqrt(mean(x^2) +
+ * eps)) * weight), then (x1, x2) = halves of x, y1 = x1*cos - x2*sin,
+ * y2 = x2*cos + x1*sin with cos/sin = cos_sin[positions[t]] ([P][head_dim] fp32,
+ * cos in the first half).  v is untouched.  A position outside [0, P) records
+ * an error in *err (may be null) and uses row 0.  Replaces the q_norm/k_norm
+ * + rotary_emb calls of Qwen3Attention.forward (nanovllm/models/qwen3.py:91-98,
+ * nanovllm/layers/layernorm.py:16-26, nanovllm/layers/rotary_embedding.py:7-15,
+ * 138-151), which produce the q/k the sparse runtime reads. */
+int nkv_qk_norm_rope(nkv_stream_t stream, void* qkv, long long row_stride, int T, int hq, int hkv,
+                     int head_dim, const void* q_weight, const void* k_weight, const float* cos_sin,
+                     const long long* positions, long long max_positions, float eps, int* err);
+
+/* Residual add + RMSNorm over [T][H] rows (H a multiple of 8, <= 4096): with
+ * has_residual, s = x + residual (fp32), residual <- bf16(s); else s = x and
+ * residual <- x; out <- bf16(bf16(s * rsqrt(mean(s^2) + eps)) * weight).  out
+ * may alias x.  Replaces RMSNorm.forward (nanovllm/layers/layernorm.py:16-50). */
+int nkv_add_rms_norm(nkv_stream_t stream, const void* x, void* residual, const void* weight, void* out,
+                     int T, int H, float eps, int has_residual);
+
+/* SwiGLU: out[t][j] = bf16(silu(g) * u), g = gate_up[t][j], u = gate_up[t][I + j]
+ * (fp32).  Replaces SiluAndMul (nanovllm/layers/activation.py:6-11). */
+int nkv_silu_mul(nkv_stream_t stream, const void* gate_up, void* out, int T, int I);
+
 #ifdef __cplusplus
 }
 #endif

@@ -17,14 +17,18 @@ from .m12_runtime import (
     prefill_recent_slice,
 )
 from .decode_graph import DecodeGraph, DeviceRingHeads
+from .qwen3_harness import DecodeLoop, Qwen3Arch, Qwen3SparseModel
 from .sharded import KVHeadShardedLayer
 
 __all__ = [
     "DecodeGraph",
+    "DecodeLoop",
     "DeviceRingHeads",
     "KVHeadShardedLayer",
     "M12Config",
     "M12LayerRuntime",
+    "Qwen3Arch",
+    "Qwen3SparseModel",
     "dynamic_top_k_from_scores",
     "prefill_query_summaries",
     "prefill_recent_slice",

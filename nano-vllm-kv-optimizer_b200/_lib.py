@@ -121,6 +121,10 @@ SIGNATURES = {
     "nkv_query_summaries": (c_int, [c_vp, c_vp, c_int, c_i64, c_i64, c_int, c_int, c_int, c_vp]),
     "nkv_store_kvcache": (c_int, [c_vp, c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_int, c_int]),
     "nkv_selftest_div": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int]),
+    "nkv_qk_norm_rope": (c_int, [c_vp, c_vp, C.c_longlong, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp,
+                                 C.c_longlong, C.c_float, c_vp]),
+    "nkv_add_rms_norm": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, C.c_float, c_int]),
+    "nkv_silu_mul": (c_int, [c_vp, c_vp, c_vp, c_int, c_int]),
 }
 
 _lib = None

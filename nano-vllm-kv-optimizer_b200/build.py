@@ -14,7 +14,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libnanokv.so")
-SOURCES = ["nkv_capi.cu", "nkv_select.cu", "nkv_attend.cu", "nkv_store.cu", "nkv_prefill.cu", "nkv_prefill_tc.cu"]
+SOURCES = ["nkv_capi.cu", "nkv_select.cu", "nkv_attend.cu", "nkv_store.cu", "nkv_prefill.cu", "nkv_prefill_tc.cu",
+           "nkv_model.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

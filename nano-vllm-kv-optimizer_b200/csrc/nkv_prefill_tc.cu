@@ -241,9 +241,13 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
 template <int G>
 __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParams p, const __grid_constant__ TcMaps tm) {
   extern __shared__ __align__(16) unsigned char sm_raw[];
-  // [query tile][buffer] where two buffers alternate by key tile
+  // [query tile][buffer] where two buffers alternate by key tile.  Every
+  // barrier a side can run ahead on is one per buffer: the softmax threads may
+  // publish P of tile j+1 before the MMA thread has waited for tile j's, and a
+  // single P barrier would then be two phases ahead of that wait (its parity
+  // would alias and the wait would miss the completed phase).
   __shared__ __align__(8) uint64_t q_full, kv_full[TC_STAGES], kv_empty[TC_STAGES], s_full[TC_QT][2],
-      s_free[TC_QT][2], p_full[TC_QT], o_done[TC_QT][2], fin;
+      s_free[TC_QT][2], p_full[TC_QT][2], o_done[TC_QT][2], fin;
   __shared__ uint32_t s_tmem;
   __shared__ volatile int s_fail;
   unsigned char* sm = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);
@@ -276,8 +280,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParam
         mbar_init(&s_full[t][b], 1);
         mbar_init(&s_free[t][b], 128);
         mbar_init(&o_done[t][b], 1);
+        mbar_init(&p_full[t][b], 128);
       }
-      mbar_init(&p_full[t], 128);
     }
     mbar_init(&fin, 1);
     fence_mbar_init();
@@ -359,7 +363,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParam
           const unsigned char* vt = vs + st * TC_KV_BYTES;
 #pragma unroll
           for (int t = 0; t < TC_QT; ++t) {
-            tc_wait(&p_full[t], jj & 1, p.err, &s_fail);
+            tc_wait(&p_full[t][jj & 1], (jj >> 1) & 1, p.err, &s_fail);
             tc_fence_after();
             const unsigned char* pt = ps + (t * 2 + (jj & 1)) * TC_P_BYTES;
 #pragma unroll
@@ -392,6 +396,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParam
     for (int j = 0; j < ntiles; ++j) {
       const int sb = j & 1;
       tc_wait(&s_full[t][sb], (j >> 1) & 1, p.err, &s_fail);
+      __syncwarp();  // the TMEM loads below are warp-collective
       tc_fence_after();
       uint32_t sr[64];
       {
@@ -426,25 +431,29 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParam
       const bool rescale = m_new > m_ref + 8.f;
       // P buffer j % 2 is free once PV_{j-2} is done; O is current once PV_{j-1} is
       if (j >= 2) tc_wait(&o_done[t][j & 1], ((j - 2) >> 1) & 1, p.err, &s_fail);
-      if (rescale) {
-        if (m_ref != -INFINITY) {  // O and l hold partial sums at the old reference: rescale
-          tc_wait(&o_done[t][(j - 1) & 1], ((j - 1) >> 1) & 1, p.err, &s_fail);
-          const float alpha = exp2f(m_ref - m_new);
-          tc_fence_after();
+      // O and l hold partial sums at the old reference: rows whose maximum grew
+      // rescale them.  tcgen05.ld/st are warp-collective (.sync.aligned), so the
+      // whole warp takes the TMEM round trip when any of its rows needs it; the
+      // other rows scale by 1.
+      const bool own = rescale && m_ref != -INFINITY;
+      if (__any_sync(0xffffffffu, own)) {
+        tc_wait(&o_done[t][(j - 1) & 1], ((j - 1) >> 1) & 1, p.err, &s_fail);
+        __syncwarp();
+        const float alpha = own ? exp2f(m_ref - m_new) : 1.f;
+        tc_fence_after();
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            uint32_t o[32];
-            tmem_ld32(trow + o_col + cc * 32, o);
-            tmem_wait_ld();
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t o[32];
+          tmem_ld32(trow + o_col + cc * 32, o);
+          tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st32(trow + o_col + cc * 32, o);
-          }
-          tmem_wait_st();
-          l *= alpha;
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(trow + o_col + cc * 32, o);
         }
-        m_ref = m_new;
+        tmem_wait_st();
+        l *= alpha;
       }
+      if (rescale) m_ref = m_new;
       const float nbase = m_ref == -INFINITY ? 0.f : -m_ref;
       uint32_t pw[32];
       // exponent arguments and row sums on packed fp32 pairs (4 independent sum chains)
@@ -466,10 +475,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParam
             make_uint4(pw[ch * 4], pw[ch * 4 + 1], pw[ch * 4 + 2], pw[ch * 4 + 3]);
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&p_full[t]);
+      mbar_arrive(&p_full[t][j & 1]);
     }
     // epilogue: O / l -> bf16
     if (ntiles > 0) tc_wait(&o_done[t][(ntiles - 1) & 1], ((ntiles - 1) >> 1) & 1, p.err, &s_fail);
+    __syncwarp();
     tc_fence_after();
     const float inv = 1.f / l;
     __nv_bfloat16* dst = p.out + (long long)pos * p.out_row + (long long)(h * G + g) * p.out_head;

@@ -1,5 +1,8 @@
 """CPU restatement of the reference's M12 block-sparse attention path.
 
+(The same torch code also runs on a CUDA device, in fp32 with TF32 off, for
+the full-model token-parity runs; ``OracleConfig.device`` places the state.)
+
 TEST INFRASTRUCTURE ONLY.  Nothing in the product package imports this module;
 only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py`` (its ``cpu_baseline``
 leg and ``--impl reference`` arm) may use it, and there only as the checker or as
@@ -72,7 +75,7 @@ def dynamic_budget(top_scores: torch.Tensor, max_k: int, mass: float) -> int:
 def rank_blocks(scores: torch.Tensor) -> torch.Tensor:
     """Block ids ordered by (score desc, id asc)."""
     n = scores.numel()
-    ids = torch.arange(n)
+    ids = torch.arange(n, device=scores.device)
     # stable sort on -score keeps ascending ids among equal scores
     order = torch.sort(-scores.double(), stable=True).indices
     return ids[order]
@@ -96,8 +99,9 @@ def build_reps(k_blocks: torch.Tensor, r: int):
     mean = kd.mean(dim=2)                                # [H, N, D]
     mean = mean / mean.norm(dim=-1, keepdim=True).clamp_min(1e-12)
     crit = (kd * mean.unsqueeze(2)).sum(-1)              # [H, N, B] cos to mean dir
-    chosen = torch.empty(H, N, r, dtype=torch.long)
-    margins = torch.empty(H, N, r, dtype=torch.float64)
+    dev = k_blocks.device
+    chosen = torch.empty(H, N, r, dtype=torch.long, device=dev)
+    margins = torch.empty(H, N, r, dtype=torch.float64, device=dev)
 
     # step 0: first token of maximal cosine to the mean direction
     top2 = torch.topk(crit, min(2, B), dim=-1).values
@@ -108,9 +112,9 @@ def build_reps(k_blocks: torch.Tensor, r: int):
     # (``torch.maximum(max_cos, mask)`` with a zero mask, m12_runtime.py:386-389)
     # and sets already-chosen tokens to 2.0, then takes the FIRST argmin.  So the
     # pick is the first token whose max-cosine is <= 0, else the smallest one.
-    worst = torch.full((H, N, B), -math.inf)
-    taken = torch.zeros(H, N, B, dtype=torch.bool)
-    pos = torch.arange(B)
+    worst = torch.full((H, N, B), -math.inf, device=dev)
+    taken = torch.zeros(H, N, B, dtype=torch.bool, device=dev)
+    pos = torch.arange(B, device=dev)
     for s in range(1, r):
         prev = chosen[..., s - 1]
         taken.scatter_(2, prev.unsqueeze(-1), True)
@@ -164,7 +168,7 @@ def mask_protected(scores: torch.Tensor, protected, nblocks: int) -> torch.Tenso
     out = scores.clone()
     ids = [p for p in protected if 0 <= p < nblocks]
     if ids:
-        out[torch.tensor(ids, dtype=torch.long)] = -math.inf
+        out[torch.tensor(ids, dtype=torch.long, device=out.device)] = -math.inf
     return out
 
 
@@ -195,7 +199,7 @@ def select_per_query(q, reps, nblocks, protected, requested):
     top = torch.stack([rank_blocks(row)[:k] for row in s])          # [Tq, k]
     union = torch.unique(top.flatten())
     pos = torch.searchsorted(union, top.flatten()).view(top.shape)
-    allowed = torch.zeros(q.shape[0], union.numel(), dtype=torch.bool)
+    allowed = torch.zeros(q.shape[0], union.numel(), dtype=torch.bool, device=q.device)
     allowed.scatter_(1, pos, True)
     return union, allowed, s
 
@@ -215,12 +219,14 @@ def attention(q, k, v, scale, causal_from=None, disallow=None):
     g = hq // hkv
     qf = q.float().view(tq, hkv, g, d)
     logits = torch.einsum("thgd,shd->thgs", qf, k.float()) * scale
-    mask = torch.zeros(tq, s_len, dtype=torch.bool)
+    if q.is_cuda and torch.backends.cuda.matmul.allow_tf32:
+        raise RuntimeError("the oracle's fp32 attention needs TF32 matmuls disabled")
+    mask = torch.zeros(tq, s_len, dtype=torch.bool, device=q.device)
     if disallow is not None:
         mask |= disallow
     if causal_from is not None and causal_from < s_len:
-        col = torch.arange(s_len).unsqueeze(0)
-        row = torch.arange(tq).unsqueeze(1) + causal_from
+        col = torch.arange(s_len, device=q.device).unsqueeze(0)
+        row = torch.arange(tq, device=q.device).unsqueeze(1) + causal_from
         mask |= (col > row) & (col >= causal_from)
     if mask.any():
         logits = logits.masked_fill(mask[:, None, None, :], -math.inf)
@@ -285,6 +291,8 @@ class OracleConfig:
     decode_relative_max_blocks: int = 48
     decode_relative_union: bool = False
     decode_query_window: int = 1
+    # where the layer state lives ("cpu", or a CUDA device for full-model runs)
+    device: str = "cpu"
 
 
 def relative_select(scores: torch.Tensor, nblocks: int, protected, k: int, a: float, scale: float,
@@ -300,7 +308,7 @@ def relative_select(scores: torch.Tensor, nblocks: int, protected, k: int, a: fl
     cand = order[:cap]
     above = scores[cand] >= threshold
     if union:
-        above = above | (torch.arange(cand.numel()) < k)
+        above = above | (torch.arange(cand.numel(), device=scores.device) < k)
     keep = cand[above]
     if keep.numel() == 0:
         keep = order[:k]
@@ -336,12 +344,12 @@ class OracleLayer:
 
     def __post_init__(self):
         c = self.cfg
-        z = lambda n: torch.zeros(n, c.num_kv_heads, c.head_dim, dtype=c.dtype)
+        z = lambda n: torch.zeros(n, c.num_kv_heads, c.head_dim, dtype=c.dtype, device=c.device)
         self.sink_k, self.sink_v = z(c.sink_tokens), z(c.sink_tokens)
         self.recent_k, self.recent_v = z(c.recent_tokens), z(c.recent_tokens)
-        self.reps = torch.zeros(c.num_kv_heads, 0, c.r, c.head_dim, dtype=c.dtype)
-        self.rep_idx = torch.zeros(c.num_kv_heads, 0, c.r, dtype=torch.long)
-        self.rep_margin = torch.zeros(c.num_kv_heads, 0, c.r, dtype=torch.float64)
+        self.reps = torch.zeros(c.num_kv_heads, 0, c.r, c.head_dim, dtype=c.dtype, device=c.device)
+        self.rep_idx = torch.zeros(c.num_kv_heads, 0, c.r, dtype=torch.long, device=c.device)
+        self.rep_margin = torch.zeros(c.num_kv_heads, 0, c.r, dtype=torch.float64, device=c.device)
 
     # -- store (m12_runtime.py:420-513) ------------------------------------
     def store(self, k, v):
@@ -405,7 +413,7 @@ class OracleLayer:
     def gather(self, ids):
         c = self.cfg
         if ids.numel() == 0:
-            e = torch.zeros(0, c.num_kv_heads, c.head_dim, dtype=c.dtype)
+            e = torch.zeros(0, c.num_kv_heads, c.head_dim, dtype=c.dtype, device=c.device)
             return e, e.clone()
         if c.quant_history:
             ks = torch.stack([self.k_hist[i].float() * self.k_scale for i in ids.tolist()])
@@ -429,7 +437,7 @@ class OracleLayer:
     def _adopt(self, ids, scores):
         self.own_ids, self.last_scores = ids, scores
         if self.force_ids is not None:
-            ids, self.force_ids = torch.as_tensor(self.force_ids, dtype=torch.long), None
+            ids, self.force_ids = torch.as_tensor(self.force_ids, dtype=torch.long).to(ids.device), None
         self.last_ids = ids
         return ids
 
@@ -460,7 +468,7 @@ class OracleLayer:
             qs = query_summaries(q, c.prefill_query_segments)
             ids = self._select(qs, c.prefill_top_k_blocks)
         else:
-            ids = torch.as_tensor(forced_ids, dtype=torch.long)
+            ids = torch.as_tensor(forced_ids, dtype=torch.long).to(q.device)
             self.last_ids = ids
         kp, vp, cf = self._history_pack(ids, k, v)
         o = attention(q, kp, vp, c.scale, causal_from=cf)
@@ -480,7 +488,7 @@ class OracleLayer:
         kp, vp, cf = self._history_pack(ids, k, v)
         dis = None
         if lossless:
-            dis = torch.zeros(q.shape[0], kp.shape[0], dtype=torch.bool)
+            dis = torch.zeros(q.shape[0], kp.shape[0], dtype=torch.bool, device=q.device)
             dis[:, :ids.numel() * B] = ~allowed.repeat_interleave(B, dim=1)
         o = attention(q, kp, vp, c.scale, causal_from=cf, disallow=dis)
         self.pending = (k, v)

@@ -455,6 +455,32 @@ def test_reset_reuses_buffers():
     assert rt.valid_len == 256 and rt.nblocks_filled == 4
 
 
+def test_reset_then_reuse_matches_fresh_runtime():
+    """A runtime that served one sequence, was reset and then serves another
+    gives the same ids and bitwise the same outputs as a fresh runtime
+    (the reference's reset between requests, m12_runtime.py:322-349)."""
+    nkv = pkg()
+    g = torch.Generator().manual_seed(321)
+    _, ka, va = qkv(g, 4096)
+    _, kb, vb = qkv(g, 8192 + 77)
+    steps = [qkv(g, 1) for _ in range(3)]
+    used = nkv.M12LayerRuntime(0, _cfg())
+    used.prefill_first(None, ka.to(DEV), va.to(DEV))
+    for q, k, v in steps:
+        used.decode(q.to(DEV), k.to(DEV), v.to(DEV), DEV)
+    used.reset()
+    fresh = nkv.M12LayerRuntime(0, _cfg())
+    for rt in (used, fresh):
+        rt.prefill_first(None, kb[:4096].to(DEV), vb[:4096].to(DEV))
+        rt._store_kv(kb[4096:].to(DEV), vb[4096:].to(DEV))
+    for q, k, v in steps:
+        a = used.decode(q.to(DEV), k.to(DEV), v.to(DEV), DEV)
+        b = fresh.decode(q.to(DEV), k.to(DEV), v.to(DEV), DEV)
+        assert torch.equal(used.last_block_ids, fresh.last_block_ids)
+        assert torch.equal(a, b)
+    assert torch.equal(used.recent_k, fresh.recent_k)
+
+
 def test_unsupported_geometry_fails_loudly():
     nkv = pkg()
     with pytest.raises(ValueError):
