@@ -361,6 +361,56 @@ def store_measure(nkv, dev, iters=16):
                          "frac": round(gbs / peak, 4), "peak_kind": kind}}
 
 
+# the full model decoding after a 32K prompt
+MODEL_PROMPT, MODEL_CHUNK = 32768, 4096
+
+
+def model_measure(nkv, dev, steps=64, warmup=8, layer_us=None):
+    """Random-init Qwen3-4B-architecture model (36 layers) with the sparse
+    runtime in every layer: a 32768-token prompt prefilled in 4096-token chunks
+    (time to first token), then greedy decode replayed from one CUDA graph per
+    token (DecodeLoop: embedding, 36 x [norm, qkv GEMM, q/k norm + RoPE, sparse
+    decode step, o_proj GEMM, norm, gate/up GEMM, SwiGLU, down GEMM], final
+    norm, LM head, argmax, token fed back on the device)."""
+    H = nkv.qwen3_harness
+    arch = H.Qwen3Arch()
+    prompt = torch.randint(0, arch.vocab_size, (MODEL_PROMPT,), generator=torch.Generator().manual_seed(2))
+    model = H.Qwen3SparseModel(arch, lambda i: nkv.M12LayerRuntime(
+        i, nkv.M12Config(max_model_len=MODEL_PROMPT + 4096, device=dev)), device=dev, seed=0)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    tok = model.prefill(prompt, MODEL_CHUNK)
+    e1.record()
+    e1.synchronize()
+    ttft_ms = e0.elapsed_time(e1)
+    tok = model.decode_step(tok)
+    loop = H.DecodeLoop(model, tok, max_steps=warmup + steps + 8)
+    loop.run(warmup)
+    torch.cuda.synchronize()
+    st = loop.stream
+    with torch.cuda.stream(st):
+        e0.record(st)
+        for _ in range(steps):
+            loop.replay()
+        e1.record(st)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    toks = loop.hist[:warmup + steps].tolist()
+    model.check_errors()
+    loop.close()
+    del loop, model
+    torch.cuda.empty_cache()
+    rec = {"workload": "Qwen3-4B architecture (36 layers, random init bf16), 32768-token prompt in 4096-token "
+                       "chunks, greedy decode from one CUDA graph per token",
+           "decode_tok_s": round(1000.0 / ms, 1), "decode_ms_per_token": round(ms, 4),
+           "prefill_ttft_ms": round(ttft_ms, 1), "decode_steps_timed": steps,
+           "first_tokens": toks[:8]}
+    if layer_us is not None:
+        rec["sparse_attention_share"] = round(layer_us * arch.num_layers / (ms * 1000.0), 3)
+    return rec
+
+
 class Clocks:
     """nvidia-smi sampling during the timed region."""
 
@@ -521,6 +571,9 @@ def main():
                     help="run only the kernel (5) store measurement and print its record (profiling)")
     ap.add_argument("--offload-only", action="store_true",
                     help="run only the host-offload decode measurement and print its record (profiling)")
+    ap.add_argument("--model-only", action="store_true",
+                    help="run only the full-model decode measurement and print its record (profiling)")
+    ap.add_argument("--no-model", action="store_true", help="skip the full-model decode tok/s measurement")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -569,6 +622,9 @@ def main():
         return
     if args.offload_only:
         print(json.dumps({"offload": offload_measure(nkv, torch.device("cuda", 0))}))
+        return
+    if args.model_only:
+        print(json.dumps({"model": model_measure(nkv, torch.device("cuda", 0))}))
         return
     if world > 1:
         import torch.distributed as dist
@@ -734,6 +790,14 @@ def main():
     if rank == 0 and not args.no_offload:
         offload = offload_measure(nkv, dev)
     store = store_measure(nkv, dev) if rank == 0 else None
+    model = None
+    if rank == 0 and not args.no_model:
+        del graph, g_att, dg
+        graph = g_att = dg = None
+        for rt in layers:
+            rt.reset()
+        torch.cuda.empty_cache()
+        model = model_measure(nkv, dev, layer_us=value * world)
     if rank == 0:
         # the CPU baseline is timed at N = 1 only (with N > 1 other ranks share the host)
         own = port = None
@@ -777,6 +841,7 @@ def main():
             "offload": offload,
             "store": store,
             "kv_head_sharded": sharded,
+            "model": model,
         }
         print(json.dumps(line))
     del graph, g_att, dg
