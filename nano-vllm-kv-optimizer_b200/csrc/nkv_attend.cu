@@ -1774,6 +1774,372 @@ __device__ void combine_cluster(const AttendParams& p, int h, float* pm, float* 
   cluster.sync();
 }
 
+// ---------------------------------------------------------------------------
+// Tile-split decode kernel (ranked decode, bf16 block store in device memory,
+// block size 64, one query).  The grid is one cluster of CL CTAs per KV head;
+// the head's keys are cut into 64-key tiles, each one TMA box (two 64-column
+// halves) for K and one for V:
+//   early tiles  the sink, then the recent ring slice as its run before and
+//                after the physical wrap (each run cut into 64-key tiles, the
+//                last one partial): they do not depend on the selection, so
+//                they are loaded and attended while the scores are produced;
+//   selected     one tile per selected block, in rank order;
+//   current      the decode token itself (one key, from registers).
+// CTA s of a head owns early tiles s, s + CL, ... and selected ranks s,
+// s + CL, ... (two ranks and at most one early tile at CL = 16, k = 32: about
+// 170 keys per CTA on 128 SMs).  Every CTA ranks the scoring grid's block
+// scores itself (topk_threshold), so no id crosses the grid.  Within a CTA a
+// warp attends 16-key chunks (warps 0-3 the four chunks of a first tile,
+// warps 4-7 those of a second) with its own online softmax state: S = Q K^T
+// and O += P V on mma.sync m16n8k16, with P split into a bf16 head and a bf16
+// remainder (two P.V products) so that P enters the sum with ~16 significant
+// bits, as the reference's fp32 P.V does.  The warp states merge in shared
+// memory, the CTAs of the head through DSMEM (combine_cluster).
+// ---------------------------------------------------------------------------
+constexpr int DS_WARPS = 8;
+constexpr int DS_TILE_BYTES = 64 * 256;  // one K (or V) tile: [2 halves][64 rows][128 B]
+
+template <int CL>
+struct DS {
+  static constexpr int MAX_EARLY = CL >= 16 ? 1 : 2;       // early tiles per CTA (<= 10 early tiles per head)
+  static constexpr int MAX_SEL = 32 / CL;                    // selected tiles per CTA (k <= 32)
+  static constexpr int MAX_TILES = MAX_EARLY + MAX_SEL;
+  static constexpr size_t SMEM = 1024 + (size_t)MAX_TILES * 2 * DS_TILE_BYTES + 2048 + 1024;
+};
+
+// Early tile e of head h: (source, first row in its 2D map, valid rows).
+__device__ __forceinline__ void ds_early_tile(const AttendParams& p, int h, int ring_start, int e, int* src, int* y,
+                                              int* valid) {
+  const int lenA = min(p.ring_len, p.ring_cap - ring_start);
+  const int nA = (lenA + 63) >> 6;
+  if (p.sink_len > 0) {
+    if (e == 0) {
+      *src = 1;
+      *y = h * p.sink_cap;
+      *valid = p.sink_len;
+      return;
+    }
+    --e;
+  }
+  *src = 2;
+  if (e < nA) {
+    *y = h * p.ring_cap + ring_start + e * 64;
+    *valid = min(64, lenA - e * 64);
+  } else {
+    e -= nA;
+    *y = h * p.ring_cap + e * 64;
+    *valid = min(64, (p.ring_len - lenA) - e * 64);
+  }
+}
+
+__device__ __forceinline__ int ds_early_count(const AttendParams& p, int ring_start) {
+  const int lenA = min(p.ring_len, p.ring_cap - ring_start);
+  return (p.sink_len > 0 ? 1 : 0) + ((lenA + 63) >> 6) + ((p.ring_len - lenA + 63) >> 6);
+}
+
+// One warp's 16-key chunk at tile rows [r0, r0 + 16): S = Q K^T (Q rows >= 4
+// zero), mask (rows >= valid), online softmax update of (m, l) for query row
+// g = lane / 4 and of the transposed output O^T += V^T P^T, whose B operand is
+// the S accumulator of the lane as it stands (P[g][keys 2t, 2t + 1]).  ofr is
+// O^T in mma layout: ofr[mt] = O[2t | 2t + 1][16 mt + g (+ 8)], t = lane % 4
+// (query rows 2t, 2t + 1 < 4 are real for t < 2).
+__device__ __forceinline__ void ds_rescale(float (&ofr)[8][4], float alpha, int qt) {
+  const float ae = __shfl_sync(FULL, alpha, (2 * qt) * 4), ao = __shfl_sync(FULL, alpha, (2 * qt + 1) * 4);
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    ofr[mt][0] *= ae;
+    ofr[mt][1] *= ao;
+    ofr[mt][2] *= ae;
+    ofr[mt][3] *= ao;
+  }
+}
+
+__device__ __forceinline__ void ds_chunk(const unsigned char* kt, const unsigned char* vt, int r0, int valid,
+                                         const uint32_t (&qa)[8][2], float scale, float& m_run, float& l_run,
+                                         float (&ofr)[8][4], int lane) {
+  const int mrow = lane & 7, msel = lane >> 3, qt = lane & 3;
+  float s[2][4], s2[2][4];
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) s[j][e] = s2[j][e] = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < 8; kk += 2) {
+    uint32_t b[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) ldsm_x4(b[j], kt + swz(64, r0 + j * 8 + mrow, (kk + (msel >> 1)) * 16 + (msel & 1) * 8));
+#pragma unroll
+    for (int j = 0; j < 2; ++j) mma_bf16(s[j], qa[kk][0], 0u, qa[kk][1], 0u, b[j][0], b[j][1]);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) mma_bf16(s2[j], qa[kk + 1][0], 0u, qa[kk + 1][1], 0u, b[j][2], b[j][3]);
+  }
+  // lane holds row g keys r0 + 8 j + 2 qt + {0, 1} (elements 0, 1)
+  float mloc = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int key = r0 + j * 8 + 2 * qt + e;
+      const float v = key < valid ? (s[j][e] + s2[j][e]) * scale : -INFINITY;
+      s[j][e] = v;
+      mloc = fmaxf(mloc, v);
+    }
+  mloc = fmaxf(mloc, __shfl_xor_sync(FULL, mloc, 1));
+  mloc = fmaxf(mloc, __shfl_xor_sync(FULL, mloc, 2));
+  const float m_new = fmaxf(m_run, mloc);
+  // nothing visible yet: the mask does not depend on the row, so this holds
+  // for every lane or none (the mma below are warp-collective)
+  if (__all_sync(FULL, m_new == -INFINITY)) return;
+  const float alpha = m_run == -INFINITY ? 0.f : __expf(m_run - m_new);
+  float lsum = 0.f;
+  uint32_t ph[2], pl[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    float pe[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      pe[e] = s[j][e] == -INFINITY ? 0.f : __expf(s[j][e] - m_new);
+      lsum += pe[e];
+    }
+    ph[j] = pack_bf16x2(pe[0], pe[1]);
+    pl[j] = pack_bf16x2(pe[0] - bf_lo(ph[j]), pe[1] - __uint_as_float(ph[j] & 0xffff0000u));
+  }
+  lsum += __shfl_xor_sync(FULL, lsum, 1);
+  lsum += __shfl_xor_sync(FULL, lsum, 2);
+  l_run = l_run * alpha + lsum;
+  m_run = m_new;
+  ds_rescale(ofr, alpha, qt);
+  // O^T += V^T P^T: A = V^T (16 dims x 16 keys) by ldmatrix.trans of the key
+  // rows (matrix q: keys r0 + (q >> 1) * 8 + row, dims 16 mt + (q & 1) * 8),
+  // B = (P head | P remainder) from the lane's own scores
+  const int vrow = r0 + (msel >> 1) * 8 + mrow;
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    uint32_t a[4];
+    ldsm_x4_t(a, vt + swz(64, vrow, mt * 16 + (msel & 1) * 8));
+    mma_bf16(ofr[mt], a[0], a[1], a[2], a[3], ph[0], ph[1]);
+    mma_bf16(ofr[mt], a[0], a[1], a[2], a[3], pl[0], pl[1]);
+  }
+}
+
+template <int CL>
+__global__ void __launch_bounds__(DS_WARPS * 32) decode_split_kernel(const AttendParams p,
+                                                                     const __grid_constant__ DecodeMaps tm) {
+  constexpr int G = 4, NW = DS_WARPS, NT = NW * 32;
+  constexpr int MT = DS<CL>::MAX_TILES;
+  extern __shared__ __align__(16) unsigned char sm_raw[];
+  __shared__ __align__(8) uint64_t bar[MT];
+  __shared__ u64 s_sel[32];
+  __shared__ u64 s_cand[FS_CAND_MAX];
+  __shared__ unsigned s_misc[2 * NW];
+  __shared__ int s_head;
+  __shared__ int t_y[MT], t_valid[MT], t_src[MT];
+  const int split = blockIdx.x, h = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  unsigned char* sm = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);
+  unsigned char* tiles = sm;  // [MT][K | V]
+  float* pm = reinterpret_cast<float*>(sm + (size_t)MT * 2 * DS_TILE_BYTES);  // CTA partial: m[64], l[64], o[G][D]
+  float* pl = pm + 64;
+  float* po = pl + 64;
+
+  pdl_launch_dependents();
+  // recent ring: explicit, or the device-resident head (graph replay)
+  int ring_start = p.ring_start, ring_wpos = p.ring_write_pos;
+  if (p.ring_dyn) {
+    if (tid == 0) s_head = ld_relaxed_s32(p.ring_dyn);
+    __syncthreads();
+    ring_wpos = s_head;
+    ring_start = s_head + p.ring_cap - p.ring_len;
+    if (ring_start >= p.ring_cap) ring_start -= p.ring_cap;
+  }
+  const int n_early = ds_early_count(p, ring_start);
+  int n_my_early = 0;
+  for (int e = split; e < n_early && n_my_early < DS<CL>::MAX_EARLY; e += CL) ++n_my_early;
+  int n_my_sel = 0;
+  for (int r = split; r < p.n_sel && n_my_sel < DS<CL>::MAX_SEL; r += CL) ++n_my_sel;
+  const int ntiles = n_my_early + n_my_sel;
+  if (tid < MT) {
+    mbar_init(&bar[tid], 1);
+    fence_mbar_init();
+  }
+  // early tiles: loaded now (thread i issues tile i's four boxes)
+  if (tid < n_my_early) {
+    int src, y, valid;
+    ds_early_tile(p, h, ring_start, split + tid * CL, &src, &y, &valid);
+    t_src[tid] = src;
+    t_y[tid] = y;
+    t_valid[tid] = valid;
+    unsigned char* kd = tiles + (size_t)tid * 2 * DS_TILE_BYTES;
+    mbar_expect_tx(&bar[tid], 2 * DS_TILE_BYTES);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      tma_box(kd + half * (64 * 128), &tm.m[src][0][1], half * 64, y, &bar[tid]);
+      tma_box(kd + DS_TILE_BYTES + half * (64 * 128), &tm.m[src][1][1], half * 64, y, &bar[tid]);
+    }
+  }
+  // Q as the A operand (rows >= G are zero)
+  const int qg = lane >> 2, qt = lane & 3;
+  uint32_t qa[8][2];
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    if (qg < G) {
+      const __nv_bfloat16* qrow = p.q + (long long)(h * G + qg) * p.q_head + kk * 16 + 2 * qt;
+      qa[kk][0] = __ldg(reinterpret_cast<const uint32_t*>(qrow));
+      qa[kk][1] = __ldg(reinterpret_cast<const uint32_t*>(qrow + 8));
+    } else {
+      qa[kk][0] = qa[kk][1] = 0u;
+    }
+  }
+  float m_run = -INFINITY, l_run = 0.f;
+  float ofr[8][4];
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) ofr[mt][0] = ofr[mt][1] = ofr[mt][2] = ofr[mt][3] = 0.f;
+  __syncthreads();  // barrier init and early-tile table visible
+  // early tiles: warps 4t .. 4t + 3 take the four chunks of tile t
+  for (int t = 0; t < n_my_early; ++t) {
+    if ((warp >> 2) != (t & 1)) continue;
+    mbar_wait_poll(&bar[t], 0, p.err);
+    const unsigned char* kt = tiles + (size_t)t * 2 * DS_TILE_BYTES;
+    ds_chunk(kt, kt + DS_TILE_BYTES, (warp & 3) * 16, t_valid[t], qa, p.scale, m_run, l_run, ofr, lane);
+  }
+
+  // ---- selection: every CTA ranks the scoring grid's scores ----------------------------
+  pdl_wait();  // the scores are complete past this point
+  rank_topk<NW>(p.rank_scores, p.rank_n, p.n_sel, s_sel, s_cand, s_misc, nullptr);
+  if (split == 0 && h == 0 && tid < p.n_sel) {
+    p.rank_out[tid] = (long long)key_id(s_sel[tid]);
+    if (p.rank_out_scores) p.rank_out_scores[tid] = key_score(s_sel[tid]);
+  }
+  if (tid < n_my_sel) {
+    const int slot = n_my_early + tid;
+    long long id = (long long)key_id(s_sel[split + tid * CL]);
+    if (id < 0 || id >= p.max_blocks) {  // only after a bad score array
+      if (p.err) atomicExch(p.err, ERR_BAD_INDEX);
+      id = 0;
+    }
+    const int y = (int)((id * p.hkv + h) * 64);
+    t_src[slot] = 0;
+    t_y[slot] = y;
+    t_valid[slot] = 64;
+    unsigned char* kd = tiles + (size_t)slot * 2 * DS_TILE_BYTES;
+    mbar_expect_tx(&bar[slot], 2 * DS_TILE_BYTES);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      tma_box(kd + half * (64 * 128), &tm.m[0][0][1], half * 64, y, &bar[slot]);
+      tma_box(kd + DS_TILE_BYTES + half * (64 * 128), &tm.m[0][1][1], half * 64, y, &bar[slot]);
+    }
+  }
+  // selected tiles: tile n_my_early + j goes to warps 4 * ((n_my_early + j) & 1) ...
+  for (int t = n_my_early; t < ntiles; ++t) {
+    if ((warp >> 2) != (t & 1)) continue;
+    mbar_wait_poll(&bar[t], 0, p.err);
+    const unsigned char* kt = tiles + (size_t)t * 2 * DS_TILE_BYTES;
+    ds_chunk(kt, kt + DS_TILE_BYTES, (warp & 3) * 16, 64, qa, p.scale, m_run, l_run, ofr, lane);
+  }
+  // the current token: one key, attended by warp NW - 1 of the head's last CTA
+  const bool cur_owner = split == CL - 1 && p.n_cur > 0;
+  if (cur_owner && warp == NW - 1) {
+    const __nv_bfloat16* kc = p.cur_k + (long long)h * p.cur_head;
+    const __nv_bfloat16* vc = p.cur_v + (long long)h * p.cur_head;
+    // s = q_g . k (lanes of a row quad hold dims 2 qt + 8 i + {0, 1}, i.e.
+    // the qa layout: k-step kk covers dims 16 kk .. 16 kk + 15)
+    float part = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const uint32_t k0 = __ldg(reinterpret_cast<const uint32_t*>(kc + kk * 16 + 2 * qt));
+      const uint32_t k1 = __ldg(reinterpret_cast<const uint32_t*>(kc + kk * 16 + 8 + 2 * qt));
+      part = fmaf(bf_lo(qa[kk][0]), bf_lo(k0), part);
+      part = fmaf(__uint_as_float(qa[kk][0] & 0xffff0000u), __uint_as_float(k0 & 0xffff0000u), part);
+      part = fmaf(bf_lo(qa[kk][1]), bf_lo(k1), part);
+      part = fmaf(__uint_as_float(qa[kk][1] & 0xffff0000u), __uint_as_float(k1 & 0xffff0000u), part);
+    }
+    part += __shfl_xor_sync(FULL, part, 1);
+    part += __shfl_xor_sync(FULL, part, 2);
+    const float sc = part * p.scale;
+    const float m_new = fmaxf(m_run, sc);
+    const float alpha = m_run == -INFINITY ? 0.f : __expf(m_run - m_new);
+    const float pe = __expf(sc - m_new);
+    l_run = l_run * alpha + pe;
+    m_run = m_new;
+    ds_rescale(ofr, alpha, qt);
+    // lane (g, qt) holds O[2 qt | 2 qt + 1][16 mt + g (+ 8)]
+    const float pe_e = __shfl_sync(FULL, pe, (2 * qt) * 4), pe_o = __shfl_sync(FULL, pe, (2 * qt + 1) * 4);
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      const float v0 = __bfloat162float(vc[mt * 16 + qg]), v1 = __bfloat162float(vc[mt * 16 + qg + 8]);
+      ofr[mt][0] = fmaf(pe_e, v0, ofr[mt][0]);
+      ofr[mt][1] = fmaf(pe_o, v0, ofr[mt][1]);
+      ofr[mt][2] = fmaf(pe_e, v1, ofr[mt][2]);
+      ofr[mt][3] = fmaf(pe_o, v1, ofr[mt][3]);
+    }
+  }
+
+  // ---- warp states -> CTA partial -> cluster merge -----------------------------------
+  __syncthreads();  // every warp is done with the tiles
+  float* wpo = reinterpret_cast<float*>(tiles);  // [NW][G][D]
+  float* wml = wpo + NW * G * NKV_D;              // [NW][G][2]
+  if (qt < 2) {  // query rows 2 qt, 2 qt + 1
+    float* o0 = wpo + (warp * G + 2 * qt) * NKV_D;
+    float* o1 = o0 + NKV_D;
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      o0[mt * 16 + qg] = ofr[mt][0];
+      o1[mt * 16 + qg] = ofr[mt][1];
+      o0[mt * 16 + qg + 8] = ofr[mt][2];
+      o1[mt * 16 + qg + 8] = ofr[mt][3];
+    }
+  }
+  if (qg < G && qt == 0) {
+    wml[(warp * G + qg) * 2] = m_run;
+    wml[(warp * G + qg) * 2 + 1] = l_run;
+  }
+  __syncthreads();
+  for (int it = tid; it < G * (NKV_D / 4); it += NT) {
+    const int g = it / (NKV_D / 4), d4 = it % (NKV_D / 4);
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, wml[(w * G + g) * 2]);
+    float L = 0.f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float m = wml[(w * G + g) * 2];
+      if (m == -INFINITY) continue;
+      const float sw = __expf(m - M);
+      L += sw * wml[(w * G + g) * 2 + 1];
+      const float4 v = *reinterpret_cast<const float4*>(wpo + (w * G + g) * NKV_D + d4 * 4);
+      o.x = fmaf(sw, v.x, o.x);
+      o.y = fmaf(sw, v.y, o.y);
+      o.z = fmaf(sw, v.z, o.z);
+      o.w = fmaf(sw, v.w, o.w);
+    }
+    *reinterpret_cast<float4*>(po + g * NKV_D + d4 * 4) = o;
+    if (d4 == 0) {
+      pm[g] = M;
+      pl[g] = L;
+    }
+  }
+  // the decode token goes into the ring slot no CTA reads in this call
+  if (cur_owner && ring_wpos >= 0 && tid >= NT - 32) {
+    const int i = tid - (NT - 32);  // 16-byte chunks: 16 of K, 16 of V
+    const __nv_bfloat16* src = (i < 16 ? p.cur_k : p.cur_v) + (long long)h * p.cur_head + (i & 15) * 8;
+    __nv_bfloat16* dst = (i < 16 ? p.ring_k : p.ring_v) + ((long long)h * p.ring_cap + ring_wpos) * NKV_D + (i & 15) * 8;
+    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+  }
+  combine_cluster<G>(p, h, pm, pl, po);  // begins and ends with a cluster barrier
+  // device-resident ring head: the last CTA of the grid to get here (every CTA
+  // has read the head by now) advances it past the slot written above
+  if (p.ring_dyn && tid == 0) {
+    const unsigned total = gridDim.x * gridDim.y;
+    if (atomicAdd(reinterpret_cast<unsigned*>(p.ring_dyn) + 1, 1u) == total - 1u) {
+      p.ring_dyn[1] = 0;
+      int nh = s_head + 1;
+      if (nh >= p.ring_cap) nh = 0;
+      p.ring_dyn[0] = nh;
+    }
+  }
+}
+
 // Log-sum-exp merge of the splits of head h, run by the head's last CTA.
 // wbuf (shared, >= 2 * nr * splits floats) first receives every split's (m, l)
 // in one parallel load, then the per-(row, split) weights exp(m - M) / L; the
@@ -2107,6 +2473,52 @@ int attend_step(nkv_stream_t stream, const nkv_attend_args* a, const void* reps,
 }
 }  // namespace nkv
 
+// The tile-split decode kernel for a ranked single-query step: one cluster of
+// 16 CTAs per KV head where the SMs hold every head's cluster, else 8; returns
+// FS_DECLINED (nothing launched) when neither shape fits the call or the
+// device, so that the caller takes the general decode kernel.
+static int launch_split(AttendParams p, const DecodeMaps& maps, const nkv_attend_args* a, cudaStream_t st) {
+  const int early_max = (a->sink_len > 0 ? 1 : 0) + (a->ring_len + 63) / 64 + 1;
+  for (int CL : {16, 8}) {
+    const int max_early = CL >= 16 ? DS<16>::MAX_EARLY : DS<8>::MAX_EARLY;
+    if (early_max > CL * max_early || a->n_sel > 32) continue;
+    const void* kern = CL == 16 ? (const void*)decode_split_kernel<16> : (const void*)decode_split_kernel<8>;
+    const size_t smem = CL == 16 ? DS<16>::SMEM : DS<8>::SMEM;
+    if (ensure_smem(kern, smem, "attend split")) return NKV_ERR_CUDA;
+    if (CL > 8 && ensure_nonportable_cluster(kern, "attend split")) {
+      cudaGetLastError();
+      continue;
+    }
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t lc = {};
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = p.overlap;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = CL;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    lc.gridDim = dim3(CL, a->hkv);
+    lc.blockDim = dim3(DS_WARPS * 32);
+    lc.dynamicSmemBytes = smem;
+    lc.stream = st;
+    lc.attrs = attr;
+    lc.numAttrs = 2;
+    int nclusters = 0;
+    if (!cluster_occupancy(kern, lc, &nclusters) || nclusters < 1) continue;
+    p.cluster = 1;
+    p.splits = CL;
+    p.tps = (int)((p.ntok + CL - 1) / CL);
+    g_last_cluster = 1;
+    g_last_splits = CL;
+    g_last_tps = p.tps;
+    const cudaError_t le = CL == 16 ? cudaLaunchKernelEx(&lc, decode_split_kernel<16>, p, maps)
+                                    : cudaLaunchKernelEx(&lc, decode_split_kernel<8>, p, maps);
+    if (le != cudaSuccess) return check_launch("attend split");
+    return check_launch("attend split");
+  }
+  return FS_DECLINED;
+}
+
 static int attend_impl(nkv_stream_t stream, const nkv_attend_args* a, const RankArgs* rank) {
   NKV_REQUIRE(a, "attend: null args");
   NKV_SUPPORTED(a->head_dim == NKV_D, "attend: head_dim %d unsupported (128 only)", a->head_dim);
@@ -2388,6 +2800,13 @@ static int attend_impl(nkv_stream_t stream, const nkv_attend_args* a, const Rank
                     ((uintptr_t)a->sink_k & 15) == 0 && ((uintptr_t)a->sink_v & 15) == 0 &&
                     ((uintptr_t)a->ring_k & 15) == 0 && ((uintptr_t)a->ring_v & 15) == 0,
                 "attend: store, sink and ring must be 16-byte aligned");
+  }
+  if (q1 && rank && rank->scores && !rank->peer && G == 4 && a->store_kind == NKV_STORE_BF16 &&
+      a->block_size == 64 && a->n_sel >= 1 && a->n_sel <= 32 && a->sink_len <= 64 && a->n_cur == 1 &&
+      (p.tma_mask & 1) && (a->sink_len == 0 || (p.tma_mask & 2)) && (a->ring_len == 0 || (p.tma_mask & 4)) &&
+      env_int("NKV_DECODE_SPLIT", 1)) {
+    const int r = launch_split(p, maps, a, st);
+    if (r != FS_DECLINED) return r;
   }
   switch (G * 2 + (q1 ? 1 : 0)) {
 #define NKV_AT_CASE(GG, QQ)                                                                     \

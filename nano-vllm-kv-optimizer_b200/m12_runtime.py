@@ -408,9 +408,14 @@ class M12LayerRuntime:
     # lifecycle
     # ------------------------------------------------------------------
     def reset(self) -> None:
-        """Start a new sequence, keeping every buffer (reference :322-349)."""
+        """Start a new sequence, keeping every buffer (reference :322-349).
+
+        The recent ring restarts at physical slot 0, so a reused runtime lays
+        out its next sequence exactly as a fresh one (the decode kernels tile
+        the ring by physical runs)."""
         self.nblocks_filled = 0
         self.valid_len = 0
+        self._ring_head = 0
         self.prefill_len = 0
         self._last_ids_dev = self._last_ids_host = None
         self.protected_blocks.clear()
