@@ -847,9 +847,11 @@ __device__ __forceinline__ uint32_t fs_tag(uint32_t epoch) { return epoch % 0xff
 // no atomics); the block score is the max over the warps' entries, and
 // protected blocks publish -inf.  Scores are fp32 sums of exact bf16
 // products, in the tensor core's summation order.
+// s_prot (optional): shared flags of the CTA's blocks that are protected
+// (block b0 + i at index i), in place of a scan of the protected list per block.
 template <int G, int NW>
 __device__ void fs_score_publish(const AttendParams& p, int cta, uint32_t tag, unsigned (*s_part)[FS_BPC_MAX],
-                                 [[maybe_unused]] int* trc) {
+                                 [[maybe_unused]] int* trc, const unsigned char* s_prot = nullptr) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int b0 = cta * p.fs_bpc, nb = min(p.fs_bpc, p.rank_n - b0);
   if (nb <= 0) return;  // CTA-uniform
@@ -914,8 +916,12 @@ __device__ void fs_score_publish(const AttendParams& p, int cta, uint32_t tag, u
     uint32_t u = 0u;
 #pragma unroll
     for (int w = 0; w < NW; ++w) u = max(u, s_part[w][tid]);
-    for (int i = 0; i < p.fs_nprot; ++i)
-      if (__ldg(p.fs_prot + i) == b) u = f32_order(-INFINITY);
+    if (s_prot) {
+      if (s_prot[tid]) u = f32_order(-INFINITY);
+    } else {
+      for (int i = 0; i < p.fs_nprot; ++i)
+        if (__ldg(p.fs_prot + i) == b) u = f32_order(-INFINITY);
+    }
     st_relaxed_u64(p.fs_keys + b, ((unsigned long long)tag << 32) | u);
   }
 }
@@ -1079,6 +1085,7 @@ __device__ void fs_select(const AttendParams& p, uint32_t tag, u64* s_sel, u64* 
       if (p.err) atomicExch(p.err, ERR_WAIT_TIMEOUT);
       break;
     }
+    if (pending) __nanosleep(64);  // keep the polls from crowding the publishers' traffic
   }
   NKV_STAMP(trc, 40);
   topk_threshold<NW>(u, live, n, k, s_sel, s_cand, s_misc, trc);
@@ -1794,17 +1801,48 @@ __device__ void combine_cluster(const AttendParams& p, int h, float* pm, float* 
 // and O += P V on mma.sync m16n8k16, with P split into a bf16 head and a bf16
 // remainder (two P.V products) so that P enters the sum with ~16 significant
 // bits, as the reference's fp32 P.V does.  The warp states merge in shared
-// memory, the CTAs of the head through DSMEM (combine_cluster).
+// memory; each CTA of the head merges D / CL output dims, and every CTA
+// pushes the matching parts of its partial into the others with asynchronous
+// remote stores (st.async) that complete their merge barriers (no cluster
+// barrier on the way out, no remote loads).
 // ---------------------------------------------------------------------------
 constexpr int DS_WARPS = 8;
 constexpr int DS_TILE_BYTES = 64 * 256;  // one K (or V) tile: [2 halves][64 rows][128 B]
+
+// Cluster helpers: split arrive / wait barrier, the shared::cluster address of
+// a variable in another CTA's shared memory, and an asynchronous remote store
+// that completes `bytes` of the remote mbarrier's transaction count.
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+__device__ __forceinline__ uint32_t cluster_addr(const void* local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_async_v4(uint32_t raddr, float4 v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(raddr),
+               "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(rbar)
+               : "memory");
+}
+__device__ __forceinline__ void st_async_v2(uint32_t raddr, float a, float b, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(raddr), "f"(a),
+               "f"(b), "r"(rbar)
+               : "memory");
+}
 
 template <int CL>
 struct DS {
   static constexpr int MAX_EARLY = CL >= 16 ? 1 : 2;       // early tiles per CTA (<= 10 early tiles per head)
   static constexpr int MAX_SEL = 32 / CL;                    // selected tiles per CTA (k <= 32)
   static constexpr int MAX_TILES = MAX_EARLY + MAX_SEL;
-  static constexpr size_t SMEM = 1024 + (size_t)MAX_TILES * 2 * DS_TILE_BYTES + 2048 + 1024;
+  // output dims each CTA of the cluster merges, and the bytes one CTA pushes
+  // into another: its partial o for those dims of the 4 query rows, and (m, l)
+  static constexpr int SW = NKV_D / CL;
+  static constexpr int PUSH_BYTES = 4 * SW * 4 + 4 * 2 * 4;
+  // tiles, then the receive area: o [CL][4][SW], (m, l) [CL][4][2]
+  static constexpr size_t SMEM = 1024 + (size_t)MAX_TILES * 2 * DS_TILE_BYTES + (size_t)CL * PUSH_BYTES;
 };
 
 // Early tile e of head h: (source, first row in its 2D map, valid rows).
@@ -1922,8 +1960,8 @@ __device__ __forceinline__ void ds_chunk(const unsigned char* kt, const unsigned
   }
 }
 
-template <int CL>
-__global__ void __launch_bounds__(DS_WARPS * 32) decode_split_kernel(const AttendParams p,
+template <int CL, bool FUSED>
+__global__ void __launch_bounds__(DS_WARPS * 32, 2) decode_split_kernel(const AttendParams p,
                                                                      const __grid_constant__ DecodeMaps tm) {
   constexpr int G = 4, NW = DS_WARPS, NT = NW * 32;
   constexpr int MT = DS<CL>::MAX_TILES;
@@ -1934,15 +1972,60 @@ __global__ void __launch_bounds__(DS_WARPS * 32) decode_split_kernel(const Atten
   __shared__ unsigned s_misc[2 * NW];
   __shared__ int s_head;
   __shared__ int t_y[MT], t_valid[MT], t_src[MT];
+  __shared__ __align__(8) uint64_t merge_bar;  // the other CTAs' partials for this CTA's dims have landed
+  __shared__ unsigned s_part[FUSED ? NW : 1][FS_BPC_MAX];  // fused scoring: per-warp block maxima
+  __shared__ unsigned char s_pflag[FUSED ? FS_BPC_MAX : 1];   // fused scoring: protected flags of this CTA's blocks
   const int split = blockIdx.x, h = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   unsigned char* sm = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);
   unsigned char* tiles = sm;  // [MT][K | V]
-  float* pm = reinterpret_cast<float*>(sm + (size_t)MT * 2 * DS_TILE_BYTES);  // CTA partial: m[64], l[64], o[G][D]
-  float* pl = pm + 64;
-  float* po = pl + 64;
+  // every CTA of the cluster merges SW output dims: it receives each CTA's
+  // partial for them, o [CL][G][SW], and (m, l) [CL][G][2]
+  constexpr int SW = DS<CL>::SW;
+  float* recv = reinterpret_cast<float*>(sm + (size_t)MT * 2 * DS_TILE_BYTES);
+  float* recv_ml = recv + CL * G * SW;
 
+  // fused scoring (FUSED): this launch's key tag, and an L2 prefetch of the
+  // representatives this CTA scores (a prefetch reads nothing into the SM, so
+  // it may run before the wait below; every load waits)
+  uint32_t fs_tg = 0u;
+  if constexpr (FUSED) {
+    fs_tg = fs_tag(ld_relaxed_u32(p.fs_sync));
+    for (int i = tid; i < NW * FS_BPC_MAX; i += NT) (&s_part[0][0])[i] = 0u;
+    if (tid < FS_BPC_MAX) s_pflag[tid] = 0;
+    const int b0 = (h * CL + split) * p.fs_bpc, nb = min(p.fs_bpc, p.rank_n - b0);
+    if (tid < p.hkv && nb > 0)
+      prefetch_l2_bulk(p.fs_reps + ((long long)tid * p.fs_reps_blocks + b0) * p.fs_r * NKV_D,
+                       (uint32_t)(nb * p.fs_r * NKV_D * 2));
+  }
   pdl_launch_dependents();
+  // With fused scoring the preceding kernel may produce q, the current token,
+  // the representatives or the sink / ring: everything below waits for it.
+  // Otherwise the preceding kernel is the scoring grid, which itself waited
+  // for its predecessor before releasing this grid: only the scores wait.
+  if (FUSED) pdl_wait();
+  // Q as the A operand (rows >= G are zero); the loads are in flight while
+  // the ring head and the protected list are read
+  const int qg = lane >> 2, qt = lane & 3;
+  uint32_t qa[8][2];
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    if (qg < G) {
+      const __nv_bfloat16* qrow = p.q + (long long)(h * G + qg) * p.q_head + kk * 16 + 2 * qt;
+      qa[kk][0] = __ldg(reinterpret_cast<const uint32_t*>(qrow));
+      qa[kk][1] = __ldg(reinterpret_cast<const uint32_t*>(qrow + 8));
+    } else {
+      qa[kk][0] = qa[kk][1] = 0u;
+    }
+  }
+  if constexpr (FUSED) {
+    __syncthreads();  // the flags were cleared before the wait
+    const int b0 = (h * CL + split) * p.fs_bpc;
+    for (int i = tid; i < p.fs_nprot; i += NT) {
+      const int b = __ldg(p.fs_prot + i) - b0;
+      if (b >= 0 && b < p.fs_bpc) s_pflag[b] = 1;
+    }
+  }
   // recent ring: explicit, or the device-resident head (graph replay)
   int ring_start = p.ring_start, ring_wpos = p.ring_write_pos;
   if (p.ring_dyn) {
@@ -1958,10 +2041,15 @@ __global__ void __launch_bounds__(DS_WARPS * 32) decode_split_kernel(const Atten
   int n_my_sel = 0;
   for (int r = split; r < p.n_sel && n_my_sel < DS<CL>::MAX_SEL; r += CL) ++n_my_sel;
   const int ntiles = n_my_early + n_my_sel;
-  if (tid < MT) {
-    mbar_init(&bar[tid], 1);
-    fence_mbar_init();
+  if (tid < MT) mbar_init(&bar[tid], 1);
+  if (tid == MT) {
+    mbar_init(&merge_bar, 1);
+    mbar_expect_tx(&merge_bar, (CL - 1) * DS<CL>::PUSH_BYTES);  // the one arrival; the rest are st.async bytes
   }
+  if (tid <= MT) fence_mbar_init();
+  // every CTA's merge barrier is initialised before any CTA of the cluster
+  // stores into it: each CTA arrives here and waits before its pushes
+  cluster_arrive_release();
   // early tiles: loaded now (thread i issues tile i's four boxes)
   if (tid < n_my_early) {
     int src, y, valid;
@@ -1977,24 +2065,14 @@ __global__ void __launch_bounds__(DS_WARPS * 32) decode_split_kernel(const Atten
       tma_box(kd + DS_TILE_BYTES + half * (64 * 128), &tm.m[src][1][1], half * 64, y, &bar[tid]);
     }
   }
-  // Q as the A operand (rows >= G are zero)
-  const int qg = lane >> 2, qt = lane & 3;
-  uint32_t qa[8][2];
-#pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
-    if (qg < G) {
-      const __nv_bfloat16* qrow = p.q + (long long)(h * G + qg) * p.q_head + kk * 16 + 2 * qt;
-      qa[kk][0] = __ldg(reinterpret_cast<const uint32_t*>(qrow));
-      qa[kk][1] = __ldg(reinterpret_cast<const uint32_t*>(qrow + 8));
-    } else {
-      qa[kk][0] = qa[kk][1] = 0u;
-    }
-  }
   float m_run = -INFINITY, l_run = 0.f;
   float ofr[8][4];
 #pragma unroll
   for (int mt = 0; mt < 8; ++mt) ofr[mt][0] = ofr[mt][1] = ofr[mt][2] = ofr[mt][3] = 0.f;
   __syncthreads();  // barrier init and early-tile table visible
+  // fused scoring: this CTA's blocks are scored and published first, so that
+  // the other CTAs' keys arrive while the early tiles are attended
+  if constexpr (FUSED) fs_score_publish<G, NW>(p, h * CL + split, fs_tg, s_part, nullptr, s_pflag);
   // early tiles: warps 4t .. 4t + 3 take the four chunks of tile t
   for (int t = 0; t < n_my_early; ++t) {
     if ((warp >> 2) != (t & 1)) continue;
@@ -2003,9 +2081,15 @@ __global__ void __launch_bounds__(DS_WARPS * 32) decode_split_kernel(const Atten
     ds_chunk(kt, kt + DS_TILE_BYTES, (warp & 3) * 16, t_valid[t], qa, p.scale, m_run, l_run, ofr, lane);
   }
 
-  // ---- selection: every CTA ranks the scoring grid's scores ----------------------------
-  pdl_wait();  // the scores are complete past this point
-  rank_topk<NW>(p.rank_scores, p.rank_n, p.n_sel, s_sel, s_cand, s_misc, nullptr);
+  // ---- selection: every CTA ranks the block scores itself -----------------------------
+  if constexpr (FUSED) {
+    // the top n_sel of every CTA's keys, once they all carry this launch's tag
+    fs_select<NW>(p, fs_tg, s_sel, s_cand, s_misc, nullptr);
+    if (tid == 0) fs_arrive(p);
+  } else {
+    pdl_wait();  // the scoring grid's scores are complete past this point
+    rank_topk<NW>(p.rank_scores, p.rank_n, p.n_sel, s_sel, s_cand, s_misc, nullptr);
+  }
   if (split == 0 && h == 0 && tid < p.n_sel) {
     p.rank_out[tid] = (long long)key_id(s_sel[tid]);
     if (p.rank_out_scores) p.rank_out_scores[tid] = key_score(s_sel[tid]);
@@ -2094,6 +2178,7 @@ __global__ void __launch_bounds__(DS_WARPS * 32) decode_split_kernel(const Atten
     wml[(warp * G + qg) * 2 + 1] = l_run;
   }
   __syncthreads();
+  cluster_wait_acquire();
   for (int it = tid; it < G * (NKV_D / 4); it += NT) {
     const int g = it / (NKV_D / 4), d4 = it % (NKV_D / 4);
     float M = -INFINITY;
@@ -2113,10 +2198,21 @@ __global__ void __launch_bounds__(DS_WARPS * 32) decode_split_kernel(const Atten
       o.z = fmaf(sw, v.z, o.z);
       o.w = fmaf(sw, v.w, o.w);
     }
-    *reinterpret_cast<float4*>(po + g * NKV_D + d4 * 4) = o;
-    if (d4 == 0) {
-      pm[g] = M;
-      pl[g] = L;
+    // the CTA partial goes to the CTAs that merge its dims: to this CTA by a
+    // plain store, to the others by asynchronous remote stores that complete
+    // their merge barriers; (m, l) goes to every CTA of the cluster
+    const int r = (d4 * 4) / SW;
+    float* dst_o = recv + ((size_t)split * G + g) * SW + (d4 * 4) % SW;
+    if (r == split) *reinterpret_cast<float4*>(dst_o) = o;
+    else st_async_v4(cluster_addr(dst_o, r), o, cluster_addr(&merge_bar, r));
+    if (d4 < CL) {  // (m, l) of row g to CTA d4 (one remote store per thread)
+      float* dst_ml = recv_ml + ((size_t)split * G + g) * 2;
+      if (d4 == split) {
+        dst_ml[0] = M;
+        dst_ml[1] = L;
+      } else {
+        st_async_v2(cluster_addr(dst_ml, d4), M, L, cluster_addr(&merge_bar, d4));
+      }
     }
   }
   // the decode token goes into the ring slot no CTA reads in this call
@@ -2126,7 +2222,25 @@ __global__ void __launch_bounds__(DS_WARPS * 32) decode_split_kernel(const Atten
     __nv_bfloat16* dst = (i < 16 ? p.ring_k : p.ring_v) + ((long long)h * p.ring_cap + ring_wpos) * NKV_D + (i & 15) * 8;
     *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
   }
-  combine_cluster<G>(p, h, pm, pl, po);  // begins and ends with a cluster barrier
+  // this CTA's dims: wait for every CTA's partial, merge, write the output
+  __syncthreads();  // this CTA's own stores into the receive area
+  mbar_wait_poll(&merge_bar, 0, p.err);
+  if (tid < G * SW) {
+    const int g = tid / SW, d = tid % SW;
+    float M = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < CL; ++c) M = fmaxf(M, recv_ml[(c * G + g) * 2]);
+    float L = 0.f, o = 0.f;
+#pragma unroll
+    for (int c = 0; c < CL; ++c) {
+      const float m = recv_ml[(c * G + g) * 2];
+      if (m == -INFINITY) continue;
+      const float sw = __expf(m - M);
+      L = fmaf(sw, recv_ml[(c * G + g) * 2 + 1], L);
+      o = fmaf(sw, recv[(c * G + g) * SW + d], o);
+    }
+    p.out[(long long)(h * G + g) * p.out_head + split * SW + d] = __float2bfloat16(o / L);
+  }
   // device-resident ring head: the last CTA of the grid to get here (every CTA
   // has read the head by now) advances it past the slot written above
   if (p.ring_dyn && tid == 0) {
@@ -2413,6 +2527,7 @@ struct RankArgs {
   int nprot;
   void* sel_ws;  // select workspace: epoch at +16, arrivals at +20, keys at +256
   int32_t* ring_head;  // device-resident recent-ring head [head, arrivals] (decode kernel) or null
+  int split_only;      // one-launch step: the fused tile-split kernel only (FS_DECLINED otherwise)
 };
 static bool g_fs_unavailable = false;  // the cooperative cluster launch was refused once
 
@@ -2450,7 +2565,7 @@ int attend_ranked(nkv_stream_t stream, const nkv_attend_args* a, const float* sc
                 "current token",
                 a->ring_len, a->ring_cap);
   }
-  RankArgs r{scores, nblocks, out_ids, out_scores, peer, out_full, nullptr, 0, 0, nullptr, 0, nullptr, ring_head};
+  RankArgs r{scores, nblocks, out_ids, out_scores, peer, out_full, nullptr, 0, 0, nullptr, 0, nullptr, ring_head, 0};
   return attend_impl(stream, a, &r);
 }
 
@@ -2459,16 +2574,23 @@ int attend_ranked(nkv_stream_t stream, const nkv_attend_args* a, const float* sc
 // apply; the caller then runs the scoring grid and the ranked attention.
 int attend_step(nkv_stream_t stream, const nkv_attend_args* a, const void* reps, int r, int reps_blocks,
                 int nblocks, const int32_t* prot, int nprot, void* sel_ws, size_t sel_ws_bytes, int64_t* out_ids,
-                float* out_scores) {
+                float* out_scores, int32_t* ring_head, int split_only) {
   NKV_REQUIRE(a && a->nq == 1 && reps && out_ids && sel_ws, "decode step: null argument");
   NKV_REQUIRE(a->n_sel >= 1 && a->n_sel <= nblocks && nblocks <= reps_blocks, "decode step: k=%d, nblocks=%d",
               a->n_sel, nblocks);
   NKV_REQUIRE(nprot == 0 || prot, "decode step: protected ids missing");
   NKV_REQUIRE(((uintptr_t)reps & 15) == 0, "decode step: reps must be 16-byte aligned");
   NKV_REQUIRE(sel_ws_bytes >= nkv_select_workspace_bytes(reps_blocks, 1), "decode step: select workspace too small");
-  if (g_fs_unavailable || a->n_sel > 32 || r < 1 || r > 4 || r == 3 || nblocks > FS_MAXE * NKV_DECODE_WARPS * 32)
+  if ((g_fs_unavailable && !split_only) || a->n_sel > 32 || r < 1 || r > 4 || r == 3 ||
+      nblocks > FS_MAXE * NKV_DECODE_WARPS * 32)
     return FS_DECLINED;
-  RankArgs ra{nullptr, nblocks, out_ids, out_scores, nullptr, nullptr, reps, r, reps_blocks, prot, nprot, sel_ws};
+  if (ring_head)
+    NKV_REQUIRE(((uintptr_t)ring_head & 7) == 0 && a->n_cur == 1 && a->ring_cap >= 1 && a->ring_write_pos >= 0 &&
+                    a->ring_len == a->ring_cap - 1 && a->ring_k && a->ring_v,
+                "decode step: a device ring head needs a full recent window (ring_len %d, cap %d)", a->ring_len,
+                a->ring_cap);
+  RankArgs ra{nullptr, nblocks, out_ids, out_scores, nullptr, nullptr, reps, r, reps_blocks, prot, nprot, sel_ws,
+              ring_head, split_only};
   return attend_impl(stream, a, &ra);
 }
 }  // namespace nkv
@@ -2477,12 +2599,18 @@ int attend_step(nkv_stream_t stream, const nkv_attend_args* a, const void* reps,
 // 16 CTAs per KV head where the SMs hold every head's cluster, else 8; returns
 // FS_DECLINED (nothing launched) when neither shape fits the call or the
 // device, so that the caller takes the general decode kernel.
+template <bool FUSED>
 static int launch_split(AttendParams p, const DecodeMaps& maps, const nkv_attend_args* a, cudaStream_t st) {
   const int early_max = (a->sink_len > 0 ? 1 : 0) + (a->ring_len + 63) / 64 + 1;
   for (int CL : {16, 8}) {
     const int max_early = CL >= 16 ? DS<16>::MAX_EARLY : DS<8>::MAX_EARLY;
     if (early_max > CL * max_early || a->n_sel > 32) continue;
-    const void* kern = CL == 16 ? (const void*)decode_split_kernel<16> : (const void*)decode_split_kernel<8>;
+    if (FUSED) {
+      p.fs_bpc = (p.rank_n + CL * a->hkv - 1) / (CL * a->hkv);
+      if (p.fs_bpc > FS_BPC_MAX) continue;
+    }
+    const void* kern =
+        CL == 16 ? (const void*)decode_split_kernel<16, FUSED> : (const void*)decode_split_kernel<8, FUSED>;
     const size_t smem = CL == 16 ? DS<16>::SMEM : DS<8>::SMEM;
     if (ensure_smem(kern, smem, "attend split")) return NKV_ERR_CUDA;
     if (CL > 8 && ensure_nonportable_cluster(kern, "attend split")) {
@@ -2511,8 +2639,8 @@ static int launch_split(AttendParams p, const DecodeMaps& maps, const nkv_attend
     g_last_cluster = 1;
     g_last_splits = CL;
     g_last_tps = p.tps;
-    const cudaError_t le = CL == 16 ? cudaLaunchKernelEx(&lc, decode_split_kernel<16>, p, maps)
-                                    : cudaLaunchKernelEx(&lc, decode_split_kernel<8>, p, maps);
+    const cudaError_t le = CL == 16 ? cudaLaunchKernelEx(&lc, decode_split_kernel<16, FUSED>, p, maps)
+                                    : cudaLaunchKernelEx(&lc, decode_split_kernel<8, FUSED>, p, maps);
     if (le != cudaSuccess) return check_launch("attend split");
     return check_launch("attend split");
   }
@@ -2755,7 +2883,7 @@ static int attend_impl(nkv_stream_t stream, const nkv_attend_args* a, const Rank
   cudaStream_t st = (cudaStream_t)stream;
   const bool q1 = a->nq == 1;
   p.overlap = pg.overlap = a->overlap_select ? 1 : 0;
-  if (one_launch) {
+  if (one_launch && !rank->split_only) {
     // every CTA of the grid waits for every other CTA's keys: cluster mode
     // only, as one cooperative launch (all CTAs co-resident), no overlap
     // with the preceding kernel
@@ -2805,9 +2933,18 @@ static int attend_impl(nkv_stream_t stream, const nkv_attend_args* a, const Rank
       a->block_size == 64 && a->n_sel >= 1 && a->n_sel <= 32 && a->sink_len <= 64 && a->n_cur == 1 &&
       (p.tma_mask & 1) && (a->sink_len == 0 || (p.tma_mask & 2)) && (a->ring_len == 0 || (p.tma_mask & 4)) &&
       env_int("NKV_DECODE_SPLIT", 1)) {
-    const int r = launch_split(p, maps, a, st);
+    const int r = launch_split<false>(p, maps, a, st);
     if (r != FS_DECLINED) return r;
   }
+  // one-launch step: the fused form of the same kernel where it applies
+  if (q1 && one_launch && G == 4 && a->store_kind == NKV_STORE_BF16 && a->block_size == 64 && a->n_sel >= 1 &&
+      a->n_sel <= 32 && a->sink_len <= 64 && a->n_cur == 1 && (p.tma_mask & 1) &&
+      (a->sink_len == 0 || (p.tma_mask & 2)) && (a->ring_len == 0 || (p.tma_mask & 4)) &&
+      env_int("NKV_DECODE_SPLIT", 1)) {
+    const int r = launch_split<true>(p, maps, a, st);
+    if (r != FS_DECLINED) return r;
+  }
+  if (one_launch && rank->split_only) return FS_DECLINED;
   switch (G * 2 + (q1 ? 1 : 0)) {
 #define NKV_AT_CASE(GG, QQ)                                                                     \
   case GG * 2 + (QQ ? 1 : 0): {                                                                 \

@@ -97,9 +97,26 @@ extern "C" int nkv_decode_step(nkv_stream_t stream, const nkv_decode_args* a) {
     b.overlap_select = 0;
     const int rc = nkv::attend_step(stream, &b, a->reps, a->r, a->reps_blocks, a->nblocks, a->protected_ids,
                                     a->n_protected, a->select_workspace, a->select_workspace_bytes, a->out_ids,
-                                    a->out_topk_scores);
+                                    a->out_topk_scores, nullptr, 0);
     if (rc != nkv::FS_DECLINED) {
       g_decode_form = 1;
+      return rc;
+    }
+  }
+  // one launch of the tile-split kernel with the scoring inside (bf16 block
+  // store in device memory, 64-token blocks, G = 4, k <= 32); NKV_DECODE_SPLIT=0
+  // or a call outside that cover takes the two launches below
+  if (nkv::knob("NKV_DECODE_SPLIT", 1) != 0 && nkv::knob("NKV_SPLIT_FUSED", 0) != 0 && a->k <= 32 &&
+      a->nblocks <= 2048) {
+    nkv_attend_args b = t;
+    b.block_ids = a->out_ids;
+    b.n_sel = a->k;
+    b.overlap_select = nkv::knob("NKV_PDL", 1) != 0 ? 1 : 0;
+    const int rc = nkv::attend_step(stream, &b, a->reps, a->r, a->reps_blocks, a->nblocks, a->protected_ids,
+                                    a->n_protected, a->select_workspace, a->select_workspace_bytes, a->out_ids,
+                                    a->out_topk_scores, a->ring_head, 1);
+    if (rc != nkv::FS_DECLINED) {
+      g_decode_form = 4;
       return rc;
     }
   }

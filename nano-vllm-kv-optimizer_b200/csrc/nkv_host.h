@@ -129,9 +129,13 @@ int attend_ranked(nkv_stream_t stream, const nkv_attend_args* args, const float*
 // where the configuration is outside it (the caller then runs select_scores +
 // attend_ranked).
 constexpr int FS_DECLINED = 1;
+// ring_head: a device-resident recent-ring head (graph replay) or null;
+// split_only: launch only the fused tile-split kernel (FS_DECLINED where it
+// does not apply), not the cooperative one-launch decode kernel.
 int attend_step(nkv_stream_t stream, const nkv_attend_args* args, const void* reps, int r, int reps_blocks,
                 int nblocks, const int32_t* protected_ids, int n_protected, void* select_workspace,
-                size_t select_workspace_bytes, int64_t* out_ids, float* out_scores);
+                size_t select_workspace_bytes, int64_t* out_ids, float* out_scores, int32_t* ring_head,
+                int split_only);
 
 // prefill_tc: kernel (4) on tcgen05/TMEM for the calls it supports (bf16
 // history in device memory, block_size 64, TMA-addressable tensors); returns
