@@ -24,6 +24,7 @@ reference arm when the package is absent).
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -50,8 +51,9 @@ ATTEND_TOKENS = TOPK * B + SINK + RECENT                 # 2624 keys per kv head
 ATTEND_BYTES = ATTEND_TOKENS * HKV * D * 2 * 2 + (HQ * D * 2) * 2 + HKV * D * 2 * 2
 SELECT_BYTES = (CTX // B) * HKV * R_REPS * D * 2 + HQ * D * 2
 STEP_BYTES = ATTEND_BYTES + SELECT_BYTES
-# DRAM bytes of one attend launch, recorded from an ncu capture of this kernel
-ATTEND_TRAFFIC = 10851328
+# DRAM bytes of one launch of the step's attention kernel (decode_split_kernel),
+# recorded from a separate ncu capture of this kernel
+ATTEND_TRAFFIC = 10816000
 # segmented prefill operator: a 4096-token chunk after a
 # 28672-token history; visible (query, key) pairs per head x 32 heads x 4 D
 PF_CHUNK, PF_HIST = 4096, 28672
@@ -662,15 +664,21 @@ def main():
     # whole step (select + attend for every layer) recorded once and replayed
     # per token with the recent windows advancing on the device (DecodeGraph)
     graph = nkv.DecodeGraph(layers, views, stream=stream)
-    # kernel (2) alone over the same ids, for the roofline of the dominant kernel
-    ids_saved = [rt._ids[:TOPK].clone() for rt in layers]
+    # kernel (2) alone, for the roofline of the dominant kernel: the step's
+    # attention kernel (tile-split, it ranks the block scores itself) on each
+    # layer's block scores saved from one scoring pass, back to back
+    with torch.cuda.stream(stream):
+        scores_saved = [rt.block_scores_dev(qs[li]).clone() for li, rt in enumerate(layers)]
+    stream.synchronize()
     g_att = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_att, stream=stream):
         for li, rt in enumerate(layers):
-            sink_len = min(SINK, rt.valid_len)
-            w, start, n, _ = nkv.m12_runtime.ring_decode_plan(rt._ring_head, rt.valid_len, RECENT)
-            rt._attend(qs[li], ids_saved[li], TOPK, sink_len, start, n, ks[li], vs[li],
-                       ring_write_pos=w)
+            d, _, _ = rt._decode_fill(qs[li], ks[li], vs[li], TOPK)
+            a = nkv._lib.AttendArgs.from_buffer_copy(d.attend)
+            a.block_ids, a.n_sel, a.overlap_select = rt._ids.data_ptr(), TOPK, 0
+            nkv._lib.call("nkv_attend_ranked", stream.cuda_stream, ctypes.byref(a), scores_saved[li].data_ptr(),
+                          scores_saved[li].numel(), rt._ids.data_ptr(), rt._topk_scores.data_ptr())
+    att_kernel = "decode_split_kernel" if nkv._lib.attend_last_config()[0] == 2 else "decode_kernel"
 
     def timed(g, iters, rotate=True):
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -810,7 +818,7 @@ def main():
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) K/V/Q)", "config": config,
             "step_hbm_gbs": round(step_gbs, 1),
-            "roofline": {"bound": "hbm", "kernel": "nkv attend (kernel 2)",
+            "roofline": {"bound": "hbm", "kernel": f"{att_kernel} (kernel 2), ranked on saved block scores",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "us_per_launch": round(att_us, 3), "bytes_per_launch": ATTEND_BYTES,

@@ -148,8 +148,9 @@ typedef struct nkv_attend_args {
 size_t nkv_attend_workspace_bytes(int hkv, int hq, int nq, int max_tokens);
 int nkv_attend(nkv_stream_t stream, const nkv_attend_args* args);
 /* Launch shape chosen by the last nkv_attend on the calling thread: whether the
- * splits of a head were merged inside a thread-block cluster, the number of
- * splits per head and the keys per CTA.  Host only (no GPU work). */
+ * splits of a head were merged inside a thread-block cluster (0: no, 1: yes,
+ * 2: yes, by the tile-split decode kernel of a ranked single-query call), the
+ * number of splits per head and the keys per CTA.  Host only (no GPU work). */
 int nkv_attend_last_config(int* cluster, int* splits, int* keys_per_cta);
 
 /* nkv_attend without a caller workspace.  No counterpart in the reference (its

@@ -1812,8 +1812,8 @@ constexpr int DS_TILE_BYTES = 64 * 256;  // one K (or V) tile: [2 halves][64 row
 // Cluster helpers: split arrive / wait barrier, the shared::cluster address of
 // a variable in another CTA's shared memory, and an asynchronous remote store
 // that completes `bytes` of the remote mbarrier's transaction count.
-__device__ __forceinline__ void cluster_arrive_release() {
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void cluster_wait_acquire() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 __device__ __forceinline__ uint32_t cluster_addr(const void* local, uint32_t rank) {
@@ -1845,118 +1845,159 @@ struct DS {
   static constexpr size_t SMEM = 1024 + (size_t)MAX_TILES * 2 * DS_TILE_BYTES + (size_t)CL * PUSH_BYTES;
 };
 
-// Early tile e of head h: (source, first row in its 2D map, valid rows).
-__device__ __forceinline__ void ds_early_tile(const AttendParams& p, int h, int ring_start, int e, int* src, int* y,
-                                              int* valid) {
-  const int lenA = min(p.ring_len, p.ring_cap - ring_start);
-  const int nA = (lenA + 63) >> 6;
+// Early tiles: the sink (one tile of sink_len rows), then the ring in its
+// physical order, 64 slots per tile (softmax is order-independent, so the
+// tiles do not depend on the ring head: they are issued before the head is
+// read, and the head only decides which of their rows are attended).
+// Early tile e of head h: (source, first row in its 2D map).
+__device__ __forceinline__ void ds_early_tile(const AttendParams& p, int h, int e, int* src, int* y) {
   if (p.sink_len > 0) {
     if (e == 0) {
       *src = 1;
       *y = h * p.sink_cap;
-      *valid = p.sink_len;
       return;
     }
     --e;
   }
   *src = 2;
-  if (e < nA) {
-    *y = h * p.ring_cap + ring_start + e * 64;
-    *valid = min(64, lenA - e * 64);
-  } else {
-    e -= nA;
-    *y = h * p.ring_cap + e * 64;
-    *valid = min(64, (p.ring_len - lenA) - e * 64);
+  *y = h * p.ring_cap + e * 64;
+}
+
+__device__ __forceinline__ int ds_early_count(const AttendParams& p) {
+  return (p.sink_len > 0 ? 1 : 0) + (p.ring_len > 0 ? (p.ring_cap + 63) >> 6 : 0);
+}
+
+// Rows of a tile that are attended: row r is a key iff r < rows and
+// (r + off) mod cap < len.  Selected and sink tiles use the first rows; a
+// ring tile starting at slot b attends the slots of the window
+// [ring_start, ring_start + ring_len) mod ring_cap.
+struct DsMask {
+  int rows, off, cap, len;
+};
+__device__ __forceinline__ DsMask ds_mask_rows(int rows) { return DsMask{rows, 0, 1 << 30, 1 << 30}; }
+__device__ __forceinline__ DsMask ds_early_mask(const AttendParams& p, int e, int ring_start) {
+  if (p.sink_len > 0) {
+    if (e == 0) return ds_mask_rows(p.sink_len);
+    --e;
   }
+  const int b = e * 64;
+  int off = b - ring_start;
+  if (off < 0) off += p.ring_cap;
+  return DsMask{min(64, p.ring_cap - b), off, p.ring_cap, p.ring_len};
+}
+__device__ __forceinline__ bool ds_key(const DsMask& m, int r) {
+  int u = r + m.off;
+  if (u >= m.cap) u -= m.cap;  // r < cap and off < cap
+  return r < m.rows && u < m.len;
 }
 
-__device__ __forceinline__ int ds_early_count(const AttendParams& p, int ring_start) {
-  const int lenA = min(p.ring_len, p.ring_cap - ring_start);
-  return (p.sink_len > 0 ? 1 : 0) + ((lenA + 63) >> 6) + ((p.ring_len - lenA + 63) >> 6);
+// The G query rows as bf16 pairs in shared memory, row stride DS_QW words
+// (lanes of a row quad and the 4 rows hit 16 distinct banks); read per chunk
+// instead of held in registers.
+constexpr int DS_QW = 68;
+__device__ __forceinline__ uint32_t ds_q(const uint32_t* sq, int g, int word) {
+  return g < 4 ? sq[g * DS_QW + word] : 0u;
 }
 
-// One warp's 16-key chunk at tile rows [r0, r0 + 16): S = Q K^T (Q rows >= 4
-// zero), mask (rows >= valid), online softmax update of (m, l) for query row
-// g = lane / 4 and of the transposed output O^T += V^T P^T, whose B operand is
-// the S accumulator of the lane as it stands (P[g][keys 2t, 2t + 1]).  ofr is
-// O^T in mma layout: ofr[mt] = O[2t | 2t + 1][16 mt + g (+ 8)], t = lane % 4
-// (query rows 2t, 2t + 1 < 4 are real for t < 2).
-__device__ __forceinline__ void ds_rescale(float (&ofr)[8][4], float alpha, int qt) {
-  const float ae = __shfl_sync(FULL, alpha, (2 * qt) * 4), ao = __shfl_sync(FULL, alpha, (2 * qt + 1) * 4);
+// Transpose of an 8 x 8 b16 matrix held in mma fragment layout (lane l: row
+// l / 4, columns 2 (l % 4), + 1).
+__device__ __forceinline__ uint32_t movm_t(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+  return d;
+}
+
+// One warp's 16-key chunk at tile rows [r0, r0 + 16), all in the transposed
+// orientation, whose N = 8 columns are the query rows (4 real, G = 4):
+//   S^T = K Q^T   (A = 16 key rows by ldmatrix, B = Q^T from shared memory;
+//                  8 mma for 16 keys x 128 dims),
+//   O^T += V^T P^T (A = V^T by ldmatrix.trans, B = P^T: the S^T accumulator
+//                  as bf16, transposed in registers by movmatrix).
+// Lane (g, t) = (lane / 4, lane % 4) holds S^T[key g | g + 8][query 2t | 2t + 1]
+// and the online softmax state (m, l) of queries 2t and 2t + 1 (real for
+// t < 2); ofr is O^T in mma layout: ofr[mt] = O[query 2t | 2t + 1][dim 16 mt +
+// g (+ 8)].  P enters P.V split into a bf16 head and a bf16 remainder (two
+// products), so that it carries ~16 significant bits, as an fp32 P.V does.
+__device__ __forceinline__ void ds_chunk(const unsigned char* kt, unsigned char* vt, int r0, const DsMask& mk,
+                                         const uint32_t* sq, float scale, float (&m_run)[2], float (&l_run)[2],
+                                         float (&ofr)[8][4], int lane) {
+  const int mrow = lane & 7, msel = lane >> 3, g = lane >> 2, t = lane & 3;
+  // rows of the chunk that are not keys: their V rows are zeroed, so that
+  // whatever the tile holds there (a slot outside the window, a slot being
+  // rewritten in this call) contributes exactly nothing (p = 0 times a
+  // finite value)
+  const unsigned dead = __ballot_sync(FULL, !ds_key(mk, r0 + (lane & 15))) & 0xffffu;
+  // S^T, k-steps of 16 dims alternating between two accumulators
+  float c[2][4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) c[0][e] = c[1][e] = 0.f;
+  const int krow = r0 + (msel & 1) * 8 + mrow;
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    uint32_t a[4];
+    ldsm_x4(a, kt + swz(64, krow, ks * 16 + (msel >> 1) * 8));
+    mma_bf16(c[ks & 1], a[0], a[1], a[2], a[3], ds_q(sq, g, ks * 8 + t), ds_q(sq, g, ks * 8 + 4 + t));
+  }
+  const bool dlo = (dead >> g) & 1u, dhi = (dead >> (g + 8)) & 1u;
+  float v[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) v[e] = (e < 2 ? dlo : dhi) ? -INFINITY : (c[0][e] + c[1][e]) * scale;
+  // per query: max over the 16 keys (the 8 lanes of a column)
+  float mq[2] = {fmaxf(v[0], v[2]), fmaxf(v[1], v[3])};
+#pragma unroll
+  for (int x = 4; x < 32; x <<= 1) {
+    mq[0] = fmaxf(mq[0], __shfl_xor_sync(FULL, mq[0], x));
+    mq[1] = fmaxf(mq[1], __shfl_xor_sync(FULL, mq[1], x));
+  }
+  const float mn[2] = {fmaxf(m_run[0], mq[0]), fmaxf(m_run[1], mq[1])};
+  // nothing visible yet: the mask does not depend on the query, so this holds
+  // for every lane or none (the mma below are warp-collective)
+  if (__all_sync(FULL, mn[0] == -INFINITY && mn[1] == -INFINITY)) return;
+  float al[2], pe[4], ls[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) al[i] = m_run[i] == -INFINITY ? 0.f : __expf(m_run[i] - mn[i]);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) pe[e] = v[e] == -INFINITY ? 0.f : __expf(v[e] - mn[e & 1]);
+  ls[0] = pe[0] + pe[2];
+  ls[1] = pe[1] + pe[3];
+#pragma unroll
+  for (int x = 4; x < 32; x <<= 1) {
+    ls[0] += __shfl_xor_sync(FULL, ls[0], x);
+    ls[1] += __shfl_xor_sync(FULL, ls[1], x);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    l_run[i] = l_run[i] * al[i] + ls[i];
+    m_run[i] = mn[i];
+  }
 #pragma unroll
   for (int mt = 0; mt < 8; ++mt) {
-    ofr[mt][0] *= ae;
-    ofr[mt][1] *= ao;
-    ofr[mt][2] *= ae;
-    ofr[mt][3] *= ao;
+    ofr[mt][0] *= al[0];
+    ofr[mt][1] *= al[1];
+    ofr[mt][2] *= al[0];
+    ofr[mt][3] *= al[1];
   }
-}
-
-__device__ __forceinline__ void ds_chunk(const unsigned char* kt, const unsigned char* vt, int r0, int valid,
-                                         const uint32_t (&qa)[8][2], float scale, float& m_run, float& l_run,
-                                         float (&ofr)[8][4], int lane) {
-  const int mrow = lane & 7, msel = lane >> 3, qt = lane & 3;
-  float s[2][4], s2[2][4];
+  // P^T fragments: [key g | g + 8][queries 2t, 2t + 1] packed, then transposed
+  // to [query g][keys 2t, 2t + 1 (+ 8)] = the B operand of O^T += V^T P^T
+  const uint32_t h0 = pack_bf16x2(pe[0], pe[1]), h1 = pack_bf16x2(pe[2], pe[3]);
+  const uint32_t l0 = pack_bf16x2(pe[0] - bf_lo(h0), pe[1] - __uint_as_float(h0 & 0xffff0000u));
+  const uint32_t l1 = pack_bf16x2(pe[2] - bf_lo(h1), pe[3] - __uint_as_float(h1 & 0xffff0000u));
+  const uint32_t ph0 = movm_t(h0), ph1 = movm_t(h1), pl0 = movm_t(l0), pl1 = movm_t(l1);
+  if (dead) {  // warp-uniform
 #pragma unroll
-  for (int j = 0; j < 2; ++j)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) s[j][e] = s2[j][e] = 0.f;
-#pragma unroll
-  for (int kk = 0; kk < 8; kk += 2) {
-    uint32_t b[2][4];
-#pragma unroll
-    for (int j = 0; j < 2; ++j) ldsm_x4(b[j], kt + swz(64, r0 + j * 8 + mrow, (kk + (msel >> 1)) * 16 + (msel & 1) * 8));
-#pragma unroll
-    for (int j = 0; j < 2; ++j) mma_bf16(s[j], qa[kk][0], 0u, qa[kk][1], 0u, b[j][0], b[j][1]);
-#pragma unroll
-    for (int j = 0; j < 2; ++j) mma_bf16(s2[j], qa[kk + 1][0], 0u, qa[kk + 1][1], 0u, b[j][2], b[j][3]);
+    for (int rr = lane >> 4; rr < 16; rr += 2)
+      if ((dead >> rr) & 1u) *reinterpret_cast<uint4*>(vt + swz(64, r0 + rr, (lane & 15) * 8)) = make_uint4(0u, 0u, 0u, 0u);
+    __syncwarp();
   }
-  // lane holds row g keys r0 + 8 j + 2 qt + {0, 1} (elements 0, 1)
-  float mloc = -INFINITY;
-#pragma unroll
-  for (int j = 0; j < 2; ++j)
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int key = r0 + j * 8 + 2 * qt + e;
-      const float v = key < valid ? (s[j][e] + s2[j][e]) * scale : -INFINITY;
-      s[j][e] = v;
-      mloc = fmaxf(mloc, v);
-    }
-  mloc = fmaxf(mloc, __shfl_xor_sync(FULL, mloc, 1));
-  mloc = fmaxf(mloc, __shfl_xor_sync(FULL, mloc, 2));
-  const float m_new = fmaxf(m_run, mloc);
-  // nothing visible yet: the mask does not depend on the row, so this holds
-  // for every lane or none (the mma below are warp-collective)
-  if (__all_sync(FULL, m_new == -INFINITY)) return;
-  const float alpha = m_run == -INFINITY ? 0.f : __expf(m_run - m_new);
-  float lsum = 0.f;
-  uint32_t ph[2], pl[2];
-#pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    float pe[2];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      pe[e] = s[j][e] == -INFINITY ? 0.f : __expf(s[j][e] - m_new);
-      lsum += pe[e];
-    }
-    ph[j] = pack_bf16x2(pe[0], pe[1]);
-    pl[j] = pack_bf16x2(pe[0] - bf_lo(ph[j]), pe[1] - __uint_as_float(ph[j] & 0xffff0000u));
-  }
-  lsum += __shfl_xor_sync(FULL, lsum, 1);
-  lsum += __shfl_xor_sync(FULL, lsum, 2);
-  l_run = l_run * alpha + lsum;
-  m_run = m_new;
-  ds_rescale(ofr, alpha, qt);
   // O^T += V^T P^T: A = V^T (16 dims x 16 keys) by ldmatrix.trans of the key
-  // rows (matrix q: keys r0 + (q >> 1) * 8 + row, dims 16 mt + (q & 1) * 8),
-  // B = (P head | P remainder) from the lane's own scores
+  // rows (matrix q: keys r0 + (q >> 1) * 8 + row, dims 16 mt + (q & 1) * 8)
   const int vrow = r0 + (msel >> 1) * 8 + mrow;
 #pragma unroll
   for (int mt = 0; mt < 8; ++mt) {
     uint32_t a[4];
     ldsm_x4_t(a, vt + swz(64, vrow, mt * 16 + (msel & 1) * 8));
-    mma_bf16(ofr[mt], a[0], a[1], a[2], a[3], ph[0], ph[1]);
-    mma_bf16(ofr[mt], a[0], a[1], a[2], a[3], pl[0], pl[1]);
+    mma_bf16(ofr[mt], a[0], a[1], a[2], a[3], ph0, ph1);
+    mma_bf16(ofr[mt], a[0], a[1], a[2], a[3], pl0, pl1);
   }
 }
 
@@ -1971,8 +2012,8 @@ __global__ void __launch_bounds__(DS_WARPS * 32, 2) decode_split_kernel(const At
   __shared__ u64 s_cand[FS_CAND_MAX];
   __shared__ unsigned s_misc[2 * NW];
   __shared__ int s_head;
-  __shared__ int t_y[MT], t_valid[MT], t_src[MT];
   __shared__ __align__(8) uint64_t merge_bar;  // the other CTAs' partials for this CTA's dims have landed
+  __shared__ __align__(16) uint32_t s_q[G * DS_QW];  // this head's G query rows (bf16 pairs)
   __shared__ unsigned s_part[FUSED ? NW : 1][FS_BPC_MAX];  // fused scoring: per-warp block maxima
   __shared__ unsigned char s_pflag[FUSED ? FS_BPC_MAX : 1];   // fused scoring: protected flags of this CTA's blocks
   const int split = blockIdx.x, h = blockIdx.y;
@@ -1998,44 +2039,9 @@ __global__ void __launch_bounds__(DS_WARPS * 32, 2) decode_split_kernel(const At
       prefetch_l2_bulk(p.fs_reps + ((long long)tid * p.fs_reps_blocks + b0) * p.fs_r * NKV_D,
                        (uint32_t)(nb * p.fs_r * NKV_D * 2));
   }
-  pdl_launch_dependents();
-  // With fused scoring the preceding kernel may produce q, the current token,
-  // the representatives or the sink / ring: everything below waits for it.
-  // Otherwise the preceding kernel is the scoring grid, which itself waited
-  // for its predecessor before releasing this grid: only the scores wait.
-  if (FUSED) pdl_wait();
-  // Q as the A operand (rows >= G are zero); the loads are in flight while
-  // the ring head and the protected list are read
-  const int qg = lane >> 2, qt = lane & 3;
-  uint32_t qa[8][2];
-#pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
-    if (qg < G) {
-      const __nv_bfloat16* qrow = p.q + (long long)(h * G + qg) * p.q_head + kk * 16 + 2 * qt;
-      qa[kk][0] = __ldg(reinterpret_cast<const uint32_t*>(qrow));
-      qa[kk][1] = __ldg(reinterpret_cast<const uint32_t*>(qrow + 8));
-    } else {
-      qa[kk][0] = qa[kk][1] = 0u;
-    }
-  }
-  if constexpr (FUSED) {
-    __syncthreads();  // the flags were cleared before the wait
-    const int b0 = (h * CL + split) * p.fs_bpc;
-    for (int i = tid; i < p.fs_nprot; i += NT) {
-      const int b = __ldg(p.fs_prot + i) - b0;
-      if (b >= 0 && b < p.fs_bpc) s_pflag[b] = 1;
-    }
-  }
-  // recent ring: explicit, or the device-resident head (graph replay)
-  int ring_start = p.ring_start, ring_wpos = p.ring_write_pos;
-  if (p.ring_dyn) {
-    if (tid == 0) s_head = ld_relaxed_s32(p.ring_dyn);
-    __syncthreads();
-    ring_wpos = s_head;
-    ring_start = s_head + p.ring_cap - p.ring_len;
-    if (ring_start >= p.ring_cap) ring_start -= p.ring_cap;
-  }
-  const int n_early = ds_early_count(p, ring_start);
+  // barriers, then the early tiles' loads, before anything else: they do
+  // not depend on the scores, on q or on the ring head
+  const int n_early = ds_early_count(p);
   int n_my_early = 0;
   for (int e = split; e < n_early && n_my_early < DS<CL>::MAX_EARLY; e += CL) ++n_my_early;
   int n_my_sel = 0;
@@ -2047,29 +2053,71 @@ __global__ void __launch_bounds__(DS_WARPS * 32, 2) decode_split_kernel(const At
     mbar_expect_tx(&merge_bar, (CL - 1) * DS<CL>::PUSH_BYTES);  // the one arrival; the rest are st.async bytes
   }
   if (tid <= MT) fence_mbar_init();
-  // every CTA's merge barrier is initialised before any CTA of the cluster
-  // stores into it: each CTA arrives here and waits before its pushes
-  cluster_arrive_release();
-  // early tiles: loaded now (thread i issues tile i's four boxes)
-  if (tid < n_my_early) {
-    int src, y, valid;
-    ds_early_tile(p, h, ring_start, split + tid * CL, &src, &y, &valid);
-    t_src[tid] = src;
-    t_y[tid] = y;
-    t_valid[tid] = valid;
-    unsigned char* kd = tiles + (size_t)tid * 2 * DS_TILE_BYTES;
-    mbar_expect_tx(&bar[tid], 2 * DS_TILE_BYTES);
+  // early tile i: thread i (which initialised its barrier) issues its four boxes
+  auto issue_early = [&]() {
+    if (tid < n_my_early) {
+      int src, y;
+      ds_early_tile(p, h, split + tid * CL, &src, &y);
+      unsigned char* kd = tiles + (size_t)tid * 2 * DS_TILE_BYTES;
+      mbar_expect_tx(&bar[tid], 2 * DS_TILE_BYTES);
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      tma_box(kd + half * (64 * 128), &tm.m[src][0][1], half * 64, y, &bar[tid]);
-      tma_box(kd + DS_TILE_BYTES + half * (64 * 128), &tm.m[src][1][1], half * 64, y, &bar[tid]);
+      for (int half = 0; half < 2; ++half) {
+        tma_box(kd + half * (64 * 128), &tm.m[src][0][1], half * 64, y, &bar[tid]);
+        tma_box(kd + DS_TILE_BYTES + half * (64 * 128), &tm.m[src][1][1], half * 64, y, &bar[tid]);
+      }
+    }
+  };
+  // With fused scoring the preceding kernel may produce q, the current token,
+  // the representatives or the sink / ring: everything waits for it.
+  // Otherwise the preceding kernel is the scoring grid, which itself waited
+  // for its predecessor before releasing this grid: only the scores wait.
+  if (!FUSED) issue_early();
+  // every CTA's merge barrier is initialised before any CTA of the cluster
+  // stores into it: each CTA arrives here and waits before its pushes (the
+  // init fence above orders the inits; a relaxed arrival does not wait for
+  // this thread's loads in flight)
+  cluster_arrive_relaxed();
+  // the descriptors of the maps used later, by threads off the early path
+  if (tid >= NT - 6) prefetch_tmap(&tm.m[(tid - (NT - 6)) >> 1][tid & 1][1]);
+  pdl_launch_dependents();
+  if (FUSED) pdl_wait();
+  // device-resident ring head (graph replay)
+  int head_v = 0;
+  if (p.ring_dyn && tid == 0) head_v = ld_relaxed_s32(p.ring_dyn);
+  // Q into shared memory: one 32-bit word (two dims of one row) per thread
+  const int qg = lane >> 2, qt = lane & 3;
+  static_assert(G * (NKV_D / 2) == NT, "one Q word per thread");
+  s_q[(tid >> 6) * DS_QW + (tid & 63)] =
+      __ldg(reinterpret_cast<const uint32_t*>(p.q + (long long)(h * G + (tid >> 6)) * p.q_head) + (tid & 63));
+  if constexpr (FUSED) {
+    issue_early();
+    __syncthreads();  // the flags were cleared before the wait
+    const int b0 = (h * CL + split) * p.fs_bpc;
+    for (int i = tid; i < p.fs_nprot; i += NT) {
+      const int b = __ldg(p.fs_prot + i) - b0;
+      if (b >= 0 && b < p.fs_bpc) s_pflag[b] = 1;
     }
   }
-  float m_run = -INFINITY, l_run = 0.f;
+  if (p.ring_dyn && tid == 0) s_head = head_v;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};  // queries 2t, 2t + 1
   float ofr[8][4];
 #pragma unroll
   for (int mt = 0; mt < 8; ++mt) ofr[mt][0] = ofr[mt][1] = ofr[mt][2] = ofr[mt][3] = 0.f;
-  __syncthreads();  // barrier init and early-tile table visible
+  __syncthreads();  // barrier init and the ring head visible
+  // The recent window: explicit, or from the device-resident head.  With a
+  // device head every CTA arrives once it has read it; the last to arrive
+  // advances it at its end.  The arrival is issued here and its result used
+  // only at the end, so its round trip overlaps the CTA's work.  (An arrival
+  // comes after the CTA's read of the head has returned its value, so the
+  // advance cannot reach a read.)
+  int ring_start = p.ring_start, ring_wpos = p.ring_write_pos;
+  unsigned ring_ticket = 0u;
+  if (p.ring_dyn) {
+    ring_wpos = s_head;
+    ring_start = s_head + p.ring_cap - p.ring_len;
+    if (ring_start >= p.ring_cap) ring_start -= p.ring_cap;
+    if (tid == 0) ring_ticket = atomicAdd(reinterpret_cast<unsigned*>(p.ring_dyn) + 1, 1u);
+  }
   // fused scoring: this CTA's blocks are scored and published first, so that
   // the other CTAs' keys arrive while the early tiles are attended
   if constexpr (FUSED) fs_score_publish<G, NW>(p, h * CL + split, fs_tg, s_part, nullptr, s_pflag);
@@ -2077,8 +2125,9 @@ __global__ void __launch_bounds__(DS_WARPS * 32, 2) decode_split_kernel(const At
   for (int t = 0; t < n_my_early; ++t) {
     if ((warp >> 2) != (t & 1)) continue;
     mbar_wait_poll(&bar[t], 0, p.err);
-    const unsigned char* kt = tiles + (size_t)t * 2 * DS_TILE_BYTES;
-    ds_chunk(kt, kt + DS_TILE_BYTES, (warp & 3) * 16, t_valid[t], qa, p.scale, m_run, l_run, ofr, lane);
+    unsigned char* kt = tiles + (size_t)t * 2 * DS_TILE_BYTES;
+    ds_chunk(kt, kt + DS_TILE_BYTES, (warp & 3) * 16, ds_early_mask(p, split + t * CL, ring_start), s_q, p.scale,
+             m_run, l_run, ofr, lane);
   }
 
   // ---- selection: every CTA ranks the block scores itself -----------------------------
@@ -2102,9 +2151,6 @@ __global__ void __launch_bounds__(DS_WARPS * 32, 2) decode_split_kernel(const At
       id = 0;
     }
     const int y = (int)((id * p.hkv + h) * 64);
-    t_src[slot] = 0;
-    t_y[slot] = y;
-    t_valid[slot] = 64;
     unsigned char* kd = tiles + (size_t)slot * 2 * DS_TILE_BYTES;
     mbar_expect_tx(&bar[slot], 2 * DS_TILE_BYTES);
 #pragma unroll
@@ -2117,44 +2163,49 @@ __global__ void __launch_bounds__(DS_WARPS * 32, 2) decode_split_kernel(const At
   for (int t = n_my_early; t < ntiles; ++t) {
     if ((warp >> 2) != (t & 1)) continue;
     mbar_wait_poll(&bar[t], 0, p.err);
-    const unsigned char* kt = tiles + (size_t)t * 2 * DS_TILE_BYTES;
-    ds_chunk(kt, kt + DS_TILE_BYTES, (warp & 3) * 16, 64, qa, p.scale, m_run, l_run, ofr, lane);
+    unsigned char* kt = tiles + (size_t)t * 2 * DS_TILE_BYTES;
+    ds_chunk(kt, kt + DS_TILE_BYTES, (warp & 3) * 16, ds_mask_rows(64), s_q, p.scale, m_run, l_run, ofr, lane);
   }
   // the current token: one key, attended by warp NW - 1 of the head's last CTA
   const bool cur_owner = split == CL - 1 && p.n_cur > 0;
   if (cur_owner && warp == NW - 1) {
     const __nv_bfloat16* kc = p.cur_k + (long long)h * p.cur_head;
     const __nv_bfloat16* vc = p.cur_v + (long long)h * p.cur_head;
-    // s = q_g . k (lanes of a row quad hold dims 2 qt + 8 i + {0, 1}, i.e.
-    // the qa layout: k-step kk covers dims 16 kk .. 16 kk + 15)
+    // s = q_g . k (lane qt of row quad g takes dims 16 kk + 2 qt + {0, 1}
+    // and 16 kk + 8 + 2 qt + {0, 1} for every k-step kk)
     float part = 0.f;
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) {
       const uint32_t k0 = __ldg(reinterpret_cast<const uint32_t*>(kc + kk * 16 + 2 * qt));
       const uint32_t k1 = __ldg(reinterpret_cast<const uint32_t*>(kc + kk * 16 + 8 + 2 * qt));
-      part = fmaf(bf_lo(qa[kk][0]), bf_lo(k0), part);
-      part = fmaf(__uint_as_float(qa[kk][0] & 0xffff0000u), __uint_as_float(k0 & 0xffff0000u), part);
-      part = fmaf(bf_lo(qa[kk][1]), bf_lo(k1), part);
-      part = fmaf(__uint_as_float(qa[kk][1] & 0xffff0000u), __uint_as_float(k1 & 0xffff0000u), part);
+      const uint32_t q0 = ds_q(s_q, qg, kk * 8 + qt), q1 = ds_q(s_q, qg, kk * 8 + 4 + qt);
+      part = fmaf(bf_lo(q0), bf_lo(k0), part);
+      part = fmaf(__uint_as_float(q0 & 0xffff0000u), __uint_as_float(k0 & 0xffff0000u), part);
+      part = fmaf(bf_lo(q1), bf_lo(k1), part);
+      part = fmaf(__uint_as_float(q1 & 0xffff0000u), __uint_as_float(k1 & 0xffff0000u), part);
     }
     part += __shfl_xor_sync(FULL, part, 1);
     part += __shfl_xor_sync(FULL, part, 2);
-    const float sc = part * p.scale;
-    const float m_new = fmaxf(m_run, sc);
-    const float alpha = m_run == -INFINITY ? 0.f : __expf(m_run - m_new);
-    const float pe = __expf(sc - m_new);
-    l_run = l_run * alpha + pe;
-    m_run = m_new;
-    ds_rescale(ofr, alpha, qt);
+    // this lane's queries 2 qt, 2 qt + 1 (their sums sit in row quads 2 qt, 2 qt + 1)
+    const float sc[2] = {__shfl_sync(FULL, part, (2 * qt) * 4) * p.scale,
+                         __shfl_sync(FULL, part, (2 * qt + 1) * 4) * p.scale};
+    float al[2], pe[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float m_new = fmaxf(m_run[i], sc[i]);
+      al[i] = m_run[i] == -INFINITY ? 0.f : __expf(m_run[i] - m_new);
+      pe[i] = __expf(sc[i] - m_new);
+      l_run[i] = l_run[i] * al[i] + pe[i];
+      m_run[i] = m_new;
+    }
     // lane (g, qt) holds O[2 qt | 2 qt + 1][16 mt + g (+ 8)]
-    const float pe_e = __shfl_sync(FULL, pe, (2 * qt) * 4), pe_o = __shfl_sync(FULL, pe, (2 * qt + 1) * 4);
 #pragma unroll
     for (int mt = 0; mt < 8; ++mt) {
       const float v0 = __bfloat162float(vc[mt * 16 + qg]), v1 = __bfloat162float(vc[mt * 16 + qg + 8]);
-      ofr[mt][0] = fmaf(pe_e, v0, ofr[mt][0]);
-      ofr[mt][1] = fmaf(pe_o, v0, ofr[mt][1]);
-      ofr[mt][2] = fmaf(pe_e, v1, ofr[mt][2]);
-      ofr[mt][3] = fmaf(pe_o, v1, ofr[mt][3]);
+      ofr[mt][0] = fmaf(pe[0], v0, ofr[mt][0] * al[0]);
+      ofr[mt][1] = fmaf(pe[1], v0, ofr[mt][1] * al[1]);
+      ofr[mt][2] = fmaf(pe[0], v1, ofr[mt][2] * al[0]);
+      ofr[mt][3] = fmaf(pe[1], v1, ofr[mt][3] * al[1]);
     }
   }
 
@@ -2173,13 +2224,20 @@ __global__ void __launch_bounds__(DS_WARPS * 32, 2) decode_split_kernel(const At
       o1[mt * 16 + qg + 8] = ofr[mt][3];
     }
   }
-  if (qg < G && qt == 0) {
-    wml[(warp * G + qg) * 2] = m_run;
-    wml[(warp * G + qg) * 2 + 1] = l_run;
+  if (qg == 0 && qt < 2) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      wml[(warp * G + 2 * qt + i) * 2] = m_run[i];
+      wml[(warp * G + 2 * qt + i) * 2 + 1] = l_run[i];
+    }
   }
   __syncthreads();
   cluster_wait_acquire();
-  for (int it = tid; it < G * (NKV_D / 4); it += NT) {
+  {
+    // (row g, 4 dims d4) per lane pair: lane hs of the pair sums warps
+    // 4 hs .. 4 hs + 3, one shuffle adds the halves
+    static_assert(G * (NKV_D / 4) * 2 == NT, "one lane pair per 4 output dims");
+    const int it = tid >> 1, hs = tid & 1;
     const int g = it / (NKV_D / 4), d4 = it % (NKV_D / 4);
     float M = -INFINITY;
 #pragma unroll
@@ -2187,25 +2245,32 @@ __global__ void __launch_bounds__(DS_WARPS * 32, 2) decode_split_kernel(const At
     float L = 0.f;
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int w = 0; w < NW; ++w) {
+    for (int w4 = 0; w4 < NW / 2; ++w4) {
+      const int w = hs * (NW / 2) + w4;
       const float m = wml[(w * G + g) * 2];
       if (m == -INFINITY) continue;
       const float sw = __expf(m - M);
-      L += sw * wml[(w * G + g) * 2 + 1];
+      L = fmaf(sw, wml[(w * G + g) * 2 + 1], L);
       const float4 v = *reinterpret_cast<const float4*>(wpo + (w * G + g) * NKV_D + d4 * 4);
       o.x = fmaf(sw, v.x, o.x);
       o.y = fmaf(sw, v.y, o.y);
       o.z = fmaf(sw, v.z, o.z);
       o.w = fmaf(sw, v.w, o.w);
     }
+    L += __shfl_xor_sync(FULL, L, 1);
+    o.x += __shfl_xor_sync(FULL, o.x, 1);
+    o.y += __shfl_xor_sync(FULL, o.y, 1);
+    o.z += __shfl_xor_sync(FULL, o.z, 1);
+    o.w += __shfl_xor_sync(FULL, o.w, 1);
     // the CTA partial goes to the CTAs that merge its dims: to this CTA by a
     // plain store, to the others by asynchronous remote stores that complete
     // their merge barriers; (m, l) goes to every CTA of the cluster
-    const int r = (d4 * 4) / SW;
-    float* dst_o = recv + ((size_t)split * G + g) * SW + (d4 * 4) % SW;
-    if (r == split) *reinterpret_cast<float4*>(dst_o) = o;
-    else st_async_v4(cluster_addr(dst_o, r), o, cluster_addr(&merge_bar, r));
-    if (d4 < CL) {  // (m, l) of row g to CTA d4 (one remote store per thread)
+    if (hs == 0) {
+      const int r = (d4 * 4) / SW;
+      float* dst_o = recv + ((size_t)split * G + g) * SW + (d4 * 4) % SW;
+      if (r == split) *reinterpret_cast<float4*>(dst_o) = o;
+      else st_async_v4(cluster_addr(dst_o, r), o, cluster_addr(&merge_bar, r));
+    } else if (d4 < CL) {  // (m, l) of row g to CTA d4 (one remote store per lane)
       float* dst_ml = recv_ml + ((size_t)split * G + g) * 2;
       if (d4 == split) {
         dst_ml[0] = M;
@@ -2225,32 +2290,45 @@ __global__ void __launch_bounds__(DS_WARPS * 32, 2) decode_split_kernel(const At
   // this CTA's dims: wait for every CTA's partial, merge, write the output
   __syncthreads();  // this CTA's own stores into the receive area
   mbar_wait_poll(&merge_bar, 0, p.err);
-  if (tid < G * SW) {
-    const int g = tid / SW, d = tid % SW;
+  {
+    // LPO adjacent lanes per output, each taking SPL of the CL partials, then
+    // a shuffle tree (short dependency chains instead of CL serial steps)
+    constexpr int NOUT = G * SW, LPO = NT / NOUT, SPL = CL / LPO;
+    static_assert(NOUT * LPO == NT && SPL * LPO == CL && 32 % LPO == 0, "merge lanes");
+    const int oi = tid / LPO, j = tid % LPO;
+    const int g = oi / SW, d = oi % SW;
+    float mv[SPL];
     float M = -INFINITY;
 #pragma unroll
-    for (int c = 0; c < CL; ++c) M = fmaxf(M, recv_ml[(c * G + g) * 2]);
+    for (int c = 0; c < SPL; ++c) {
+      mv[c] = recv_ml[((j * SPL + c) * G + g) * 2];
+      M = fmaxf(M, mv[c]);
+    }
+#pragma unroll
+    for (int x = 1; x < LPO; x <<= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, x));
     float L = 0.f, o = 0.f;
 #pragma unroll
-    for (int c = 0; c < CL; ++c) {
-      const float m = recv_ml[(c * G + g) * 2];
-      if (m == -INFINITY) continue;
-      const float sw = __expf(m - M);
-      L = fmaf(sw, recv_ml[(c * G + g) * 2 + 1], L);
-      o = fmaf(sw, recv[(c * G + g) * SW + d], o);
+    for (int c = 0; c < SPL; ++c) {
+      if (mv[c] == -INFINITY) continue;
+      const int sc = j * SPL + c;
+      const float sw = __expf(mv[c] - M);
+      L = fmaf(sw, recv_ml[(sc * G + g) * 2 + 1], L);
+      o = fmaf(sw, recv[(sc * G + g) * SW + d], o);
     }
-    p.out[(long long)(h * G + g) * p.out_head + split * SW + d] = __float2bfloat16(o / L);
+#pragma unroll
+    for (int x = 1; x < LPO; x <<= 1) {
+      L += __shfl_xor_sync(FULL, L, x);
+      o += __shfl_xor_sync(FULL, o, x);
+    }
+    if (j == 0) p.out[(long long)(h * G + g) * p.out_head + split * SW + d] = __float2bfloat16(o / L);
   }
-  // device-resident ring head: the last CTA of the grid to get here (every CTA
-  // has read the head by now) advances it past the slot written above
-  if (p.ring_dyn && tid == 0) {
-    const unsigned total = gridDim.x * gridDim.y;
-    if (atomicAdd(reinterpret_cast<unsigned*>(p.ring_dyn) + 1, 1u) == total - 1u) {
-      p.ring_dyn[1] = 0;
-      int nh = s_head + 1;
-      if (nh >= p.ring_cap) nh = 0;
-      p.ring_dyn[0] = nh;
-    }
+  // device-resident ring head: the last CTA of the grid to arrive (every CTA
+  // had read the head before its arrival) advances it past the slot written above
+  if (p.ring_dyn && tid == 0 && ring_ticket == gridDim.x * gridDim.y - 1u) {
+    p.ring_dyn[1] = 0;
+    int nh = s_head + 1;
+    if (nh >= p.ring_cap) nh = 0;
+    p.ring_dyn[0] = nh;
   }
 }
 
@@ -2601,7 +2679,7 @@ int attend_step(nkv_stream_t stream, const nkv_attend_args* a, const void* reps,
 // device, so that the caller takes the general decode kernel.
 template <bool FUSED>
 static int launch_split(AttendParams p, const DecodeMaps& maps, const nkv_attend_args* a, cudaStream_t st) {
-  const int early_max = (a->sink_len > 0 ? 1 : 0) + (a->ring_len + 63) / 64 + 1;
+  const int early_max = (a->sink_len > 0 ? 1 : 0) + (a->ring_len > 0 ? (a->ring_cap + 63) / 64 : 0);
   for (int CL : {16, 8}) {
     const int max_early = CL >= 16 ? DS<16>::MAX_EARLY : DS<8>::MAX_EARLY;
     if (early_max > CL * max_early || a->n_sel > 32) continue;
@@ -2636,7 +2714,7 @@ static int launch_split(AttendParams p, const DecodeMaps& maps, const nkv_attend
     p.cluster = 1;
     p.splits = CL;
     p.tps = (int)((p.ntok + CL - 1) / CL);
-    g_last_cluster = 1;
+    g_last_cluster = 2;
     g_last_splits = CL;
     g_last_tps = p.tps;
     const cudaError_t le = CL == 16 ? cudaLaunchKernelEx(&lc, decode_split_kernel<16, FUSED>, p, maps)
