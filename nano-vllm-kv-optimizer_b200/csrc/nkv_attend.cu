@@ -135,6 +135,9 @@ struct AttendParams {
 // store, 1 = sink, 2 = recent ring; box 0 = 8 rows, 1 = 64 rows.
 struct DecodeMaps {
   CUtensorMap m[3][2][2];
+  // whole 64-row tiles in one box: dims (64 columns, rows, 2 halves), the
+  // halves 128 bytes apart, so one box lands as the [2][64][128 B] tile
+  CUtensorMap t3[3][2];
 };
 
 __device__ __forceinline__ long long clamp_id(const AttendParams& p, int slot, bool* bad) {
@@ -775,6 +778,15 @@ enum : int { PT_SEL = 0, PT_SINK = 1, PT_RING = 2, PT_THREADS = 3, PT_SKIP = 4, 
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+// One 64-row tile (both 64-column halves) of a [rows][128] bf16 tensor in one
+// box of a DecodeMaps::t3 map.
+__device__ __forceinline__ void tma_tile3(void* dst, const CUtensorMap* map, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(y), "r"(0), "r"(smem_u32(bar))
+      : "memory");
 }
 // One box (8 or 64 rows x 64 columns) of a [rows][128] bf16 tensor into swizzled shared memory.
 __device__ __forceinline__ void tma_box(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -1867,6 +1879,24 @@ __device__ __forceinline__ int ds_early_count(const AttendParams& p) {
   return (p.sink_len > 0 ? 1 : 0) + (p.ring_len > 0 ? (p.ring_cap + 63) >> 6 : 0);
 }
 
+// The K and V tiles of 64 rows of source src from row y: one whole-tile box
+// each where the source has the 3D maps (tma_mask bit 3 + src), else two
+// 64-column boxes each.
+__device__ __forceinline__ void ds_issue_tile(const DecodeMaps& tm, int tma_mask, int src, int y, unsigned char* kd,
+                                              uint64_t* bar) {
+  mbar_expect_tx(bar, 2 * DS_TILE_BYTES);
+  if ((tma_mask >> (3 + src)) & 1) {
+    tma_tile3(kd, &tm.t3[src][0], y, bar);
+    tma_tile3(kd + DS_TILE_BYTES, &tm.t3[src][1], y, bar);
+  } else {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      tma_box(kd + half * (64 * 128), &tm.m[src][0][1], half * 64, y, bar);
+      tma_box(kd + DS_TILE_BYTES + half * (64 * 128), &tm.m[src][1][1], half * 64, y, bar);
+    }
+  }
+}
+
 // Rows of a tile that are attended: row r is a key iff r < rows and
 // (r + off) mod cap < len.  Selected and sink tiles use the first rows; a
 // ring tile starting at slot b attends the slots of the window
@@ -2058,13 +2088,7 @@ __global__ void __launch_bounds__(DS_WARPS * 32, 2) decode_split_kernel(const At
     if (tid < n_my_early) {
       int src, y;
       ds_early_tile(p, h, split + tid * CL, &src, &y);
-      unsigned char* kd = tiles + (size_t)tid * 2 * DS_TILE_BYTES;
-      mbar_expect_tx(&bar[tid], 2 * DS_TILE_BYTES);
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        tma_box(kd + half * (64 * 128), &tm.m[src][0][1], half * 64, y, &bar[tid]);
-        tma_box(kd + DS_TILE_BYTES + half * (64 * 128), &tm.m[src][1][1], half * 64, y, &bar[tid]);
-      }
+      ds_issue_tile(tm, p.tma_mask, src, y, tiles + (size_t)tid * 2 * DS_TILE_BYTES, &bar[tid]);
     }
   };
   // With fused scoring the preceding kernel may produce q, the current token,
@@ -2078,7 +2102,10 @@ __global__ void __launch_bounds__(DS_WARPS * 32, 2) decode_split_kernel(const At
   // this thread's loads in flight)
   cluster_arrive_relaxed();
   // the descriptors of the maps used later, by threads off the early path
-  if (tid >= NT - 6) prefetch_tmap(&tm.m[(tid - (NT - 6)) >> 1][tid & 1][1]);
+  if (tid >= NT - 6) {
+    const int src = (tid - (NT - 6)) >> 1;
+    prefetch_tmap((p.tma_mask >> (3 + src)) & 1 ? &tm.t3[src][tid & 1] : &tm.m[src][tid & 1][1]);
+  }
   pdl_launch_dependents();
   if (FUSED) pdl_wait();
   // device-resident ring head (graph replay)
@@ -2150,14 +2177,8 @@ __global__ void __launch_bounds__(DS_WARPS * 32, 2) decode_split_kernel(const At
       if (p.err) atomicExch(p.err, ERR_BAD_INDEX);
       id = 0;
     }
-    const int y = (int)((id * p.hkv + h) * 64);
-    unsigned char* kd = tiles + (size_t)slot * 2 * DS_TILE_BYTES;
-    mbar_expect_tx(&bar[slot], 2 * DS_TILE_BYTES);
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      tma_box(kd + half * (64 * 128), &tm.m[0][0][1], half * 64, y, &bar[slot]);
-      tma_box(kd + DS_TILE_BYTES + half * (64 * 128), &tm.m[0][1][1], half * 64, y, &bar[slot]);
-    }
+    ds_issue_tile(tm, p.tma_mask, 0, (int)((id * p.hkv + h) * 64), tiles + (size_t)slot * 2 * DS_TILE_BYTES,
+                  &bar[slot]);
   }
   // selected tiles: tile n_my_early + j goes to warps 4 * ((n_my_early + j) & 1) ...
   for (int t = n_my_early; t < ntiles; ++t) {
@@ -2454,6 +2475,7 @@ static EncodeTiledFn encode_tiled() {
 // memory), a base that is not 16-byte aligned, or more rows than a coordinate
 // holds.  Maps are cached per thread in a small hash table keyed by
 // (base, rows, box_rows); encoding touches no device state.
+// box_rows = -64: the whole-tile 3D form of DecodeMaps::t3.
 static bool tma_rows_map(CUtensorMap* out, const void* base, long long rows, int box_rows) {
   struct Entry { const void* base; long long rows; int box; bool ok; CUtensorMap map; };
   constexpr int N = 512;
@@ -2476,7 +2498,15 @@ static bool tma_rows_map(CUtensorMap* out, const void* base, long long rows, int
   const bool dev = cudaPointerGetAttributes(&pa, base) == cudaSuccess && pa.type == cudaMemoryTypeDevice;
   cudaGetLastError();
   EncodeTiledFn fn = encode_tiled();
-  if (dev && fn && box_rows <= rows) {
+  if (dev && fn && box_rows < 0 && -box_rows <= rows) {
+    const cuuint64_t dims[3] = {64, (cuuint64_t)rows, 2};
+    const cuuint64_t strides[2] = {(cuuint64_t)NKV_D * 2, 128};
+    const cuuint32_t box[3] = {64, (cuuint32_t)(-box_rows), 2};
+    const cuuint32_t es[3] = {1, 1, 1};
+    e.ok = fn(&e.map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  } else if (dev && fn && box_rows > 0 && box_rows <= rows) {
     const cuuint64_t dims[2] = {(cuuint64_t)NKV_D, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)NKV_D * 2};
     const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
@@ -2491,10 +2521,15 @@ static bool tma_rows_map(CUtensorMap* out, const void* base, long long rows, int
 
 // The four maps of one source (K and V, 8- and 64-row boxes); a source of
 // fewer than 64 rows never has a piece of 64 rows and gets no 64-row maps.
-static bool source_maps(DecodeMaps* m, int src, const void* k, const void* v, long long rows) {
+// *tile3: the source also has whole-tile maps (t3).
+static bool source_maps(DecodeMaps* m, int src, const void* k, const void* v, long long rows, bool* tile3) {
+  *tile3 = false;
   if (!tma_rows_map(&m->m[src][0][0], k, rows, 8) || !tma_rows_map(&m->m[src][1][0], v, rows, 8)) return false;
   if (rows < 64) return true;
-  return tma_rows_map(&m->m[src][0][1], k, rows, 64) && tma_rows_map(&m->m[src][1][1], v, rows, 64);
+  if (!tma_rows_map(&m->m[src][0][1], k, rows, 64) || !tma_rows_map(&m->m[src][1][1], v, rows, 64)) return false;
+  *tile3 = env_int("NKV_TMA_TILE3", 1) && tma_rows_map(&m->t3[src][0], k, rows, -64) &&
+           tma_rows_map(&m->t3[src][1], v, rows, -64);
+  return true;
 }
 
 // The decode kernel's tensor maps for one combination of sources (block
@@ -2528,10 +2563,12 @@ static const DecodeMaps& decode_maps(const void* ks, const void* vs, long long k
   }
   DecodeMaps& m = victim ? victim->maps : scratch;
   memset(&m, 0, sizeof(m));
+  // bit s: source s is TMA-readable; bit 3 + s: it also has whole-tile maps
   int mk = 0;
-  if (ks && source_maps(&m, 0, ks, vs, krows)) mk |= 1;
-  if (sk && source_maps(&m, 1, sk, sv, srows)) mk |= 2;
-  if (rk && source_maps(&m, 2, rk, rv, rrows)) mk |= 4;
+  bool t3 = false;
+  if (ks && source_maps(&m, 0, ks, vs, krows, &t3)) mk |= 1 | (t3 ? 8 : 0);
+  if (sk && source_maps(&m, 1, sk, sv, srows, &t3)) mk |= 2 | (t3 ? 16 : 0);
+  if (rk && source_maps(&m, 2, rk, rv, rrows, &t3)) mk |= 4 | (t3 ? 32 : 0);
   if (victim) {
     for (int i = 0; i < 6; ++i) victim->ptr[i] = ptr[i];
     for (int i = 0; i < 3; ++i) victim->rows[i] = rows[i];
