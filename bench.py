@@ -153,124 +153,167 @@ def offload_measure(nkv, dev, steps=20):
                          "peak_kind": "measured pinned H2D copy (256 MiB) on this box"}}
 
 
-# BASELINE config 5 (operator part): KV heads sharded over the N ranks, 128K history
-SH_CTX, SH_LAYERS = 131072, 4
+# BASELINE config 5 (operator part): KV heads sharded over the N ranks, 128K
+# history; 8 layer states (27.5 MB of representatives and selected KV per
+# layer: 220 MB per step, above the 126 MB L2), inputs rotating over NSETS sets
+SH_CTX, SH_LAYERS = 131072, 8
 
 
-def sharded_measure(nkv, dev, world, steps=20):
-    """Decode step with the KV heads split over the ranks (KVHeadShardedLayer)
-    at 128K, per layer: scoring of the rank's heads, the maximum over ranks of
-    the block scores, attention of the rank's heads, the gather of the outputs.
-    Measured for both exchange forms -- "peer" (inside the kernels, through
-    peer memory) and "nccl" (MAX all-reduce + all-gather) -- each replayed from
-    a CUDA graph (eager if capture is refused); device time between events,
-    max over ranks.  Rank 0 also times the same layers unsharded on its GPU."""
+def _sharded_build(nkv, dev, make):
+    """SH_LAYERS layers of 128K history (the same seeded K/V on every rank)."""
+    g = torch.Generator(device=dev).manual_seed(5150)
+    layers = []
+    for li in range(SH_LAYERS):
+        lay = make(li)
+        rt = getattr(lay, "rt", lay)
+        rt.reserve_blocks(SH_CTX // B)
+        for c in range(SH_CTX // 4096):
+            k = torch.randn(4096, HKV, D, generator=g, device=dev).bfloat16()
+            v = torch.randn(4096, HKV, D, generator=g, device=dev).bfloat16()
+            if c == 0:
+                lay.prefill_first(None, k, v)
+            elif lay is rt:
+                rt._store_kv(k, v)
+            else:
+                lay.store(k, v)
+        layers.append(lay)
+    return layers
+
+
+def _sharded_inputs(dev):
+    """NSETS input sets of every layer's q/k/v and the staging buffer the step reads."""
+    QKV = (HQ + 2 * HKV) * D
+    xs = torch.randn(NSETS, SH_LAYERS, QKV, generator=torch.Generator(device=dev).manual_seed(77),
+                     device=dev).bfloat16()
+    x = xs[0].clone()
+    views = [(x[li, :HQ * D].view(1, HQ, D), x[li, HQ * D:(HQ + HKV) * D].view(1, HKV, D),
+              x[li, (HQ + HKV) * D:].view(1, HKV, D)) for li in range(SH_LAYERS)]
+    return xs, x, views
+
+
+def _graph_time(fn, xs, x, stream, steps, collective):
+    """us per layer of fn() replayed from a CUDA graph (eager when every rank
+    cannot capture), the staging buffer refilled from the next input set
+    before each replay; max over ranks when collective."""
     import torch.distributed as dist
-    res = {"workload": f"decode step @128K (Top-32 of 2048 blocks), KV heads sharded {world} ways, "
-                       f"{SH_LAYERS} layer states", "kv_heads_per_gpu": HKV // world}
-    for exchange in ("peer", "nccl"):
-        g = torch.Generator(device=dev).manual_seed(5150)
-        layers = []
-        for li in range(SH_LAYERS):
-            lay = nkv.KVHeadShardedLayer(li, nkv.M12Config(max_model_len=SH_CTX + 4096, device=dev),
-                                         exchange=exchange)
-            lay.rt.reserve_blocks(SH_CTX // B)
-            for c in range(SH_CTX // 4096):
-                k = torch.randn(4096, HKV, D, generator=g, device=dev).bfloat16()
-                v = torch.randn(4096, HKV, D, generator=g, device=dev).bfloat16()
-                if c == 0:
-                    lay.prefill_first(None, k, v)
-                else:
-                    lay.store(k, v)
-            layers.append(lay)
-        q = torch.randn(SH_LAYERS, 1, HQ, D, generator=g, device=dev).bfloat16()
-        k = torch.randn(SH_LAYERS, 1, HKV, D, generator=g, device=dev).bfloat16()
-        v = torch.randn(SH_LAYERS, 1, HKV, D, generator=g, device=dev).bfloat16()
-
-        def step():
-            for li, lay in enumerate(layers):
-                lay.decode(q[li], k[li], v[li])
-        stream = torch.cuda.Stream(dev)
-        with torch.cuda.stream(stream):
-            for _ in range(3):
-                step()
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            x.copy_(xs[i % NSETS])
+            fn()
+    torch.cuda.synchronize()
+    graph, mode = None, "eager"
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            fn()
+        mode = "cuda graph"
+    except Exception:  # noqa: BLE001 - measured eagerly instead
+        graph = None
         torch.cuda.synchronize()
-        dist.barrier()
-        # the whole sharded step captured in one CUDA graph; eager replay is the
-        # fallback when capture is refused
-        graph, mode = None, "eager"
-        try:
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=stream):
-                step()
-            mode = "cuda graph"
-        except Exception:  # noqa: BLE001 - measured eagerly instead
-            graph = None
-            torch.cuda.synchronize()
-        # every rank replays the same way (the exchanges must match)
-        ok = torch.tensor([0 if graph is None else 1], device=dev)
+    if collective:
+        ok = torch.tensor([0 if graph is None else 1], device=x.device)
         dist.all_reduce(ok, op=dist.ReduceOp.MIN)
         if int(ok.item()) == 0:
             graph, mode = None, "eager"
         dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            for _ in range(3):
-                graph.replay() if graph is not None else step()
-            e0.record(stream)
-            for _ in range(steps):
-                graph.replay() if graph is not None else step()
-            e1.record(stream)
-        e1.synchronize()
-        errs = sum(int(lay.rt._att_ws[:4].view(torch.int32).item()) != 0 for lay in layers)
-        t = torch.tensor([e0.elapsed_time(e1) * 1000.0 / (steps * SH_LAYERS), float(errs)], device=dev)
+    run = graph.replay if graph is not None else fn
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            x.copy_(xs[i % NSETS])
+            run()
+        e0.record(stream)
+        for i in range(steps):
+            x.copy_(xs[i % NSETS])
+            run()
+        e1.record(stream)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / (steps * SH_LAYERS)
+    if collective:
+        t = torch.tensor([us], device=x.device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        del graph
-        torch.cuda.synchronize()
+        us = float(t.item())
+    del graph
+    torch.cuda.synchronize()
+    return us, mode
+
+
+def sharded_measure(nkv, dev, world, steps=20):
+    """Decode step with the KV heads split over the ranks (KVHeadShardedLayer)
+    at 128K, per layer, three forms: sharded scoring with the exchange inside
+    the kernels ("peer") or as NCCL collectives ("nccl": MAX all-reduce of the
+    scores, all-gather of the outputs), and replicated scoring ("replicated":
+    every rank scores all heads, the output all-gather is the only collective).
+    Each is replayed from a CUDA graph with the inputs changing every step
+    (device time between events, max over ranks); the input copies (the same
+    in every form) are inside the timed region.  For the NCCL forms the step
+    is also timed cut after the scoring (with its exchange) and after the
+    attention, which gives the marginal cost of each phase.  Rank 0 also times
+    the same layers unsharded on its GPU."""
+    import torch.distributed as dist
+    res = {"workload": f"decode step @128K (Top-32 of 2048 blocks), KV heads sharded {world} ways, "
+                       f"{SH_LAYERS} layer states, inputs rotating over {NSETS} sets",
+           "kv_heads_per_gpu": HKV // world}
+    stream = torch.cuda.Stream(dev)
+    for name, exchange, scoring in (("peer", "peer", "sharded"), ("nccl", "nccl", "sharded"),
+                                    ("replicated", "nccl", "replicated")):
+        cfg = nkv.M12Config(max_model_len=SH_CTX + 4096, device=dev)
+        layers = _sharded_build(nkv, dev, lambda li: nkv.KVHeadShardedLayer(li, cfg, exchange=exchange,
+                                                                             scoring=scoring))
+        xs, x, views = _sharded_inputs(dev)
+
+        def step():
+            for lay, (q, k, v) in zip(layers, views):
+                lay.decode(q, k, v)
+        us, mode = _graph_time(step, xs, x, stream, steps, True)
+        entry = {"us_per_layer": round(us, 2), "mode": mode, "exchange": layers[0].exchange,
+                 "scoring": scoring}
+        if exchange == "nccl":
+            def scores_only():
+                for lay, (q, k, v) in zip(layers, views):
+                    if scoring == "replicated":
+                        lay.scores_all(q)
+                    else:
+                        sc = lay.rt.block_scores_dev(lay._q(q))
+                        dist.all_reduce(sc, op=dist.ReduceOp.MAX, group=lay.group)
+
+            def no_gather():
+                for lay, (q, k, v) in zip(layers, views):
+                    if scoring == "replicated":
+                        sc = lay.scores_all(q)
+                    else:
+                        sc = lay.rt.block_scores_dev(lay._q(q))
+                        dist.all_reduce(sc, op=dist.ReduceOp.MAX, group=lay.group)
+                    lay.rt.decode_ranked(lay._q(q), lay._kv(k), lay._kv(v), sc)
+            t_sc, _ = _graph_time(scores_only, xs, x, stream, steps, True)
+            t_at, _ = _graph_time(no_gather, xs, x, stream, steps, True)
+            entry["marginal_us_per_layer"] = {
+                "scoring" + ("" if scoring == "replicated" else " + MAX all-reduce"): round(t_sc, 2),
+                "attention": round(t_at - t_sc, 2), "output all-gather": round(us - t_at, 2)}
+        errs = sum(int(lay.rt._att_ws[:4].view(torch.int32).item()) != 0 for lay in layers)
+        t = torch.tensor([float(errs)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        entry["kernel_errors"] = int(t.item())
         for lay in layers:
             lay.close()
-        res[exchange] = {"us_per_layer": round(float(t[0].item()), 2), "mode": mode,
-                         "exchange": layers[0].exchange, "kernel_errors": int(t[1].item())}
-        del layers
+        res[name] = entry
+        del layers, xs, x, views
         torch.cuda.synchronize()
+        torch.cuda.empty_cache()
     if dist.get_rank() == 0:
         # the same layers on one GPU, every head (the unsharded reference point)
-        g = torch.Generator(device=dev).manual_seed(5150)
-        rts = []
-        for li in range(SH_LAYERS):
-            rt = nkv.M12LayerRuntime(li, nkv.M12Config(max_model_len=SH_CTX + 4096, device=dev))
-            rt.reserve_blocks(SH_CTX // B)
-            for c in range(SH_CTX // 4096):
-                k = torch.randn(4096, HKV, D, generator=g, device=dev).bfloat16()
-                v = torch.randn(4096, HKV, D, generator=g, device=dev).bfloat16()
-                if c == 0:
-                    rt.prefill_first(None, k, v)
-                else:
-                    rt._store_kv(k, v)
-            rts.append(rt)
-        q = torch.randn(SH_LAYERS, 1, HQ, D, generator=g, device=dev).bfloat16()
-        k = torch.randn(SH_LAYERS, 1, HKV, D, generator=g, device=dev).bfloat16()
-        v = torch.randn(SH_LAYERS, 1, HKV, D, generator=g, device=dev).bfloat16()
-        stream = torch.cuda.Stream(dev)
-        with torch.cuda.stream(stream):
-            for _ in range(3):
-                for li, rt in enumerate(rts):
-                    rt.decode(q[li], k[li], v[li], dev)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=stream):
-                for li, rt in enumerate(rts):
-                    rt.decode(q[li], k[li], v[li], dev)
-            for _ in range(3):
-                graph.replay()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            for _ in range(steps):
-                graph.replay()
-            e1.record(stream)
-        e1.synchronize()
-        res["unsharded_1gpu_us_per_layer"] = round(e0.elapsed_time(e1) * 1000.0 / (steps * SH_LAYERS), 2)
-        del graph, rts
+        rts = _sharded_build(nkv, dev, lambda li: nkv.M12LayerRuntime(
+            li, nkv.M12Config(max_model_len=SH_CTX + 4096, device=dev)))
+        xs, x, views = _sharded_inputs(dev)
+
+        def step1():
+            for rt, (q, k, v) in zip(rts, views):
+                rt.decode(q, k, v, dev)
+        us, _ = _graph_time(step1, xs, x, stream, steps, False)
+        res["unsharded_1gpu_us_per_layer"] = round(us, 2)
+        del rts, xs, x, views
         torch.cuda.synchronize()
+        torch.cuda.empty_cache()
     dist.barrier()
     return res
 

@@ -388,11 +388,10 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel(SelectParams p) {
 // CTAs): a lighter grid of at most one 256-thread CTA per SM, so that the
 // attention CTAs launched after it (programmatic dependent launch) are
 // resident beside it and run their prologue while it scores.  CTA c owns
-// blocks [c * bpc, (c + 1) * bpc) for every KV head; warp w scores heads w,
-// w + 8, ...; per head the warp takes its blocks SC_UPW at a time with every
-// representative load of the group issued before the arithmetic (one DRAM
-// round trip per group).  Lane layout and summation order are unit_score's,
-// so the scores are bit-identical to select_kernel's.
+// blocks [c * bpc, (c + 1) * bpc) for every KV head; block score = max over
+// the CTA's warps' partial maxima, protected blocks -inf.  Two kernels with
+// the same interface: score_kernel (fp32 FMA, for up to 4 blocks per CTA)
+// and score_kernel_tc (tensor cores, for larger ranges).
 // Bulk prefetch of `bytes` (a multiple of 16, 16-byte aligned) into L2.
 __device__ __forceinline__ void prefetch_l2_range(const void* src, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
@@ -400,9 +399,17 @@ __device__ __forceinline__ void prefetch_l2_range(const void* src, uint32_t byte
 
 constexpr int SC_THREADS = 256;
 constexpr int SC_WARPS = SC_THREADS / 32;
-constexpr int SC_UPW = 4;       // (head, block) units per warp in flight
+constexpr int SC_UPW = 4;       // blocks per CTA are a multiple of this
 constexpr int SC_BPC_MAX = 64;  // blocks per CTA
+constexpr int SC_ROWS = 32;     // representative rows per unit (4 n-tiles)
 
+// Scalar form for small block ranges (up to 4 blocks per CTA, e.g. 32K
+// tokens): warp w scores heads w, w + 8, ...; per head the warp takes its
+// blocks SC_UPW at a time with every representative load of the group issued
+// before the arithmetic (one DRAM round trip per group).  Lane layout and
+// summation order are unit_score's, so the scores are bit-identical to
+// select_kernel's.  With more blocks per CTA its fp32 FMA stream grows with
+// the blocks and score_kernel_tc (below) is faster.
 template <int G>
 __global__ void __launch_bounds__(SC_THREADS) score_kernel(SelectParams p) {
   __shared__ float part[SC_WARPS][SC_BPC_MAX];
@@ -495,6 +502,135 @@ __global__ void __launch_bounds__(SC_THREADS) score_kernel(SelectParams p) {
   }
 }
 
+// Tensor-core form for larger block ranges (e.g. 16 blocks per CTA at 128K
+// tokens).  The work is cut into units of 32 representative rows of one head
+// (contiguous in [hkv][max_blocks][r][D]); warp w takes units w, w + 8, ...,
+// so every warp has work whatever the number of heads.  A unit is scored with
+// mma.sync m16n8k16 (bf16 in, fp32 accumulate): the head's G query rows are
+// the M rows (rows >= G zero), the 32 representative rows four n-tiles of 8
+// columns, K = D in a permuted order that is the same for both operands (at
+// k-steps 2i and 2i + 1 lane quad t holds dims 32 i + 8 t ... + 7, one 16-byte
+// load per operand row), so each product is a full dot product.  All 16 loads
+// of a lane for the unit are issued before its 32 mma.  Per representative
+// row the max over the query rows (shuffles), then per block the max over its
+// r rows, kept per (warp, block) in shared memory.  Its sums run in the tensor
+// core's order, so its scores can differ from score_kernel's in the last bits.
+template <int G>
+__global__ void __launch_bounds__(SC_THREADS) score_kernel_tc(SelectParams p) {
+  static_assert(G >= 1 && G <= 8, "query rows per KV head fit the 16 M rows");
+  __shared__ float part[SC_WARPS][SC_BPC_MAX];
+  __shared__ float s_rows[SC_WARPS][SC_ROWS];
+  __shared__ unsigned char s_prot[SC_BPC_MAX];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int b0 = blockIdx.x * p.bpc;
+  const int nb = min(p.bpc, p.nblocks - b0);
+  // launched with programmatic dependent launch: the CTAs may be resident
+  // before the preceding kernel has finished.  Meanwhile each warp prefetches
+  // its heads' representative rows into L2 (a prefetch reads nothing into the
+  // SM, so it cannot see data older than what the loads below will); every
+  // read waits for the preceding kernel, and the dependent attention grid is
+  // released only then (its prologue reads q and the current token, which the
+  // preceding kernel may produce)
+  if (lane == 0 && nb > 0)
+    for (int h = warp; h < p.hkv; h += SC_WARPS)
+      prefetch_l2_range(p.reps + ((long long)h * p.max_blocks + b0) * p.r * NKV_D, (uint32_t)(nb * p.r * NKV_D * 2));
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int i = threadIdx.x; i < SC_WARPS * SC_BPC_MAX; i += SC_THREADS) (&part[0][0])[i] = -INFINITY;
+  for (int i = threadIdx.x; i < SC_BPC_MAX; i += SC_THREADS) s_prot[i] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < p.n_protected; i += SC_THREADS) {
+    const int b = __ldg(p.protected_ids + i) - b0;
+    if (b >= 0 && b < nb) s_prot[b] = 1;
+  }
+  const int rows = nb * p.r;  // representative rows of one head in this CTA
+  const int upr = (rows + SC_ROWS - 1) / SC_ROWS;
+  int cur_h = -1;
+  uint4 qf[4] = {};
+  for (int u = warp; u < upr * p.hkv; u += SC_WARPS) {
+    const int h = u / upr, row0 = (u % upr) * SC_ROWS;
+    if (h != cur_h) {  // this lane's dims 32 i + 8 t ... + 7 of query row g of head h
+      cur_h = h;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        qf[i] = make_uint4(0u, 0u, 0u, 0u);
+        if (g < G) {
+          const __nv_bfloat16* qs = p.q + (long long)(h * G + g) * p.q_head_stride + i * 32 + t * 8;
+          if (NKV_INB(p.err, 51, qs - p.q, 8, p.ext_q)) qf[i] = __ldg(reinterpret_cast<const uint4*>(qs));
+        }
+      }
+    }
+    const __nv_bfloat16* rbase = p.reps + ((long long)h * p.max_blocks + b0) * p.r * NKV_D;
+    uint4 rf[SC_ROWS / 8][4];
+#pragma unroll
+    for (int j = 0; j < SC_ROWS / 8; ++j) {
+      const int rr = row0 + j * 8 + g;
+      const long long off = (long long)rr * NKV_D + t * 8;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        rf[j][i] = make_uint4(0u, 0u, 0u, 0u);
+        if (rr < rows &&
+            NKV_INB(p.err, 50, ((long long)h * p.max_blocks + b0) * p.r * NKV_D + off + i * 32, 8, p.ext_reps))
+          rf[j][i] = __ldg(reinterpret_cast<const uint4*>(rbase + off + i * 32));
+      }
+    }
+    float c[SC_ROWS / 8][4];
+#pragma unroll
+    for (int j = 0; j < SC_ROWS / 8; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+      for (int j = 0; j < SC_ROWS / 8; ++j) mma_bf16(c[j], qf[i].x, 0u, qf[i].y, 0u, rf[j][i].x, rf[j][i].y);
+#pragma unroll
+      for (int j = 0; j < SC_ROWS / 8; ++j) mma_bf16(c[j], qf[i].z, 0u, qf[i].w, 0u, rf[j][i].z, rf[j][i].w);
+    }
+    // c[j][0..1]: query row g x representative rows row0 + 8 j + 2 t, + 1;
+    // max over the query rows (lanes of a column), then lanes 0..3 hold the
+    // unit's 32 row scores
+#pragma unroll
+    for (int j = 0; j < SC_ROWS / 8; ++j) {
+      float v0 = g < G ? c[j][0] : -INFINITY, v1 = g < G ? c[j][1] : -INFINITY;
+#pragma unroll
+      for (int x = 4; x < 32; x <<= 1) {
+        v0 = fmaxf(v0, __shfl_xor_sync(FULL, v0, x));
+        v1 = fmaxf(v1, __shfl_xor_sync(FULL, v1, x));
+      }
+      if (g == 0) {
+        s_rows[warp][j * 8 + 2 * t] = v0;
+        s_rows[warp][j * 8 + 2 * t + 1] = v1;
+      }
+    }
+    __syncwarp();
+    // blocks of the unit: lane l takes block row0 / r + l (its rows inside the unit)
+    const int blo = row0 / p.r, bhi = min((row0 + SC_ROWS - 1) / p.r, nb - 1);
+    if (lane <= bhi - blo) {
+      const int bl = blo + lane;
+      const int ra = max(row0, bl * p.r), rb = min(min(row0 + SC_ROWS, (bl + 1) * p.r), rows);
+      float m = -INFINITY;
+      for (int rr = ra; rr < rb; ++rr) m = fmaxf(m, s_rows[warp][rr - row0]);
+      part[warp][bl] = fmaxf(part[warp][bl], m);
+    }
+    __syncwarp();
+  }
+  __syncthreads();
+  if (threadIdx.x < nb) {
+    const int b = b0 + threadIdx.x;
+    float m = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < SC_WARPS; ++w) m = fmaxf(m, part[w][threadIdx.x]);
+    if (s_prot[threadIdx.x]) m = -INFINITY;
+    p.scores[b] = m;
+    if (p.out_block_scores) p.out_block_scores[b] = m;
+    if (p.xs_P) {
+      const uint32_t ep = ld_peer_u32(p.xs_epoch);
+      const u64 w = ((u64)step_tag(ep) << 32) | f32_order(m);
+      const long long at = ((long long)(ep & 1u) * p.xs_P + p.xs_rank) * p.xs_cap + b;
+      for (int r = 0; r < p.xs_P; ++r) st_peer_u64(p.xs_peer[r] + at, w);
+    }
+  }
+}
+
 }  // namespace nkv
 
 using namespace nkv;
@@ -515,10 +651,13 @@ static int launch_score(cudaStream_t st, SelectParams& p, int G) {
   lc.attrs = attr;
   lc.numAttrs = 1;
   cudaError_t e;
+  // NKV_SCORE_TC: 1 always the tensor-core form, 0 never, default above 4 blocks per CTA
+  const int tc_knob = knob("NKV_SCORE_TC", -1);
+  const bool tc = tc_knob > 0 || (tc_knob < 0 && p.bpc > SC_UPW);
   switch (G) {
-    case 1: e = cudaLaunchKernelEx(&lc, score_kernel<1>, p); break;
-    case 2: e = cudaLaunchKernelEx(&lc, score_kernel<2>, p); break;
-    case 4: e = cudaLaunchKernelEx(&lc, score_kernel<4>, p); break;
+    case 1: e = tc ? cudaLaunchKernelEx(&lc, score_kernel_tc<1>, p) : cudaLaunchKernelEx(&lc, score_kernel<1>, p); break;
+    case 2: e = tc ? cudaLaunchKernelEx(&lc, score_kernel_tc<2>, p) : cudaLaunchKernelEx(&lc, score_kernel<2>, p); break;
+    case 4: e = tc ? cudaLaunchKernelEx(&lc, score_kernel_tc<4>, p) : cudaLaunchKernelEx(&lc, score_kernel<4>, p); break;
     default:
       set_error("score: unsupported G=%d", G);
       return NKV_ERR_UNSUPPORTED;

@@ -14,7 +14,17 @@ NVLink:
 2. the per-rank attention outputs [1, Hq/P, D] are gathered into [1, Hq, D]
    (the all-gather before o_proj).
 
-Two forms of the exchange:
+Two forms of the scoring:
+
+- ``scoring="sharded"`` (option B): each rank scores its own heads and the
+  block scores are max-reduced over the ranks (one exchange), as above;
+- ``scoring="replicated"`` (option A): every rank also keeps the
+  representatives of every KV head (built from the full-width keys each rank
+  receives; the store itself stays sharded) and scores all heads itself, so
+  every rank computes the single-GPU scores with no exchange; the output
+  gather (one NCCL all-gather) is the only collective.
+
+Two forms of the exchange for sharded scoring:
 
 - ``exchange="peer"`` (the default where every pair of GPUs has peer access):
   inside the kernels, through per-layer exchange buffers that every rank maps
@@ -49,9 +59,14 @@ class KVHeadShardedLayer:
     ``_store_kv``, ``block_scores_dev`` and ``decode_ranked``.
     """
 
-    def __init__(self, layer_id: int, cfg: M12Config, group=None, runtime_factory=None, exchange: str = "auto"):
+    def __init__(self, layer_id: int, cfg: M12Config, group=None, runtime_factory=None, exchange: str = "auto",
+                 scoring: str = "sharded"):
         if exchange not in ("auto", "peer", "nccl"):
             raise ValueError(f"exchange must be 'auto', 'peer' or 'nccl', not {exchange!r}")
+        if scoring not in ("sharded", "replicated"):
+            raise ValueError(f"scoring must be 'sharded' or 'replicated', not {scoring!r}")
+        if scoring == "replicated" and runtime_factory is not None:
+            raise ValueError("replicated scoring needs the CUDA runtime (its representatives store)")
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -64,7 +79,18 @@ class KVHeadShardedLayer:
         self.cfg = cfg
         self.local_cfg = dataclasses.replace(cfg, num_heads=self.hq, num_kv_heads=self.hkv)
         self.rt = (runtime_factory or M12LayerRuntime)(layer_id, self.local_cfg)
-        self.exchange = "nccl" if (self.world == 1 or exchange == "nccl" or runtime_factory is not None) else exchange
+        self.scoring = scoring
+        self.exchange = "nccl" if (self.world == 1 or exchange == "nccl" or runtime_factory is not None
+                                   or scoring == "replicated") else exchange
+        # replicated scoring: every KV head's representatives [Hkv][max_blocks][r][D]
+        self.reps_all = self._rep_index_all = self._scores = None
+        if scoring == "replicated":
+            dev = self.rt.device
+            self.reps_all = torch.zeros(cfg.num_kv_heads, self.rt.max_blocks, cfg.r, cfg.head_dim,
+                                        dtype=torch.bfloat16, device=dev)
+            self._rep_index_all = torch.zeros(cfg.num_kv_heads, self.rt.max_blocks, cfg.r, dtype=torch.int16,
+                                              device=dev)
+            self._scores = torch.empty(self.rt.max_blocks, dtype=torch.float32, device=dev)
         self._exch = None      # ctypes array of the ranks' exchange buffers (peer form)
         self._exch_cap = 0     # block capacity they were made for
         self._own = None       # this rank's buffer
@@ -86,11 +112,50 @@ class KVHeadShardedLayer:
         return self.rt.last_block_ids
 
     def prefill_first(self, q, k, v) -> dict:
-        return self.rt.prefill_first(None if q is None else self._q(q), self._kv(k), self._kv(v))
+        start = self.rt.nblocks_filled
+        out = self.rt.prefill_first(None if q is None else self._q(q), self._kv(k), self._kv(v))
+        self._store_reps_all(k, start)
+        return out
 
     def store(self, k: torch.Tensor, v: torch.Tensor) -> None:
         """Append a chunk of history (the store half of prefill)."""
+        start = self.rt.nblocks_filled
         self.rt._store_kv(self._kv(k), self._kv(v))
+        self._store_reps_all(k, start)
+
+    def _store_reps_all(self, k: torch.Tensor, start_block: int) -> None:
+        """Replicated scoring: the representatives of every KV head for the
+        chunk's blocks (the store kernel's representatives-only form)."""
+        if self.reps_all is None:
+            return
+        cfg = self.cfg
+        k = k if (k.stride(-1) == 1 and k.data_ptr() % 16 == 0) else k.contiguous()
+        a = _lib.StoreArgs()
+        a.k = a.v = k.data_ptr()
+        a.k_row_stride, a.k_head_stride = k.stride(0), k.stride(1)
+        a.v_row_stride, a.v_head_stride = k.stride(0), k.stride(1)
+        a.T, a.hkv, a.head_dim, a.block_size, a.r = k.shape[0], cfg.num_kv_heads, cfg.head_dim, cfg.block_size, cfg.r
+        a.start_block, a.max_blocks = start_block, self.rt.max_blocks
+        a.store_kind = _lib.STORE_BF16
+        a.k_store = a.v_store = 0
+        a.reps, a.rep_index = self.reps_all.data_ptr(), self._rep_index_all.data_ptr()
+        a.sink_cap = a.sink_write = a.ring_cap = 0
+        _lib.call("nkv_store_chunk", torch.cuda.current_stream(self.rt.device).cuda_stream, C.byref(a))
+
+    def scores_all(self, q: torch.Tensor) -> torch.Tensor:
+        """Replicated scoring: the single-GPU block scores from every query head
+        and every KV head's representatives ([nblocks] fp32)."""
+        cfg, rt = self.cfg, self.rt
+        q = q if q.ndim == 3 else q.unsqueeze(0)
+        if q.stride(-1) != 1 or q.stride(1) % 8 or q.data_ptr() % 16:
+            q = q.contiguous()
+        nb = rt.nblocks_filled
+        prot, nprot = rt._protected_dev(nb)
+        ws = rt._select_ws(1)
+        _lib.call("nkv_select_scores", torch.cuda.current_stream(rt.device).cuda_stream, q.data_ptr(), q.stride(0),
+                  q.stride(1), cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, self.reps_all.data_ptr(), cfg.r,
+                  rt.max_blocks, nb, prot.data_ptr(), nprot, self._scores.data_ptr(), ws.data_ptr(), ws.numel())
+        return self._scores[:nb]
 
     # ---- peer exchange buffers (collective: every rank calls at the same point) ----
     def _peer_ok(self) -> bool:
@@ -156,12 +221,16 @@ class KVHeadShardedLayer:
             self.rt.shard_scores(self._q(q), self._exch, self.world, self.rank)
             return self.rt.decode_shard(self._q(q), self._kv(k), self._kv(v), self._exch, self.world, self.rank,
                                         out)
-        scores = self.rt.block_scores_dev(self._q(q))
-        if self.world > 1:
-            dist.all_reduce(scores, op=dist.ReduceOp.MAX, group=self.group)
+        if self.scoring == "replicated":
+            scores = self.scores_all(q)
+        else:
+            scores = self.rt.block_scores_dev(self._q(q))
+            if self.world > 1:
+                dist.all_reduce(scores, op=dist.ReduceOp.MAX, group=self.group)
         o = self.rt.decode_ranked(self._q(q), self._kv(k), self._kv(v), scores)
         if self.world == 1:
             return o
-        parts = [torch.empty_like(o) for _ in range(self.world)]
-        dist.all_gather(parts, o.contiguous(), group=self.group)
-        return torch.cat(parts, dim=1)
+        # rank-major rows = head-major rows: rank i holds query heads [i hq, (i + 1) hq)
+        out = torch.empty(self.world * o.numel(), dtype=o.dtype, device=o.device)
+        dist.all_gather_into_tensor(out, o.contiguous().view(-1), group=self.group)
+        return out.view(1, self.cfg.num_heads, self.cfg.head_dim)

@@ -7,9 +7,13 @@ oracle within the parity tolerance, with the selected block ids equal to the
 oracle's own selection modulo 1e-3 score ties, and must match the single-GPU
 runtime (ids identical: each rank's block scores are the same fp32 values the
 single GPU computes for those heads and the maximum over ranks is exact).
-Both exchange forms: NCCL collectives, and the peer-memory exchange inside the
-kernels (several steps in a row, so both parities of the exchange buffers and
-the step tags are exercised; no wait may time out).
+Sharded scoring with both exchange forms: NCCL collectives, and the
+peer-memory exchange inside the kernels (several steps in a row, so both
+parities of the exchange buffers and the step tags are exercised; no wait may
+time out).  Replicated scoring (every rank scores all heads from its copy of
+every head's representatives, the output all-gather the only collective):
+the outputs equal the single GPU's bit for bit (the same scores, the same
+kernel per head).
 """
 import importlib
 import os
@@ -52,7 +56,10 @@ def _run(rank, world, q_out, exchange):
     nkv = importlib.import_module(PKG_NAME)
     dev = torch.device("cuda", rank)
     cfg = nkv.M12Config(max_model_len=16384, device=dev)
-    layer = nkv.KVHeadShardedLayer(0, cfg, exchange=exchange)
+    if exchange == "replicated":
+        layer = nkv.KVHeadShardedLayer(0, cfg, exchange="nccl", scoring="replicated")
+    else:
+        layer = nkv.KVHeadShardedLayer(0, cfg, exchange=exchange)
     single = nkv.M12LayerRuntime(0, cfg) if rank == 0 else None
     oracle = orc.OracleLayer(orc.OracleConfig()) if rank == 0 else None
     g = torch.Generator().manual_seed(3)  # host generator: every rank draws the same inputs
@@ -87,14 +94,14 @@ def _run(rank, world, q_out, exchange):
     torch.cuda.synchronize()
     err = int(layer.rt._att_ws[:4].view(torch.int32).item())
     assert err == 0, f"rank {rank}: kernel error word {err}"
-    assert layer.exchange == exchange, (layer.exchange, exchange)
+    assert layer.exchange == ("nccl" if exchange == "replicated" else exchange), (layer.exchange, exchange)
     layer.close()
     if rank == 0:
         q_out.put(("ok", 0, [tuple(t.numpy() for t in r) for r in out]))
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
-@pytest.mark.parametrize("exchange", ["nccl", "peer"])
+@pytest.mark.parametrize("exchange", ["nccl", "peer", "replicated"])
 def test_kv_head_sharding(world, exchange):
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
@@ -116,3 +123,5 @@ def test_kv_head_sharding(world, exchange):
         assert ok, why
         torch.testing.assert_close(torch.from_numpy(got), torch.from_numpy(o_want), atol=ATOL, rtol=RTOL)
         torch.testing.assert_close(torch.from_numpy(got), torch.from_numpy(want), atol=ATOL, rtol=RTOL)
+        if exchange == "replicated":
+            assert (got == want).all(), "replicated scoring must reproduce the single GPU bit for bit"
