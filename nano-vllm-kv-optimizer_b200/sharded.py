@@ -112,14 +112,14 @@ class KVHeadShardedLayer:
         return self.rt.last_block_ids
 
     def prefill_first(self, q, k, v) -> dict:
-        start = self.rt.nblocks_filled
+        start = self.rt.nblocks_filled if self.reps_all is not None else 0
         out = self.rt.prefill_first(None if q is None else self._q(q), self._kv(k), self._kv(v))
         self._store_reps_all(k, start)
         return out
 
     def store(self, k: torch.Tensor, v: torch.Tensor) -> None:
         """Append a chunk of history (the store half of prefill)."""
-        start = self.rt.nblocks_filled
+        start = self.rt.nblocks_filled if self.reps_all is not None else 0
         self.rt._store_kv(self._kv(k), self._kv(v))
         self._store_reps_all(k, start)
 
