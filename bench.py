@@ -444,13 +444,42 @@ def model_measure(nkv, dev, steps=64, warmup=8, layer_us=None):
     toks = loop.hist[:warmup + steps].tolist()
     model.check_errors()
     loop.close()
+    # speculative verification through the model (eager): rounds of one verify
+    # pass over [current token, 4 drafts] and a commit of all 5 (full
+    # acceptance: the upper bound of a drafter), shared and per-query selection
+    spec = {}
+    cur = int(toks[-1])
+    for lossless in (False, True):
+        for rt in model.runtimes:
+            rt.verify_lossless = lossless
+        times = []
+        for r in range(2 + 8):
+            drafts = [int(t) for t in toks[(r * 4) % 60:(r * 4) % 60 + 4]]
+            torch.cuda.synchronize()
+            e0.record()
+            logits = model.verify([cur] + drafts)
+            model.commit_verified(5)
+            e1.record()
+            e1.synchronize()
+            if r >= 2:
+                times.append(e0.elapsed_time(e1))
+            cur = int(logits[-1].argmax())
+        ms_v = statistics.median(times)
+        spec["per_query" if lossless else "shared"] = {
+            "verify_round_ms": round(ms_v, 3), "tok_s_at_full_acceptance": round(5000.0 / ms_v, 1)}
+    for rt in model.runtimes:
+        rt.verify_lossless = False
+    model.check_errors()
     del loop, model
     torch.cuda.empty_cache()
     rec = {"workload": "Qwen3-4B architecture (36 layers, random init bf16), 32768-token prompt in 4096-token "
                        "chunks, greedy decode from one CUDA graph per token",
            "decode_tok_s": round(1000.0 / ms, 1), "decode_ms_per_token": round(ms, 4),
            "prefill_ttft_ms": round(ttft_ms, 1), "decode_steps_timed": steps,
-           "first_tokens": toks[:8]}
+           "first_tokens": toks[:8],
+           "speculative_verify": dict(spec, note="eager verify pass over [current, 4 drafts] through the 36 "
+                                                 "layers + commit of all 5 tokens, median of 8 rounds; tok/s "
+                                                 "at 100 % acceptance is the ceiling a drafter could reach")}
     if layer_us is not None:
         rec["sparse_attention_share"] = round(layer_us * arch.num_layers / (ms * 1000.0), 3)
     return rec

@@ -18,17 +18,22 @@ from .m12_runtime import (
 )
 from .decode_graph import DecodeGraph, DeviceRingHeads
 from .qwen3_harness import DecodeLoop, Qwen3Arch, Qwen3SparseModel
+from .proposers import DraftArch, DraftModelProposer, NgramProposer, StaticDraftModel
 from .sharded import KVHeadShardedLayer
 
 __all__ = [
     "DecodeGraph",
     "DecodeLoop",
+    "DraftArch",
+    "DraftModelProposer",
     "DeviceRingHeads",
     "KVHeadShardedLayer",
     "M12Config",
     "M12LayerRuntime",
+    "NgramProposer",
     "Qwen3Arch",
     "Qwen3SparseModel",
+    "StaticDraftModel",
     "dynamic_top_k_from_scores",
     "prefill_query_summaries",
     "prefill_recent_slice",

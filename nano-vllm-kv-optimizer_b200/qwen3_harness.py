@@ -278,6 +278,87 @@ class Qwen3SparseModel:
             out.append(tok)
         return [int(t) for t in torch.cat(out).tolist()]
 
+    # ------------------------------------------------------------------
+    # speculative decoding: verify, commit, rollback
+    # ------------------------------------------------------------------
+    @torch.inference_mode()
+    def verify(self, tokens) -> torch.Tensor:
+        """One sparse verification pass over Tq tokens at positions
+        ``position .. position + Tq - 1`` (the first is the current unprocessed
+        token, the rest are draft proposals): every layer runs its runtime's
+        ``verify_tokens`` (shared or per-query selection over the frozen
+        history, nothing committed).  Returns the logits [Tq, vocab]; row i
+        predicts the token after ``tokens[i]``.  Reference:
+        ``ModelRunner.run_verify`` (model_runner.py:478-507)."""
+        ids = torch.as_tensor(tokens, dtype=torch.int64).view(-1).to(self.device)
+        Tq = ids.numel()
+        pos = torch.arange(self.position, self.position + Tq, dtype=torch.int64, device=self.device)
+        rts = self.runtimes
+        for rt in rts:
+            rt.verify_mode = True
+        try:
+            hidden = self.forward(ids, pos, "verify", last_only=False)
+        finally:
+            for rt in rts:
+                rt.verify_mode = False
+        return self.logits(hidden)
+
+    def commit_verified(self, n: int) -> None:
+        """Make the first n tokens of the last verify pass part of the sequence
+        (their K/V enter every layer's recent window); the rest are dropped."""
+        for rt in self.runtimes:
+            rt.commit_verified(n)
+        self.position += max(0, int(n))
+
+    def rollback_verified(self) -> None:
+        """Discard the last verify pass."""
+        for rt in self.runtimes:
+            rt.rollback_verified()
+
+    @torch.inference_mode()
+    def speculative_generate(self, prompt_ids: torch.Tensor, steps: int, proposer, k: int = 4,
+                             chunk: int = 4096, lossless: bool = False) -> tuple[list[int], dict]:
+        """Greedy speculative decoding: the prefill's token plus ``steps`` more.
+
+        Every round the proposer drafts up to k tokens after the current one;
+        one verify pass over [current, drafts] gives the target's greedy token
+        after each; the drafts are accepted while they equal it, the accepted
+        prefix (and the current token) is committed, and the target's token
+        after the last accepted one becomes the next current token, so a round
+        emits between 1 and k + 1 tokens.  A round without drafts is a plain
+        decode step.  ``lossless`` selects the per-query (union + mask)
+        verification.  Proposer interface (the reference's, proposers.py):
+        ``prefill(prompt_ids)``, ``propose(last_token, k, pos) -> list[int]``,
+        ``note_accepted(tokens)``.  Returns (tokens, stats)."""
+        for rt in self.runtimes:
+            rt.verify_lossless = bool(lossless)
+        tok = int(self.prefill(prompt_ids, chunk))
+        proposer.prefill([int(t) for t in prompt_ids.view(-1).tolist()])
+        out = [tok]
+        stats = {"rounds": 0, "verify_rounds": 0, "proposed": 0, "accepted": 0}
+        while len(out) < steps + 1:
+            want = min(k, steps + 1 - len(out) - 1)
+            drafts = [int(t) for t in proposer.propose(tok, want, self.position)][:max(0, want)] if want > 0 else []
+            stats["rounds"] += 1
+            if not drafts:
+                tok = int(self.decode_step(torch.tensor([tok], device=self.device)))
+                out.append(tok)
+                continue
+            logits = self.verify([tok] + drafts)
+            target = logits.argmax(dim=-1).tolist()
+            n = 0
+            while n < len(drafts) and drafts[n] == target[n]:
+                n += 1
+            self.commit_verified(n + 1)
+            proposer.note_accepted(drafts[:n])
+            out.extend(drafts[:n])
+            tok = int(target[n])
+            out.append(tok)
+            stats["verify_rounds"] += 1
+            stats["proposed"] += len(drafts)
+            stats["accepted"] += n
+        return out[:steps + 1], stats
+
     def check_errors(self):
         word = int(self.err[0].item())
         if word:

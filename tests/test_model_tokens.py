@@ -121,6 +121,28 @@ def _shadowed_runtime(nkv):
             self._compare("decode", o, self.shadow.decode(q, k, v))
             self._check_ids("decode", ids)
             return o
+
+        def verify_tokens(self, q, k, v, device):
+            o = super().verify_tokens(q, k, v, device)
+            ids = self.last_verify_block_ids.clone()
+            if self.verify_lossless:
+                # per-query selection: the union and the output must be the oracle's own
+                want = self.shadow.verify(q, k, v, lossless=True)
+                if not torch.equal(ids.cpu(), self.shadow.own_ids.cpu()):
+                    self.failures.append((self.layer_id, "verify", "union", ids.tolist()[:8]))
+                else:
+                    self._compare("verify", o, want)
+                self.ids_log.append(("verify", ids.cpu()))
+            else:
+                # shared selection: the oracle attends arm A's blocks
+                self.shadow.force_ids = ids
+                self._compare("verify", o, self.shadow.verify(q, k, v, lossless=False))
+                self._check_ids("verify", ids)
+            return o
+
+        def commit_verified(self, n):
+            super().commit_verified(n)
+            self.shadow.commit(n)
     return Shadowed
 
 
