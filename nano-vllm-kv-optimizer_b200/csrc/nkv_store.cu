@@ -327,6 +327,269 @@ __global__ void __launch_bounds__(ST_THREADS) store_kernel(StoreParams p) {
     p.rep_index[((long long)h * p.max_blocks + blk) * p.r + tid] = (short)picks[tid];
 }
 
+// Store + representatives for 64-token blocks into a bf16 block store (or
+// representatives only), as two kernels that run at the same time: the copy
+// (block store, sink and ring rows; bound by HBM) and the representative
+// choice (bound by its chain of dependent steps), each over the same
+// (block, head) grid.  The copy grid lets the representatives grid start at
+// once (programmatic dependent launch); the representatives grid reads only
+// the chunk's keys, which the copy does not write, and waits for the copy grid
+// only at its very end, so that the pair completes together (a later kernel
+// in the stream sees the store, the sink and the ring written).
+//
+// In both, thread t owns chunk c = t % 16 (dims 8c .. 8c + 7) of rows
+// t / 16 + 16 j, j < 4, and issues all of its loads before its stores.
+constexpr int SB64 = 64;
+// The copy grid is smaller than the (block, head) grid and strides over it,
+// so that it leaves room on every SM for the representatives CTAs beside it.
+__global__ void __launch_bounds__(ST_THREADS) store_copy_b64(StoreParams p, int nblk) {
+  pdl_launch_dependents();
+  const int tid = threadIdx.x;
+  const int c = tid & 15, rg = tid >> 4;
+  const bool store = p.k_store != nullptr;
+  for (int u = blockIdx.x; u < nblk * p.hkv; u += gridDim.x) {
+  const int bl = u / p.hkv, h = u % p.hkv;
+  const int blk = p.start_block + bl;
+  const long long tile = ((long long)blk * p.hkv + h) * SB64;
+  uint4 kr[4], vr[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int gt = bl * SB64 + rg + 16 * j;
+    kr[j] = vr[j] = make_uint4(0, 0, 0, 0);
+    if (gt < p.T) {
+      kr[j] = __ldg(reinterpret_cast<const uint4*>(p.k + gt * p.k_row + h * p.k_head + c * 8));
+      vr[j] = __ldg(reinterpret_cast<const uint4*>(p.v + gt * p.v_row + h * p.v_head + c * 8));
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int row = rg + 16 * j, gt = bl * SB64 + row;
+    if (store) {
+      const long long o = (tile + row) * NKV_D + c * 8;
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.k_store) + o) = kr[j];
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.v_store) + o) = vr[j];
+    }
+    if (gt < p.T) {
+      if (gt < p.sink_write) {
+        const long long o = ((long long)h * p.sink_cap + gt) * NKV_D + c * 8;
+        *reinterpret_cast<uint4*>(p.sink_k + o) = kr[j];
+        *reinterpret_cast<uint4*>(p.sink_v + o) = vr[j];
+      }
+      if (gt >= p.ring_first && p.ring_cap > 0) {
+        const int slot = (p.ring_pos0 + gt) % p.ring_cap;
+        const long long o = ((long long)h * p.ring_cap + slot) * NKV_D + c * 8;
+        *reinterpret_cast<uint4*>(p.ring_k + o) = kr[j];
+        *reinterpret_cast<uint4*>(p.ring_v + o) = vr[j];
+      }
+    }
+  }
+  }
+}
+
+// Sum over the 16 lanes of a row group of four per-lane values x[j] (one per
+// row j): a transposing butterfly (5 shuffles instead of 16).  Returns the
+// full sum of row (lane >> 2) & 3; the 4 lanes that share bits 3..2 hold the
+// same value.  The order of the additions is fixed.
+__device__ __forceinline__ float rowsum16_t(const float (&x)[4], int lane) {
+  const bool b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
+  const float s0 = b3 ? x[0] : x[2], s1 = b3 ? x[1] : x[3];
+  const float r0 = __shfl_xor_sync(FULL, s0, 8), r1 = __shfl_xor_sync(FULL, s1, 8);
+  const float k0 = (b3 ? x[2] : x[0]) + r0, k1 = (b3 ? x[3] : x[1]) + r1;  // rows 2 b3, 2 b3 + 1
+  const float r = __shfl_xor_sync(FULL, b2 ? k0 : k1, 4);
+  float v = (b2 ? k1 : k0) + r;  // row 2 b3 + b2
+  v += __shfl_xor_sync(FULL, v, 2);
+  v += __shfl_xor_sync(FULL, v, 1);
+  return v;
+}
+
+// The representatives: the general kernel's rule with the key directions held
+// in registers.  Row norms by a transposing 16-lane shuffle sum, the division
+// correctly rounded as above, the directions also written into a shared fp32
+// tile from which the farthest-point steps read their reference direction;
+// the mean direction is a fixed-order sum of the threads' partial sums.  A
+// step is 8 fmas per row, one transposing row sum (lane l then holds row
+// rg + 16 ((l >> 2) & 3)), a per-warp first-index arg-best by shuffles, one
+// barrier, and the same shuffle reduction over the 8 warps' candidates in
+// every warp (no second barrier: the candidate slots alternate by step).  The
+// chosen raw key rows are read back from the input (L2) at the end.
+template <bool COPY>
+__global__ void __launch_bounds__(ST_THREADS, 4) store_reps_b64(StoreParams p) {
+  __shared__ __align__(16) float dir_t[SB64 * NKV_D];  // [row][D] k_row / |k_row|
+  __shared__ __align__(16) float part[16][NKV_D];      // per row group: sum of its 4 rows' directions
+  __shared__ float md[NKV_D];
+  __shared__ float red[4];
+  __shared__ float s_bv[2][ST_THREADS / 32];
+  __shared__ int s_bi[2][ST_THREADS / 32];
+  const int bl = blockIdx.x, h = blockIdx.y;
+  const int blk = p.start_block + bl;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c = tid & 15, rg = tid >> 4;  // chunk; row group (rows rg + 16 j)
+  const int my_j = (lane >> 2) & 3;      // the row of the group whose sums this lane ends with
+  const int my_row = rg + 16 * my_j;
+
+  uint4 kr[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int gt = bl * SB64 + rg + 16 * j;
+    kr[j] = make_uint4(0, 0, 0, 0);
+    if (gt < p.T) kr[j] = __ldg(reinterpret_cast<const uint4*>(p.k + gt * p.k_row + h * p.k_head + c * 8));
+  }
+  if constexpr (COPY) {  // the copy in the same CTA: V loads, then every store, from the registers
+    uint4 vr[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int gt = bl * SB64 + rg + 16 * j;
+      vr[j] = make_uint4(0, 0, 0, 0);
+      if (gt < p.T) vr[j] = __ldg(reinterpret_cast<const uint4*>(p.v + gt * p.v_row + h * p.v_head + c * 8));
+    }
+    const long long tile = ((long long)blk * p.hkv + h) * SB64;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int row = rg + 16 * j, gt = bl * SB64 + row;
+      if (p.k_store) {
+        const long long o = (tile + row) * NKV_D + c * 8;
+        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.k_store) + o) = kr[j];
+        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.v_store) + o) = vr[j];
+      }
+      if (gt < p.T) {
+        if (gt < p.sink_write) {
+          const long long o = ((long long)h * p.sink_cap + gt) * NKV_D + c * 8;
+          *reinterpret_cast<uint4*>(p.sink_k + o) = kr[j];
+          *reinterpret_cast<uint4*>(p.sink_v + o) = vr[j];
+        }
+        if (gt >= p.ring_first && p.ring_cap > 0) {
+          const int slot = (p.ring_pos0 + gt) % p.ring_cap;
+          const long long o = ((long long)h * p.ring_cap + slot) * NKV_D + c * 8;
+          *reinterpret_cast<uint4*>(p.ring_k + o) = kr[j];
+          *reinterpret_cast<uint4*>(p.ring_v + o) = vr[j];
+        }
+      }
+    }
+  }
+
+  // ---- directions (registers + shared tile) and partial mean sums -------------------
+  float dr[4][8];
+  {
+    float ss[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      unpack8(kr[j], dr[j]);
+      ss[j] = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss[j] = fmaf(dr[j][e], dr[j][e], ss[j]);
+    }
+    const float mine = rowsum16_t(ss, lane);
+    float pm[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) pm[e] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      // row j's sum sits in the lanes whose bits 3..2 are j
+      const float tot = __shfl_sync(FULL, mine, (lane & ~15) | (j << 2));
+      const float n = fmaxf(sqrtf(tot), 1e-12f);
+      const float y = __frcp_rn(n);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        dr[j][e] = div_rcp(dr[j][e], n, y);
+        pm[e] += dr[j][e];
+      }
+      float* dt = dir_t + (rg + 16 * j) * NKV_D + c * 8;
+      *reinterpret_cast<float4*>(dt) = make_float4(dr[j][0], dr[j][1], dr[j][2], dr[j][3]);
+      *reinterpret_cast<float4*>(dt + 4) = make_float4(dr[j][4], dr[j][5], dr[j][6], dr[j][7]);
+    }
+    *reinterpret_cast<float4*>(&part[rg][c * 8]) = make_float4(pm[0], pm[1], pm[2], pm[3]);
+    *reinterpret_cast<float4*>(&part[rg][c * 8 + 4]) = make_float4(pm[4], pm[5], pm[6], pm[7]);
+  }
+  __syncthreads();
+  if (tid < NKV_D) {  // mean direction (unnormalised) and its squared norm per warp
+    float m = 0.f;
+#pragma unroll
+    for (int g = 0; g < 16; ++g) m += part[g][tid];
+    m *= 1.0f / SB64;  // exact: a power of two
+    md[tid] = m;
+    const float sq = warp_sum(m * m);
+    if (lane == 0) red[warp] = sq;
+  }
+  __syncthreads();
+  const float nrm = fmaxf(sqrtf(((red[0] + red[1]) + red[2]) + red[3]), 1e-12f);
+  const float nrm_y = __frcp_rn(nrm);
+  float ref[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) ref[e] = div_rcp(md[c * 8 + e], nrm, nrm_y);
+
+  // ---- r steps: step 0 max cosine to the mean direction, then farthest point --------
+  float worst = 0.f;  // running max cosine of this lane's row to the picks
+  bool taken = false;
+  int pk[8];
+#pragma unroll
+  for (int s = 0; s < 8; ++s) {
+    pk[s] = 0;
+    if (s >= p.r) continue;  // uniform
+    if (s > 0) {
+      const float* pr = dir_t + pk[s - 1] * NKV_D + c * 8;
+      const float4 a = *reinterpret_cast<const float4*>(pr), b = *reinterpret_cast<const float4*>(pr + 4);
+      ref[0] = a.x; ref[1] = a.y; ref[2] = a.z; ref[3] = a.w;
+      ref[4] = b.x; ref[5] = b.y; ref[6] = b.z; ref[7] = b.w;
+    }
+    float dd[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      dd[j] = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) dd[j] = fmaf(dr[j][e], ref[e], dd[j]);
+    }
+    const float d = rowsum16_t(dd, lane);  // row my_row
+    float bv = d;
+    if (s > 0) {
+      worst = s == 1 ? d : fmaxf(worst, d);
+      bv = taken ? 2.0f : fmaxf(worst, 0.f);
+    }
+    int bi = my_row;
+    // first-index arg-best over the warp's 8 rows (lanes 4 apart hold other rows)
+#pragma unroll
+    for (int m = 4; m < 32; m <<= 1) {
+      const float ob = __shfl_xor_sync(FULL, bv, m);
+      const int oi = __shfl_xor_sync(FULL, bi, m);
+      if (s == 0 ? (ob > bv || (ob == bv && oi < bi)) : (ob < bv || (ob == bv && oi < bi))) {
+        bv = ob;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      s_bv[s & 1][warp] = bv;
+      s_bi[s & 1][warp] = bi;
+    }
+    __syncthreads();
+    float fb = s_bv[s & 1][lane & 7];
+    int fi = s_bi[s & 1][lane & 7];
+#pragma unroll
+    for (int m = 1; m < 8; m <<= 1) {
+      const float ob = __shfl_xor_sync(FULL, fb, m);
+      const int oi = __shfl_xor_sync(FULL, fi, m);
+      if (s == 0 ? (ob > fb || (ob == fb && oi < fi)) : (ob < fb || (ob == fb && oi < fi))) {
+        fb = ob;
+        fi = oi;
+      }
+    }
+    const int pick = (fi >= 0 && fi < SB64) ? fi : 0;  // all-NaN guard
+    pk[s] = pick;
+    taken |= pick == my_row;
+  }
+  // ---- the chosen raw key rows (from the input, an L2 read) --------------------------
+#pragma unroll
+  for (int s = 0; s < 8; ++s) {
+    if (s >= p.r || (tid >> 4) != s) continue;
+    const int gt = bl * SB64 + pk[s];
+    uint4 kv = make_uint4(0, 0, 0, 0);
+    if (gt < p.T) kv = __ldg(reinterpret_cast<const uint4*>(p.k + gt * p.k_row + h * p.k_head + c * 8));
+    *reinterpret_cast<uint4*>(p.reps + (((long long)h * p.max_blocks + blk) * p.r + s) * NKV_D + c * 8) = kv;
+  }
+  if (p.rep_index && tid == 0)
+    for (int s = 0; s < p.r && s < 8; ++s) p.rep_index[((long long)h * p.max_blocks + blk) * p.r + s] = (short)pk[s];
+  // the copy grid (when there is one) has completed before this grid does
+  if (!COPY) pdl_wait();
+}
+
 // K channel scale: one CTA per kv head, thread = channel.
 __global__ void kscale_kernel(const __nv_bfloat16* k, int T, long long row, long long head,
                               float* out) {
@@ -480,8 +743,39 @@ extern "C" int nkv_store_chunk(nkv_stream_t stream, const nkv_store_args* a) {
   const bool stage_v = a->k_store != nullptr && a->store_kind != NKV_STORE_BF16;
   const size_t tile_b = (size_t)a->block_size * NKV_D;
   const size_t smem = tile_b * 2 + tile_b * 4 + (stage_v ? tile_b * 2 : 0) + (2 * ST_MAXB + NKV_D + 8) * 4;
-  if (ensure_smem(store_kernel, smem, "store_chunk")) return NKV_ERR_CUDA;
   dim3 grid(nb, a->hkv);
+  if (a->block_size == SB64 && (!a->k_store || a->store_kind == NKV_STORE_BF16) && knob("NKV_STORE_B64", 1)) {
+    const bool copy = a->k_store || p.sink_write > 0 || p.ring_cap > 0;
+    if (copy && knob("NKV_STORE_FUSED", 1)) {  // copy and representatives in one grid
+      store_reps_b64<true><<<grid, ST_THREADS, 0, (cudaStream_t)stream>>>(p);
+      return check_launch("store_chunk");
+    }
+    if (copy) {
+      const int units = nb * a->hkv;
+      int ctas = knob("NKV_STORE_COPY_CTAS", 0);
+      if (ctas <= 0) ctas = sm_count();
+      store_copy_b64<<<ctas < units ? ctas : units, ST_THREADS, 0, (cudaStream_t)stream>>>(p, nb);
+      const int rc = check_launch("store_chunk copy");
+      if (rc != NKV_OK) return rc;
+    }
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = copy ? 1 : 0;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = grid;
+    lc.blockDim = dim3(ST_THREADS);
+    lc.stream = (cudaStream_t)stream;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&lc, store_reps_b64<false>, p);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      set_error("store_chunk reps: launch failed: %s", cudaGetErrorString(e));
+      return NKV_ERR_CUDA;
+    }
+    return check_launch("store_chunk reps");
+  }
+  if (ensure_smem(store_kernel, smem, "store_chunk")) return NKV_ERR_CUDA;
   store_kernel<<<grid, ST_THREADS, smem, (cudaStream_t)stream>>>(p);
   return check_launch("store_chunk");
 }

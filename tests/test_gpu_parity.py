@@ -136,7 +136,12 @@ def test_store_and_reps_match_oracle(T, start):
     assert torch.equal(rt.v_cpu[start:start + nb].cpu(), vpad)
     reps, idx, margin = orc.build_reps(kpad, 4)
     got_idx = rt.rep_index[:, start:start + nb].long().cpu()
-    assert bool(((got_idx == idx) | (margin < 1e-5)).all())
+    # each pick equals the oracle's while the two follow the same picks; the
+    # first difference must be an fp32 near-tie (later picks depend on it)
+    differs = got_idx != idx
+    first = torch.where(differs.any(-1), differs.float().argmax(-1), torch.full(differs.shape[:-1], -1))
+    has = first >= 0
+    assert bool((torch.gather(margin, 2, first.clamp_min(0).unsqueeze(-1)).squeeze(-1)[has] < 1e-5).all())
     same = (got_idx == idx).all(-1)
     assert torch.equal(rt.reps_gpu[:, start:start + nb].cpu()[same], reps[same])
     n = min(64, T)
