@@ -2717,7 +2717,9 @@ int attend_step(nkv_stream_t stream, const nkv_attend_args* a, const void* reps,
 template <bool FUSED>
 static int launch_split(AttendParams p, const DecodeMaps& maps, const nkv_attend_args* a, cudaStream_t st) {
   const int early_max = (a->sink_len > 0 ? 1 : 0) + (a->ring_len > 0 ? (a->ring_cap + 63) / 64 : 0);
+  const int cl_knob = env_int("NKV_SPLIT_CL", 16);  // 16: try 16 then 8; 8: 8 only
   for (int CL : {16, 8}) {
+    if (CL > cl_knob) continue;
     const int max_early = CL >= 16 ? DS<16>::MAX_EARLY : DS<8>::MAX_EARLY;
     if (early_max > CL * max_early || a->n_sel > 32) continue;
     if (FUSED) {

@@ -433,10 +433,9 @@ __global__ void __launch_bounds__(SC_THREADS) score_kernel(SelectParams p) {
   for (int i = threadIdx.x; i < SC_WARPS * SC_BPC_MAX; i += SC_THREADS) (&part[0][0])[i] = -INFINITY;
   for (int i = threadIdx.x; i < SC_BPC_MAX; i += SC_THREADS) s_prot[i] = 0;
   __syncthreads();
-  for (int i = threadIdx.x; i < p.n_protected; i += SC_THREADS) {
-    const int b = __ldg(p.protected_ids + i) - b0;
-    if (b >= 0 && b < nb) s_prot[b] = 1;
-  }
+  // the protected ids are loaded now and applied after the scoring, so that
+  // their round trip overlaps it
+  const int prot0 = (int)threadIdx.x < p.n_protected ? __ldg(p.protected_ids + threadIdx.x) : -1;
   const bool jvalid = j < p.r;
   for (int h = warp; h < p.hkv; h += SC_WARPS) {
     // this lane's 16-dim slice of the head's G query rows
@@ -483,6 +482,11 @@ __global__ void __launch_bounds__(SC_THREADS) score_kernel(SelectParams p) {
         if (lane == 0 && u0 + u < nb) part[warp][u0 + u] = fmaxf(part[warp][u0 + u], best);
       }
     }
+  }
+  if (prot0 >= b0 && prot0 - b0 < nb) s_prot[prot0 - b0] = 1;
+  for (int i = threadIdx.x + SC_THREADS; i < p.n_protected; i += SC_THREADS) {
+    const int b = __ldg(p.protected_ids + i) - b0;
+    if (b >= 0 && b < nb) s_prot[b] = 1;
   }
   __syncthreads();
   if (threadIdx.x < nb) {
@@ -540,10 +544,9 @@ __global__ void __launch_bounds__(SC_THREADS) score_kernel_tc(SelectParams p) {
   for (int i = threadIdx.x; i < SC_WARPS * SC_BPC_MAX; i += SC_THREADS) (&part[0][0])[i] = -INFINITY;
   for (int i = threadIdx.x; i < SC_BPC_MAX; i += SC_THREADS) s_prot[i] = 0;
   __syncthreads();
-  for (int i = threadIdx.x; i < p.n_protected; i += SC_THREADS) {
-    const int b = __ldg(p.protected_ids + i) - b0;
-    if (b >= 0 && b < nb) s_prot[b] = 1;
-  }
+  // the protected ids are loaded now and applied after the scoring, so that
+  // their round trip overlaps it
+  const int prot0 = (int)threadIdx.x < p.n_protected ? __ldg(p.protected_ids + threadIdx.x) : -1;
   const int rows = nb * p.r;  // representative rows of one head in this CTA
   const int upr = (rows + SC_ROWS - 1) / SC_ROWS;
   int cur_h = -1;
@@ -612,6 +615,11 @@ __global__ void __launch_bounds__(SC_THREADS) score_kernel_tc(SelectParams p) {
       part[warp][bl] = fmaxf(part[warp][bl], m);
     }
     __syncwarp();
+  }
+  if (prot0 >= b0 && prot0 - b0 < nb) s_prot[prot0 - b0] = 1;
+  for (int i = threadIdx.x + SC_THREADS; i < p.n_protected; i += SC_THREADS) {
+    const int b = __ldg(p.protected_ids + i) - b0;
+    if (b >= 0 && b < nb) s_prot[b] = 1;
   }
   __syncthreads();
   if (threadIdx.x < nb) {
