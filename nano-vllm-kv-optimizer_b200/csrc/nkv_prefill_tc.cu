@@ -258,8 +258,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const TcParam
   constexpr int P = TC_M / G;  // positions per query tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.y;
-  const int p0 = ((int)gridDim.x - 1 - (int)blockIdx.x) * (TC_QT * P);  // latest positions first
+  // grid (heads, position tiles), heads fastest: CTAs start in order of
+  // decreasing work (the latest positions attend the most causal keys) across
+  // all heads, so the last wave holds the lightest tiles
+  const int h = blockIdx.x;
+  const int p0 = ((int)gridDim.y - 1 - (int)blockIdx.y) * (TC_QT * P);  // latest positions first
   const int off = p.n_cur - p.nq;
   const int last_pos = min(p.nq, p0 + TC_QT * P) - 1;
   const int lenA = min(p.ring_len, p.ring_cap - p.ring_start);
@@ -605,7 +608,7 @@ int prefill_tc(cudaStream_t st, const nkv_attend_args* a) {
   p.out_head = a->out_head_stride;
   p.err = (int*)a->workspace;
   const int P = TC_QT * TC_M / G;  // positions per CTA
-  dim3 grid((a->nq + P - 1) / P, a->hkv);
+  dim3 grid(a->hkv, (a->nq + P - 1) / P);
   switch (G) {
 #define NKV_TC_CASE(GG)                                                                \
   case GG:                                                                             \
