@@ -406,6 +406,14 @@ int nkv_add_rms_norm(nkv_stream_t stream, const void* x, void* residual, const v
  * (fp32).  Replaces SiluAndMul (nanovllm/layers/activation.py:6-11). */
 int nkv_silu_mul(nkv_stream_t stream, const void* gate_up, void* out, int T, int I);
 
+/* y[r][n] = bf16(sum_k x[r][k] * w[n][k]) for rows = 1..4 rows of x (fp32
+ * accumulation): the decode-time projections and LM head of one or a few
+ * tokens, weights [N][K] row-major (K a multiple of 8, rows 16-byte aligned),
+ * streamed from HBM once.  Replaces the M = 1 linear layers
+ * (nanovllm/layers/linear.py, embed_head.py) during decode. */
+int nkv_gemv_bf16(nkv_stream_t stream, const void* x, long long x_row_stride, int rows, const void* w,
+                  long long w_row_stride, int N, int K, void* y, long long y_row_stride);
+
 #ifdef __cplusplus
 }
 #endif

@@ -125,6 +125,7 @@ SIGNATURES = {
                                  C.c_longlong, C.c_float, c_vp]),
     "nkv_add_rms_norm": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, C.c_float, c_int]),
     "nkv_silu_mul": (c_int, [c_vp, c_vp, c_vp, c_int, c_int]),
+    "nkv_gemv_bf16": (c_int, [c_vp, c_vp, c_i64, c_int, c_vp, c_i64, c_int, c_int, c_vp, c_i64]),
 }
 
 _lib = None

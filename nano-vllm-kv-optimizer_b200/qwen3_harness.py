@@ -7,7 +7,9 @@ The reference runs its sparse path inside ``nanovllm/models/qwen3.py``
 installed by ``ModelRunner.allocate_kv_cache`` (``nanovllm/engine/model_runner.py:134-185``).
 This module is that caller, built for B200:
 
-* the dense projections are cuBLAS GEMMs (``torch.nn.functional.linear``);
+* the dense projections are cuBLAS GEMMs (``torch.nn.functional.linear``)
+  for chunks, and this package's weight-streaming GEMV (``nkv_gemv_bf16``) for
+  one to four tokens (decode);
 * the elementwise work around them is this package's kernels: residual add +
   RMSNorm (``nkv_add_rms_norm``), the per-head q/k RMSNorm fused with the YaRN
   rotary embedding in place on the qkv projection output (``nkv_qk_norm_rope``,
@@ -154,6 +156,7 @@ class Qwen3SparseModel:
         self.record_ids = False
         self.record = {"prefill": [[] for _ in self.layers], "decode": [[] for _ in self.layers]}
         self.decode_queries = None  # set by DecodeLoop(record_ids=True) while it records
+        self.use_gemv = True  # decode-time projections on nkv_gemv_bf16 (cuBLAS when False)
 
     @property
     def runtimes(self):
@@ -172,6 +175,18 @@ class Qwen3SparseModel:
         call("nkv_qk_norm_rope", _stream(self.device), qkv.data_ptr(), qkv.stride(0), qkv.shape[0], a.num_heads,
              a.num_kv_heads, a.head_dim, L.q_norm.data_ptr(), L.k_norm.data_ptr(), self.cos_sin.data_ptr(),
              positions.data_ptr(), self.cos_sin.shape[0], a.rms_norm_eps, self.err.data_ptr())
+
+    def _linear(self, x, w):
+        """x [T, K] @ w[N, K]^T: the library's weight-streaming GEMV for up to 4
+        rows (decode), cuBLAS through torch otherwise."""
+        T = x.shape[0]
+        if T > 4 or not self.use_gemv or x.stride(-1) != 1:
+            return F.linear(x, w)
+        N, K = w.shape
+        y = torch.empty(T, N, dtype=torch.bfloat16, device=self.device)
+        call("nkv_gemv_bf16", _stream(self.device), x.data_ptr(), x.stride(0), T, w.data_ptr(), w.stride(0), N, K,
+             y.data_ptr(), y.stride(0))
+        return y
 
     def _silu_mul(self, gu):
         T = gu.shape[0]
@@ -194,7 +209,7 @@ class Qwen3SparseModel:
         xn = torch.empty_like(h)
         for i, L in enumerate(self.layers):
             self._norm(h, residual, L.w_in, xn, has_residual=i > 0)
-            qkv = F.linear(xn, L.wqkv)
+            qkv = self._linear(xn, L.wqkv)
             self._qk_norm_rope(qkv, positions, L)
             q = qkv[:, :self.q_size].view(T, a.num_heads, a.head_dim)
             k = qkv[:, self.q_size:self.q_size + self.kv_size].view(T, a.num_kv_heads, a.head_dim)
@@ -204,9 +219,9 @@ class Qwen3SparseModel:
                 self.decode_queries[i] = q
             if self.record_ids and mode != "verify" and (mode == "decode" or L.rt.prefill_len > T):
                 self.record[mode][i].append(L.rt.last_block_ids.clone().cpu())
-            h = F.linear(o.reshape(T, self.q_size), L.wo)
+            h = self._linear(o.reshape(T, self.q_size), L.wo)
             self._norm(h, residual, L.w_post, xn, has_residual=True)
-            h = F.linear(self._silu_mul(F.linear(xn, L.wgu)), L.wd)
+            h = self._linear(self._silu_mul(self._linear(xn, L.wgu)), L.wd)
         if last_only:
             h, residual = h[-1:].contiguous(), residual[-1:].contiguous()
         out = torch.empty_like(h)
@@ -228,7 +243,7 @@ class Qwen3SparseModel:
         return rt.decode(q, k, v, q.device)
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
-        return F.linear(hidden, self.embed)
+        return self._linear(hidden, self.embed)
 
     # ------------------------------------------------------------------
     # generation

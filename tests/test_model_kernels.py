@@ -114,3 +114,23 @@ def test_silu_mul_matches_reference_math():
     nkv._lib.call("nkv_silu_mul", torch.cuda.current_stream().cuda_stream, gu.data_ptr(), out.data_ptr(), T, I)
     torch.cuda.synchronize()
     _check(out, want)
+
+
+@pytest.mark.parametrize("rows,N,K", [(1, 6144, 2560), (1, 2560, 9728), (2, 2560, 4096), (4, 1000, 2560),
+                                      (1, 151936, 2560), (3, 77, 136)])
+def test_gemv_matches_fp32(rows, N, K):
+    """nkv_gemv_bf16 against the fp32 product of the same bf16 operands,
+    rounded to bf16 (the kernel sums in fp32 in its own order: each output
+    within one bf16 step of the fp32 reference, or 1e-3 absolute)."""
+    nkv = pkg()
+    g = torch.Generator(device=DEV).manual_seed(N + K + rows)
+    x = torch.randn(rows, K, generator=g, device=DEV).bfloat16()
+    w = (torch.randn(N, K, generator=g, device=DEV) * 0.05).bfloat16()
+    y = torch.empty(rows, N, dtype=torch.bfloat16, device=DEV)
+    nkv._lib.call("nkv_gemv_bf16", torch.cuda.current_stream().cuda_stream, x.data_ptr(), x.stride(0), rows,
+                  w.data_ptr(), w.stride(0), N, K, y.data_ptr(), y.stride(0))
+    torch.cuda.synchronize()
+    want = x.float() @ w.float().T
+    err = (y.float() - want).abs()
+    tol = torch.maximum(want.abs() * 2.0 ** -7, torch.full_like(want, 1e-3))
+    assert bool((err <= tol).all()), float((err - tol).max())
