@@ -19,6 +19,7 @@ from .m12_runtime import (
 from .decode_graph import DecodeGraph, DeviceRingHeads
 from .qwen3_harness import DecodeLoop, Qwen3Arch, Qwen3SparseModel
 from .proposers import DraftArch, DraftModelProposer, NgramProposer, StaticDraftModel
+from .segmented_prefill import SegmentedPrefillAdapter
 from .sharded import KVHeadShardedLayer
 
 __all__ = [
@@ -33,6 +34,7 @@ __all__ = [
     "NgramProposer",
     "Qwen3Arch",
     "Qwen3SparseModel",
+    "SegmentedPrefillAdapter",
     "StaticDraftModel",
     "dynamic_top_k_from_scores",
     "prefill_query_summaries",
