@@ -408,9 +408,10 @@ def store_measure(nkv, dev, iters=16):
 
 # the full model decoding after a 32K prompt
 MODEL_PROMPT, MODEL_CHUNK = 32768, 4096
+C5_PROMPT, C5_STEPS = 131072, 256  # BASELINE config 5 (long context)
 
 
-def model_measure(nkv, dev, steps=64, warmup=8, layer_us=None):
+def model_measure(nkv, dev, steps=64, warmup=8, layer_us=None, prompt_len=None, speculative=True, seed=2):
     """Random-init Qwen3-4B-architecture model (36 layers) with the sparse
     runtime in every layer: a 32768-token prompt prefilled in 4096-token chunks
     (time to first token), then greedy decode replayed from one CUDA graph per
@@ -419,9 +420,10 @@ def model_measure(nkv, dev, steps=64, warmup=8, layer_us=None):
     norm, LM head, argmax, token fed back on the device)."""
     H = nkv.qwen3_harness
     arch = H.Qwen3Arch()
-    prompt = torch.randint(0, arch.vocab_size, (MODEL_PROMPT,), generator=torch.Generator().manual_seed(2))
+    n_prompt = prompt_len or MODEL_PROMPT
+    prompt = torch.randint(0, arch.vocab_size, (n_prompt,), generator=torch.Generator().manual_seed(seed))
     model = H.Qwen3SparseModel(arch, lambda i: nkv.M12LayerRuntime(
-        i, nkv.M12Config(max_model_len=MODEL_PROMPT + 4096, device=dev)), device=dev, seed=0)
+        i, nkv.M12Config(max_model_len=n_prompt + 4096, device=dev)), device=dev, seed=0)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     e0.record()
@@ -449,7 +451,7 @@ def model_measure(nkv, dev, steps=64, warmup=8, layer_us=None):
     # acceptance: the upper bound of a drafter), shared and per-query selection
     spec = {}
     cur = int(toks[-1])
-    for lossless in (False, True):
+    for lossless in ((False, True) if speculative else ()):
         for rt in model.runtimes:
             rt.verify_lossless = lossless
         times = []
@@ -472,14 +474,15 @@ def model_measure(nkv, dev, steps=64, warmup=8, layer_us=None):
     model.check_errors()
     del loop, model
     torch.cuda.empty_cache()
-    rec = {"workload": "Qwen3-4B architecture (36 layers, random init bf16), 32768-token prompt in 4096-token "
-                       "chunks, greedy decode from one CUDA graph per token",
+    rec = {"workload": f"Qwen3-4B architecture (36 layers, random init bf16), {n_prompt}-token prompt in "
+                       f"{MODEL_CHUNK}-token chunks, greedy decode from one CUDA graph per token",
            "decode_tok_s": round(1000.0 / ms, 1), "decode_ms_per_token": round(ms, 4),
            "prefill_ttft_ms": round(ttft_ms, 1), "decode_steps_timed": steps,
-           "first_tokens": toks[:8],
-           "speculative_verify": dict(spec, note="eager verify pass over [current, 4 drafts] through the 36 "
-                                                 "layers + commit of all 5 tokens, median of 8 rounds; tok/s "
-                                                 "at 100 % acceptance is the ceiling a drafter could reach")}
+           "first_tokens": toks[:8]}
+    if speculative:
+        rec["speculative_verify"] = dict(spec, note="eager verify pass over [current, 4 drafts] through the 36 "
+                                                    "layers + commit of all 5 tokens, median of 8 rounds; tok/s "
+                                                    "at 100 % acceptance is the ceiling a drafter could reach")
     if layer_us is not None:
         rec["sparse_attention_share"] = round(layer_us * arch.num_layers / (ms * 1000.0), 3)
     return rec
@@ -648,6 +651,7 @@ def main():
     ap.add_argument("--model-only", action="store_true",
                     help="run only the full-model decode measurement and print its record (profiling)")
     ap.add_argument("--no-model", action="store_true", help="skip the full-model decode tok/s measurement")
+    ap.add_argument("--no-c5", action="store_true", help="skip the 131072-token full-model measurement (N = 1)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -698,7 +702,12 @@ def main():
         print(json.dumps({"offload": offload_measure(nkv, torch.device("cuda", 0))}))
         return
     if args.model_only:
-        print(json.dumps({"model": model_measure(nkv, torch.device("cuda", 0))}))
+        dev0 = torch.device("cuda", 0)
+        rec = {"model": model_measure(nkv, dev0)}
+        if not args.no_c5:
+            rec["model_c5"] = model_measure(nkv, dev0, steps=C5_STEPS, warmup=8, prompt_len=C5_PROMPT,
+                                            speculative=False)
+        print(json.dumps(rec))
         return
     if world > 1:
         import torch.distributed as dist
@@ -870,14 +879,33 @@ def main():
     if rank == 0 and not args.no_offload:
         offload = offload_measure(nkv, dev)
     store = store_measure(nkv, dev) if rank == 0 else None
-    model = None
-    if rank == 0 and not args.no_model:
+    model = model_c5 = None
+    if not args.no_model:
         del graph, g_att, dg
         graph = g_att = dg = None
         for rt in layers:
             rt.reset()
         torch.cuda.empty_cache()
-        model = model_measure(nkv, dev, layer_us=value * world)
+        if world == 1:
+            model = model_measure(nkv, dev, layer_us=value * world)
+            if not args.no_c5:
+                # BASELINE config 5 on one GPU: a 131072-token prompt, 256 greedy steps
+                model_c5 = model_measure(nkv, dev, steps=C5_STEPS, warmup=8, prompt_len=C5_PROMPT,
+                                         speculative=False)
+        else:
+            # config 5's throughput variant: one independent 32K sequence per GPU
+            # (a different prompt on every rank), whole-job tok/s over the
+            # slowest rank's time per token
+            rec = model_measure(nkv, dev, speculative=False, seed=2 + rank)
+            t = torch.tensor([rec["decode_ms_per_token"], rec["prefill_ttft_ms"]], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            if rank == 0:
+                ms_tok, ttft = float(t[0].item()), float(t[1].item())
+                model = dict(rec, workload=f"{world} independent sequences, one per GPU: " + rec["workload"],
+                             decode_ms_per_token=round(ms_tok, 4), prefill_ttft_ms=round(ttft, 1),
+                             decode_tok_s=round(world * 1000.0 / ms_tok, 1),
+                             decode_tok_s_per_gpu=round(1000.0 / ms_tok, 1), replicas=world,
+                             timing="max over ranks")
     if rank == 0:
         # the CPU baseline is timed at N = 1 only (with N > 1 other ranks share the host)
         own = port = None
@@ -922,6 +950,7 @@ def main():
             "store": store,
             "kv_head_sharded": sharded,
             "model": model,
+            "model_c5": model_c5,
         }
         print(json.dumps(line))
     del graph, g_att, dg
