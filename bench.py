@@ -652,6 +652,7 @@ def main():
                     help="run only the full-model decode measurement and print its record (profiling)")
     ap.add_argument("--no-model", action="store_true", help="skip the full-model decode tok/s measurement")
     ap.add_argument("--no-c5", action="store_true", help="skip the 131072-token full-model measurement (N = 1)")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (cpu_baseline is then null)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -909,7 +910,7 @@ def main():
     if rank == 0:
         # the CPU baseline is timed at N = 1 only (with N > 1 other ranks share the host)
         own = port = None
-        if world == 1:
+        if world == 1 and not args.no_cpu:
             own = reference_own(args.cpu_steps, 3, threads)
             port = cpu_reference(args.cpu_steps, 3, threads)
         line = {
