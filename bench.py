@@ -409,9 +409,14 @@ def store_measure(nkv, dev, iters=16):
 # the full model decoding after a 32K prompt
 MODEL_PROMPT, MODEL_CHUNK = 32768, 4096
 C5_PROMPT, C5_STEPS = 131072, 256  # BASELINE config 5 (long context)
+C3_STEPS = 128  # int8 history (per-token bf16 scales) in pinned host memory
+C3_M12 = {"quant_history": True, "quant_scheme": "token", "kv_residency": "host"}
+C3_LABEL = ("history int8 with per-token per-KV-head bf16 scales in pinned host memory; each decode step "
+            "reads the selected blocks over the host link")
 
 
-def model_measure(nkv, dev, steps=64, warmup=8, layer_us=None, prompt_len=None, speculative=True, seed=2):
+def model_measure(nkv, dev, steps=64, warmup=8, layer_us=None, prompt_len=None, speculative=True, seed=2,
+                  m12=None, label=None):
     """Random-init Qwen3-4B-architecture model (36 layers) with the sparse
     runtime in every layer: a 32768-token prompt prefilled in 4096-token chunks
     (time to first token), then greedy decode replayed from one CUDA graph per
@@ -423,7 +428,13 @@ def model_measure(nkv, dev, steps=64, warmup=8, layer_us=None, prompt_len=None, 
     n_prompt = prompt_len or MODEL_PROMPT
     prompt = torch.randint(0, arch.vocab_size, (n_prompt,), generator=torch.Generator().manual_seed(seed))
     model = H.Qwen3SparseModel(arch, lambda i: nkv.M12LayerRuntime(
-        i, nkv.M12Config(max_model_len=n_prompt + 4096, device=dev)), device=dev, seed=0)
+        i, nkv.M12Config(max_model_len=n_prompt + 4096, device=dev, **(m12 or {}))), device=dev, seed=0)
+    # the history store reserved for the prompt before the timed prefill (the
+    # reference's one-shot reserve_blocks), as a server does at setup: for the
+    # host-resident history this is the pinned allocation, which would
+    # otherwise grow by doubling inside the prefill
+    for rt in model.runtimes:
+        rt.reserve_blocks(-(-n_prompt // B))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     e0.record()
@@ -475,7 +486,8 @@ def model_measure(nkv, dev, steps=64, warmup=8, layer_us=None, prompt_len=None, 
     del loop, model
     torch.cuda.empty_cache()
     rec = {"workload": f"Qwen3-4B architecture (36 layers, random init bf16), {n_prompt}-token prompt in "
-                       f"{MODEL_CHUNK}-token chunks, greedy decode from one CUDA graph per token",
+                       f"{MODEL_CHUNK}-token chunks, greedy decode from one CUDA graph per token"
+                       + (f"; {label}" if label else ""),
            "decode_tok_s": round(1000.0 / ms, 1), "decode_ms_per_token": round(ms, 4),
            "prefill_ttft_ms": round(ttft_ms, 1), "decode_steps_timed": steps,
            "first_tokens": toks[:8]}
@@ -705,6 +717,8 @@ def main():
     if args.model_only:
         dev0 = torch.device("cuda", 0)
         rec = {"model": model_measure(nkv, dev0)}
+        rec["model_c3"] = model_measure(nkv, dev0, steps=C3_STEPS, warmup=8, speculative=False, m12=C3_M12,
+                                        label=C3_LABEL)
         if not args.no_c5:
             rec["model_c5"] = model_measure(nkv, dev0, steps=C5_STEPS, warmup=8, prompt_len=C5_PROMPT,
                                             speculative=False)
@@ -880,7 +894,7 @@ def main():
     if rank == 0 and not args.no_offload:
         offload = offload_measure(nkv, dev)
     store = store_measure(nkv, dev) if rank == 0 else None
-    model = model_c5 = None
+    model = model_c3 = model_c5 = None
     if not args.no_model:
         del graph, g_att, dg
         graph = g_att = dg = None
@@ -889,6 +903,9 @@ def main():
         torch.cuda.empty_cache()
         if world == 1:
             model = model_measure(nkv, dev, layer_us=value * world)
+            # the same model with the int8 history offloaded
+            model_c3 = model_measure(nkv, dev, steps=C3_STEPS, warmup=8, speculative=False, m12=C3_M12,
+                                     label=C3_LABEL)
             if not args.no_c5:
                 # BASELINE config 5 on one GPU: a 131072-token prompt, 256 greedy steps
                 model_c5 = model_measure(nkv, dev, steps=C5_STEPS, warmup=8, prompt_len=C5_PROMPT,
@@ -951,6 +968,7 @@ def main():
             "store": store,
             "kv_head_sharded": sharded,
             "model": model,
+            "model_c3": model_c3,
             "model_c5": model_c5,
         }
         print(json.dumps(line))

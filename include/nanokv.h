@@ -306,6 +306,19 @@ int nkv_shard_attend(nkv_stream_t stream, const nkv_attend_args* args, void* con
 size_t nkv_prefill_workspace_bytes(int hkv, int hq, int nq, int max_tokens);
 int nkv_prefill(nkv_stream_t stream, const nkv_attend_args* args);
 
+/* The selected blocks of a prefill call (args->block_ids[0, n_sel) of the block
+ * store args->k_store / v_store, any store_kind, in device or mapped pinned host
+ * memory) copied into a device bf16 staging store k_out / v_out laid out as
+ * [n_sel][hkv][block_size][head_dim] (staging block i = history block ids[i]),
+ * int8 kinds dequantised with the attention kernels' rounding (bf16 of the fp32
+ * product).  Passing the staging store with block ids 0 .. n_sel - 1 and
+ * store_kind NKV_STORE_BF16 to nkv_prefill then runs the tensor-core kernel,
+ * and each selected block crosses the host link once per call.  The error word
+ * goes to args->workspace.  Replaces the reference's staging of the selected
+ * blocks for the packed prefill (m12_runtime.py:560-586) and the dequant pack
+ * of the int8 history (:1243-1267, fused_dequant.py:47-63). */
+int nkv_prefill_gather(nkv_stream_t stream, const nkv_attend_args* args, void* k_out, void* v_out);
+
 /* ------------------------------------------------------------------------ */
 /* (5) KV store + representative refresh for one prefill chunk.
  *

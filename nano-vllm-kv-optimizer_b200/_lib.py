@@ -114,6 +114,7 @@ SIGNATURES = {
     "nkv_shard_attend": (c_int, [c_vp, C.POINTER(AttendArgs), c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp]),
     "nkv_prefill_workspace_bytes": (C.c_size_t, [c_int, c_int, c_int, c_int]),
     "nkv_prefill": (c_int, [c_vp, C.POINTER(AttendArgs)]),
+    "nkv_prefill_gather": (c_int, [c_vp, C.POINTER(AttendArgs), c_vp, c_vp]),
     "nkv_store_chunk": (c_int, [c_vp, C.POINTER(StoreArgs)]),
     "nkv_ring_append": (c_int, [c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_int, c_int,
                                 c_vp, c_vp, c_int, c_int]),

@@ -21,6 +21,7 @@
 //           via ldmatrix.trans.  fp32 accumulation throughout.
 // Position tiles are scheduled last-first (they see the most keys).
 #include <stdlib.h>
+#include <string.h>
 
 #include "nkv_common.cuh"
 #include "nkv_host.h"
@@ -321,6 +322,90 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_kernel(const PrefillPar
 }  // namespace nkv
 
 using namespace nkv;
+
+namespace nkv {
+// Selected blocks of one prefill call copied into a device bf16 staging store
+// [n_sel][hkv][B][D] (staging block i = history block ids[i]), dequantised on
+// the way with int8_chunk's rounding.  Grid (n_sel, hkv): one CTA per
+// (block, head) tile, every thread's loads issued before its stores.
+constexpr int GD_THREADS = 256;
+__global__ void __launch_bounds__(GD_THREADS) gather_blocks_kernel(const PrefillParams p, __nv_bfloat16* sk,
+                                                                   __nv_bfloat16* sv) {
+  const int i = blockIdx.x, h = blockIdx.y;
+  const int nchunks = p.B * (NKV_D / 8);
+  const long long dst = ((long long)i * p.hkv + h) * p.B * NKV_D;
+  constexpr int PER = 4;  // chunks per thread and pass (B <= 128: at most two passes)
+  for (int base = threadIdx.x; base < nchunks; base += GD_THREADS * PER) {
+    uint4 kw[PER], vw[PER];
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int ch = base + u * GD_THREADS;
+      if (ch >= nchunks) continue;
+      const int row = ch >> 4, c = ch & 15;
+      const int key = i * p.B + row;
+      if (p.kind == NKV_STORE_BF16) {
+        long long id = __ldg(p.ids + i);
+        if (id < 0 || id >= p.max_blocks) {
+          if (p.err) atomicExch(p.err, ERR_BAD_INDEX);
+          id = 0;
+        }
+        const long long o = ((id * p.hkv + h) * p.B + row) * NKV_D + c * 8;
+        kw[u] = __ldg(reinterpret_cast<const uint4*>(p.k_store + o));
+        vw[u] = __ldg(reinterpret_cast<const uint4*>(p.v_store + o));
+      } else {
+        int8_chunk(p, h, key, c, &kw[u], &vw[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int ch = base + u * GD_THREADS;
+      if (ch >= nchunks) continue;
+      *reinterpret_cast<uint4*>(sk + dst + (long long)ch * 8) = kw[u];
+      *reinterpret_cast<uint4*>(sv + dst + (long long)ch * 8) = vw[u];
+    }
+  }
+}
+}  // namespace nkv
+
+extern "C" int nkv_prefill_gather(nkv_stream_t stream, const nkv_attend_args* a, void* k_out, void* v_out) {
+  NKV_REQUIRE(a && k_out && v_out, "prefill_gather: null arguments");
+  NKV_SUPPORTED(a->head_dim == NKV_D, "prefill_gather: head_dim %d unsupported (128 only)", a->head_dim);
+  NKV_REQUIRE(a->store_kind >= 0 && a->store_kind <= 2, "prefill_gather: bad store_kind");
+  NKV_REQUIRE(a->n_sel >= 1 && a->block_ids && a->k_store && a->v_store && a->max_blocks > 0 && a->hkv >= 1,
+              "prefill_gather: needs selected blocks, their ids and the block store");
+  NKV_SUPPORTED((a->block_size & (a->block_size - 1)) == 0 && a->block_size >= 16 && a->block_size <= 128,
+                "prefill_gather: block_size %d unsupported (16, 32, 64 or 128)", a->block_size);
+  NKV_REQUIRE(a->store_kind != NKV_STORE_INT8_REF || (a->k_chan_scale && a->v_block_scale),
+              "prefill_gather: int8 reference scheme needs its scales");
+  NKV_REQUIRE(a->store_kind != NKV_STORE_INT8_TOKEN || (a->k_tok_scale && a->v_tok_scale),
+              "prefill_gather: int8 token scheme needs its scales");
+  NKV_REQUIRE(((uintptr_t)a->k_store & 15) == 0 && ((uintptr_t)a->v_store & 15) == 0 &&
+                  ((uintptr_t)k_out & 15) == 0 && ((uintptr_t)v_out & 15) == 0,
+              "prefill_gather: stores must be 16-byte aligned");
+  NKV_REQUIRE(a->workspace && a->workspace_bytes >= 256, "prefill_gather: workspace (error word) missing");
+  PrefillParams p;
+  memset(&p, 0, sizeof(p));
+  p.hkv = a->hkv;
+  p.B = a->block_size;
+  p.log2B = 0;
+  while ((1 << p.log2B) < a->block_size) ++p.log2B;
+  p.ids = (const long long*)a->block_ids;
+  p.n_sel = a->n_sel;
+  p.max_blocks = a->max_blocks;
+  p.kind = a->store_kind;
+  p.k_store = (const __nv_bfloat16*)a->k_store;
+  p.v_store = (const __nv_bfloat16*)a->v_store;
+  p.k_q = (const signed char*)a->k_store;
+  p.v_q = (const signed char*)a->v_store;
+  p.kcs = a->k_chan_scale;
+  p.vbs = a->v_block_scale;
+  p.kts = (const __nv_bfloat16*)a->k_tok_scale;
+  p.vts = (const __nv_bfloat16*)a->v_tok_scale;
+  p.err = (int*)a->workspace;
+  gather_blocks_kernel<<<dim3(a->n_sel, a->hkv), GD_THREADS, 0, (cudaStream_t)stream>>>(
+      p, (__nv_bfloat16*)k_out, (__nv_bfloat16*)v_out);
+  return check_launch("prefill_gather");
+}
 
 extern "C" size_t nkv_prefill_workspace_bytes(int hkv, int hq, int nq, int max_tokens) {
   (void)hkv;

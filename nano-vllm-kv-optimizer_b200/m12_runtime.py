@@ -293,6 +293,11 @@ class M12LayerRuntime:
         self._allowed = torch.zeros(8, 8 * cfg.top_k_blocks, dtype=torch.uint8, **kw)
         self._prot_key = None
         self._dargs, self._dkey, self._ids_view = None, None, None
+        # prefill over int8 or host-resident history: the selected blocks are
+        # staged in device bf16 once per call (nkv_prefill_gather) and attended
+        # on the tensor-core kernel; False attends them in place
+        self.prefill_gather = True
+        self._stage = None
         self._bscores = None
         self._lib_h = _lib.load()
         # nkv_decode_step taking the argument struct's address (no ctypes byref per call)
@@ -744,8 +749,30 @@ class M12LayerRuntime:
         ws = self._attend_ws(nq, ntok, prefill)
         a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
         a.overlap_select = 1 if after_select else 0
-        call("nkv_prefill" if prefill else "nkv_attend", _stream(self.device), C.byref(a))
+        stream = _stream(self.device)
+        if prefill and n_sel > 0 and allowed is None and self.prefill_gather and (
+                self.store_kind != _lib.STORE_BF16 or cfg.kv_residency == "host"):
+            # int8 or host-resident history: the selected blocks are copied once
+            # into a device bf16 staging store (dequantised on the way) and the
+            # chunk attends to that on the tensor-core kernel
+            sk, sv, sids = self._prefill_staging(n_sel)
+            call("nkv_prefill_gather", stream, C.byref(a), sk.data_ptr(), sv.data_ptr())
+            a.k_store, a.v_store, a.store_kind = sk.data_ptr(), sv.data_ptr(), _lib.STORE_BF16
+            a.block_ids, a.max_blocks = sids.data_ptr(), n_sel
+            a.k_chan_scale = a.v_block_scale = a.k_tok_scale = a.v_tok_scale = 0
+        call("nkv_prefill" if prefill else "nkv_attend", stream, C.byref(a))
         return out
+
+    def _prefill_staging(self, n_sel: int):
+        """Device bf16 staging store [n_sel][Hkv][B][D] for the selected blocks
+        of a prefill call, and the ids 0 .. n_sel - 1 that address it."""
+        cfg = self.cfg
+        if self._stage is None or self._stage[0].shape[0] < n_sel:
+            shape = (n_sel, cfg.num_kv_heads, cfg.block_size, cfg.head_dim)
+            self._stage = (torch.empty(shape, dtype=torch.bfloat16, device=self.device),
+                           torch.empty(shape, dtype=torch.bfloat16, device=self.device),
+                           torch.arange(n_sel, dtype=torch.int64, device=self.device))
+        return self._stage
 
     # ------------------------------------------------------------------
     # prefill

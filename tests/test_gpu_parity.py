@@ -425,6 +425,41 @@ def test_int8_history_decode(scheme, residency):
         _close(got, want)
 
 
+@pytest.mark.parametrize("quant,scheme,residency", [(True, "reference", "hbm"), (True, "token", "host"),
+                                                   (False, "reference", "host")])
+def test_prefill_chunk_over_staged_history(quant, scheme, residency):
+    """A later prefill chunk over int8 or host-resident history: the selected
+    blocks staged in device bf16 (nkv_prefill_gather) and attended on the
+    tensor-core kernel, against the oracle's dequantised attention and against
+    the in-place form (the selected blocks read where they lie)."""
+    nkv = pkg()
+    outs = []
+    for staged in (True, False):
+        g = torch.Generator().manual_seed(77)
+        rt = nkv.M12LayerRuntime(0, _cfg(quant_history=quant, quant_scheme=scheme, kv_residency=residency,
+                                         top_k_blocks=16))
+        rt.prefill_gather = staged
+        _, k, v = qkv(g, 4096)
+        rt.prefill_first(k.new_zeros(1), k.to(DEV), v.to(DEV))
+        layer = orc.OracleLayer(orc.OracleConfig(top_k_blocks=16, quant_history=quant and scheme == "reference"))
+        layer.store(k, v)
+        if quant and scheme == "token":  # the per-token dequantised history replaces the oracle's blocks
+            kq, ks = orc.quant_token_head(k)
+            vq, vs = orc.quant_token_head(v)
+            layer.k_hist = list((kq.float() * ks.float()[..., None]).bfloat16().view(64, 64, 8, 128))
+            layer.v_hist = list((vq.float() * vs.float()[..., None]).bfloat16().view(64, 64, 8, 128))
+        layer.prefill_len = rt.prefill_len
+        q, kc, vc = qkv(g, 1024)
+        got = rt.prefill_chunk(q.to(DEV), kc.to(DEV), vc.to(DEV), DEV)
+        layer.force_ids = rt.last_prefill_block_ids.cpu()
+        want = layer.prefill_chunk(q, kc, vc)
+        assert rt.last_prefill_block_ids.numel() == 16
+        _close(got, want)
+        outs.append((rt.last_prefill_block_ids.cpu(), got.float().cpu()))
+    assert torch.equal(outs[0][0], outs[1][0])
+    torch.testing.assert_close(outs[0][1], outs[1][1], atol=ATOL, rtol=RTOL)
+
+
 def test_offload_bf16_host_history():
     nkv = pkg()
     g = torch.Generator().manual_seed(5)
