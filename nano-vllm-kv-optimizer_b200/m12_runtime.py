@@ -351,7 +351,7 @@ class M12LayerRuntime:
         self.q_history: list[torch.Tensor] = []
         self._pending_k = None
         self._pending_v = None
-        self.last_verify_block_ids: torch.Tensor | None = None
+        self._last_verify_dev = self._last_verify_host = None
         self.last_verify_timings: dict = {}
         self.verify_mode = False
         self.verify_lossless = False
@@ -408,6 +408,20 @@ class M12LayerRuntime:
     def _set_last_ids(self, ids_dev):
         self._last_ids_dev = ids_dev
         self._last_ids_host = None
+
+    @property
+    def last_verify_block_ids(self):
+        """The blocks the last verify pass attended (host int64), copied from
+        the device when first read, so that a verify pass does not wait for
+        the device."""
+        if self._last_verify_host is None and self._last_verify_dev is not None:
+            self._last_verify_host = self._last_verify_dev.cpu()
+        return self._last_verify_host
+
+    @last_verify_block_ids.setter
+    def last_verify_block_ids(self, value):
+        self._last_verify_dev = None
+        self._last_verify_host = value
 
     # ------------------------------------------------------------------
     # lifecycle
@@ -853,7 +867,7 @@ class M12LayerRuntime:
         self._pending_k = k
         self._pending_v = v
         self._set_last_ids(ids)
-        self.last_verify_block_ids = ids.cpu()
+        self._last_verify_dev, self._last_verify_host = ids.clone(), None
         return o
 
     def commit_verified(self, n: int) -> None:
