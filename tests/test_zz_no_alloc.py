@@ -4,7 +4,9 @@
 Both run the same kernels on the same arguments; the outputs must agree within
 the GPU parity tolerance (max-abs 2e-2 / rel 1e-2) on two calls in a row, for
 the single-query decode kernel with either split merge and for the multi-query
-kernel.  A call whose workspace would not fit the scratch is refused, and an
+kernel, and the scratch form's output agrees with the fp32 oracle's attention
+over the same keys (selected blocks, sink, ring slice, current tokens).  A call
+whose workspace would not fit the scratch is refused, and an
 error the kernels record in the scratch (here: a block id outside the store,
 which the kernels' bounds check replaces by block 0 and reports) is readable
 through nkv_attend_static_check.
@@ -15,7 +17,7 @@ import os
 import pytest
 import torch
 
-from helpers import pkg
+from helpers import orc, pkg
 
 pytestmark = pytest.mark.gpu
 
@@ -142,3 +144,25 @@ def test_static_scratch_error_word_is_readable():
     got = _static(nkv, args, ref)
     assert lib.nkv_attend_static_check(stream) == 0
     torch.testing.assert_close(got.float().cpu(), ref.float().cpu(), atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("nq", [1, 3])
+def test_static_scratch_matches_oracle(nq):
+    """The scratch form against the CPU oracle directly: the keys the call
+    attends (its selected blocks read back from the block store, the sink, the
+    ring slice and the current tokens, causal among themselves) packed in the
+    reference's order and attended in fp32."""
+    nkv = pkg()
+    rt = _layer(nkv, 8)
+    ref, args, (q, kc, vc, ids) = _attend_args(nkv, rt, nq, 14)
+    for _ in range(2):
+        got = _static(nkv, args, ref)
+        torch.cuda.synchronize()
+    hist_k = rt.k_cpu[ids.cpu()].reshape(-1, 8, 128).cpu()     # [n_sel * 64, Hkv, D]
+    hist_v = rt.v_cpu[ids.cpu()].reshape(-1, 8, 128).cpu()
+    ring_k = rt._ring_k.permute(1, 0, 2)[:300].cpu()           # physical slots [0, 300)
+    ring_v = rt._ring_v.permute(1, 0, 2)[:300].cpu()
+    kp = torch.cat([hist_k, rt._sink_k.permute(1, 0, 2)[:64].cpu(), ring_k, kc.cpu()])
+    vp = torch.cat([hist_v, rt._sink_v.permute(1, 0, 2)[:64].cpu(), ring_v, vc.cpu()])
+    want = orc.attention(q.cpu(), kp, vp, rt.cfg.scale, causal_from=kp.shape[0] - nq)
+    torch.testing.assert_close(got.float().cpu(), want, atol=ATOL, rtol=RTOL)
