@@ -238,6 +238,86 @@ __global__ void __launch_bounds__(GV_WARPS * 32) gemv_kernel(const __nv_bfloat16
   }
 }
 
+// The same product with each weight row split over a whole CTA: CTA b takes
+// rows [b * RPC, (b + 1) * RPC) and thread t the 16-byte chunks t, t + 256, ...
+// (CH of them) of every one of those rows and of every x row, so a warp reads
+// 512 contiguous bytes of a row and every load of the CTA is issued before the
+// first product: one DRAM round trip per CTA, RPC x CH loads in flight per
+// thread, x read straight into registers (no staging, no barrier before the
+// products).  Sums: per thread in chunk order, a warp shuffle tree, then the 8
+// warps in order.  RPC = 16 / CH keeps 64 registers of weights in flight.
+constexpr int GS_THREADS = 256;
+template <int R, int CH>
+__global__ void __launch_bounds__(GS_THREADS) gemv_split_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
+                                                                const __nv_bfloat16* __restrict__ W, long long ldw,
+                                                                int N, int K, __nv_bfloat16* __restrict__ y,
+                                                                long long ldy) {
+  constexpr int RPC = CH >= 16 ? 1 : 16 / CH;
+  constexpr int NW = GS_THREADS / 32;
+  __shared__ float red[NW][R * RPC];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nch = K >> 3;
+  const int n0 = blockIdx.x * RPC;
+  uint4 w[RPC][CH];
+#pragma unroll
+  for (int r = 0; r < RPC; ++r) {
+    const int n = n0 + r;
+#pragma unroll
+    for (int i = 0; i < CH; ++i) {
+      const int c = tid + i * GS_THREADS;
+      w[r][i] = (n < N && c < nch) ? ldg_nc_v4(W + (long long)n * ldw + c * 8) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  uint4 xv[R][CH];
+#pragma unroll
+  for (int q = 0; q < R; ++q)
+#pragma unroll
+    for (int i = 0; i < CH; ++i) {
+      const int c = tid + i * GS_THREADS;
+      xv[q][i] = c < nch ? __ldg(reinterpret_cast<const uint4*>(x + q * ldx + c * 8)) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  float acc[R][RPC];
+#pragma unroll
+  for (int q = 0; q < R; ++q)
+#pragma unroll
+    for (int r = 0; r < RPC; ++r) acc[q][r] = 0.f;
+#pragma unroll
+  for (int i = 0; i < CH; ++i) {
+#pragma unroll
+    for (int q = 0; q < R; ++q) {
+      float xf[8];
+      unpack8(xv[q][i], xf);
+#pragma unroll
+      for (int r = 0; r < RPC; ++r) {
+        const uint32_t wv[4] = {w[r][i].x, w[r][i].y, w[r][i].z, w[r][i].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          acc[q][r] = fmaf(__uint_as_float(wv[e] << 16), xf[2 * e], acc[q][r]);
+          acc[q][r] = fmaf(__uint_as_float(wv[e] & 0xffff0000u), xf[2 * e + 1], acc[q][r]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < R; ++q)
+#pragma unroll
+    for (int r = 0; r < RPC; ++r) {
+#pragma unroll
+      for (int m = 16; m > 0; m >>= 1) acc[q][r] += __shfl_xor_sync(0xffffffffu, acc[q][r], m);
+      if (lane == 0) red[warp][q * RPC + r] = acc[q][r];
+    }
+  __syncthreads();
+  if (tid < R * RPC) {
+    const int q = tid / RPC, r = tid % RPC, n = n0 + r;
+    float s = 0.f;
+#pragma unroll
+    for (int v = 0; v < NW; ++v) s += red[v][tid];
+    if (n < N) y[q * ldy + n] = __float2bfloat16_rn(s);
+  }
+}
+
 // Launch in plain stream order, or with programmatic dependent launch allowed
 // (NKV_MODEL_PDL=1): every kernel above waits for its predecessor before
 // touching memory, so that form only hides launch latency between the dense
@@ -282,6 +362,30 @@ extern "C" int nkv_gemv_bf16(nkv_stream_t stream, const void* x, long long x_row
   NKV_REQUIRE(smem <= 200 * 1024, "gemv: rows x K too large for the staged x (%zu bytes)", smem);
   NKV_REQUIRE(x_row_stride % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0,
               "gemv: x rows must be 16-byte aligned");
+  const auto* xs_ = reinterpret_cast<const __nv_bfloat16*>(x);
+  const auto* ws_ = reinterpret_cast<const __nv_bfloat16*>(w);
+  auto* ys_ = reinterpret_cast<__nv_bfloat16*>(y);
+  // rows split over a CTA (up to K = 16384) below 64 K rows; one warp per row
+  // above that (the LM head: there staging x once per CTA for many rows pays,
+  // 131 against 136 us at 151936 x 2560) or with NKV_GEMV_SPLIT=0
+  const int nch = K >> 3;
+  const int ch = (nch + GS_THREADS - 1) / GS_THREADS;
+  if (ch <= 8 && N <= 65536 && knob("NKV_GEMV_SPLIT", 1) != 0) {
+    const int chc = ch == 7 ? 8 : ch;
+    const int rpc = 16 / chc;
+    const dim3 g((unsigned)((N + rpc - 1) / rpc));
+#define NKV_GS(RR, CC)                                                                                      \
+  if (rows == RR && chc == CC)                                                                              \
+    return launch_pdl(gemv_split_kernel<RR, CC>, g, dim3(GS_THREADS), 0, (cudaStream_t)stream, "gemv", xs_, \
+                      (long long)x_row_stride, ws_, (long long)w_row_stride, N, K, ys_, (long long)y_row_stride);
+#define NKV_GS_R(RR) NKV_GS(RR, 1) NKV_GS(RR, 2) NKV_GS(RR, 3) NKV_GS(RR, 4) NKV_GS(RR, 5) NKV_GS(RR, 6) NKV_GS(RR, 8)
+    NKV_GS_R(1)
+    NKV_GS_R(2)
+    NKV_GS_R(3)
+    NKV_GS_R(4)
+#undef NKV_GS_R
+#undef NKV_GS
+  }
   // enough CTAs to keep every SM streaming, few enough that each stages x once
   // for many rows
   const long long want = (N + GV_WARPS - 1) / GV_WARPS;
