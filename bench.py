@@ -416,7 +416,7 @@ C3_LABEL = ("history int8 with per-token per-KV-head bf16 scales in pinned host 
 
 
 def model_measure(nkv, dev, steps=64, warmup=8, layer_us=None, prompt_len=None, speculative=True, seed=2,
-                  m12=None, label=None):
+                  m12=None, label=None, profile_replay=False):
     """Random-init Qwen3-4B-architecture model (36 layers) with the sparse
     runtime in every layer: a 32768-token prompt prefilled in 4096-token chunks
     (time to first token), then greedy decode replayed from one CUDA graph per
@@ -454,6 +454,13 @@ def model_measure(nkv, dev, steps=64, warmup=8, layer_us=None, prompt_len=None, 
         e1.record(st)
     e1.synchronize()
     ms = e0.elapsed_time(e1) / steps
+    if profile_replay:  # one more replay inside cudaProfilerStart/Stop (ncu --profile-from-start off)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        with torch.cuda.stream(st):
+            loop.replay()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
     toks = loop.hist[:warmup + steps].tolist()
     model.check_errors()
     loop.close()
@@ -665,6 +672,9 @@ def main():
     ap.add_argument("--no-model", action="store_true", help="skip the full-model decode tok/s measurement")
     ap.add_argument("--no-c5", action="store_true", help="skip the 131072-token full-model measurement (N = 1)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (cpu_baseline is then null)")
+    ap.add_argument("--profile-replay", action="store_true",
+                    help="with --model-only: one extra config-2 decode replay between cudaProfilerStart/Stop")
+    ap.add_argument("--no-c3", action="store_true", help="with --model-only: skip the config-3 record")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -716,9 +726,10 @@ def main():
         return
     if args.model_only:
         dev0 = torch.device("cuda", 0)
-        rec = {"model": model_measure(nkv, dev0)}
-        rec["model_c3"] = model_measure(nkv, dev0, steps=C3_STEPS, warmup=8, speculative=False, m12=C3_M12,
-                                        label=C3_LABEL)
+        rec = {"model": model_measure(nkv, dev0, profile_replay=args.profile_replay)}
+        if not args.no_c3:
+            rec["model_c3"] = model_measure(nkv, dev0, steps=C3_STEPS, warmup=8, speculative=False, m12=C3_M12,
+                                            label=C3_LABEL)
         if not args.no_c5:
             rec["model_c5"] = model_measure(nkv, dev0, steps=C5_STEPS, warmup=8, prompt_len=C5_PROMPT,
                                             speculative=False)
