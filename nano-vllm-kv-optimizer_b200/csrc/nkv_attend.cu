@@ -114,7 +114,6 @@ struct AttendParams {
   const __nv_bfloat16* fs_reps;  // [hkv][fs_reps_blocks][fs_r][D]
   int fs_r, fs_reps_blocks, fs_bpc, fs_nprot;
   int fs_prefetch;  // 1: each CTA starts an L2 prefetch of its representatives at launch
-  int rank_prefetch;  // split decode kernel: 1, L2 prefetch of the likely selected tiles while ranking
   const int* fs_prot;
   unsigned long long* fs_keys;  // [rank_n]: (tag << 32) | orderable score
   unsigned* fs_sync;            // [0] epoch, [1] CTAs done with this launch's keys
@@ -955,16 +954,9 @@ constexpr int FS_CAND_MAX = 256;  // candidates ranked by counting (more: extrac
 // With more than FS_CAND_MAX candidates (flat or tied scores) the top k are
 // extracted one per round (block-wide max of the remaining keys) instead.
 // All threads of the CTA must call; s_sel is valid after the call.
-// Early hook of topk_threshold: called per warp, before the first barrier,
-// with the warp's candidates (block id, ordinal 0-3 within the warp) at or
-// above its 4th largest distinct score, which are likely members of the top k.
-struct NoRankHook {
-  static constexpr bool active = false;
-  __device__ void operator()(int, int, int) const {}
-};
-template <int NW, class Hook = NoRankHook>
+template <int NW>
 __device__ void topk_threshold(const uint32_t (&u)[FS_MAXE], unsigned live, int n, int k, u64* s_sel,
-                               u64* s_cand, unsigned* s_misc, [[maybe_unused]] int* trc, Hook hook = Hook()) {
+                               u64* s_cand, unsigned* s_misc, [[maybe_unused]] int* trc) {
   constexpr int NT = NW * 32;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int E = (n + NT - 1) / NT;
@@ -985,20 +977,6 @@ __device__ void topk_threshold(const uint32_t (&u)[FS_MAXE], unsigned live, int 
     m = __reduce_max_sync(FULL, m);
     prev = m;
     th = m;
-  }
-  if constexpr (Hook::active) {
-    if (more) {  // warp-uniform: the warp has 4 distinct scores
-      unsigned base = 0u;
-#pragma unroll
-      for (int e = 0; e < FS_MAXE; ++e) {
-        if (e >= E) break;  // CTA-uniform
-        const bool cand = ((live >> e) & 1u) && u[e] >= th;
-        const unsigned bal = __ballot_sync(FULL, cand);
-        const unsigned i = base + (unsigned)__popc(bal & ((1u << lane) - 1u));
-        if (cand && i < 4u) hook(warp, (int)i, tid + e * NT);
-        base += (unsigned)__popc(bal);
-      }
-    }
   }
   const bool warp_live = __any_sync(FULL, live != 0u);
   if (lane == 0) s_misc[warp] = !warp_live ? 0xffffffffu : more ? th : 0u;
@@ -1127,9 +1105,9 @@ __device__ void fs_select(const AttendParams& p, uint32_t tag, u64* s_sel, u64* 
 
 // Ranked decode: the top k (<= 32) of the n fp32 block scores written by the
 // scoring grid, into s_sel (topk_threshold).  All threads of the CTA must call.
-template <int NW, class Hook = NoRankHook>
+template <int NW>
 __device__ void rank_topk(const float* __restrict__ scores, int n, int k, u64* s_sel, u64* s_cand,
-                          unsigned* s_misc, int* trc, Hook hook = Hook()) {
+                          unsigned* s_misc, int* trc) {
   constexpr int NT = NW * 32;
   const int tid = threadIdx.x;
   uint32_t u[FS_MAXE];
@@ -1143,7 +1121,7 @@ __device__ void rank_topk(const float* __restrict__ scores, int n, int k, u64* s
       live |= 1u << e;
     }
   }
-  topk_threshold<NW>(u, live, n, k, s_sel, s_cand, s_misc, trc, hook);
+  topk_threshold<NW>(u, live, n, k, s_sel, s_cand, s_misc, trc);
 }
 // rank_topk over the max across ranks of the tagged scores in this rank's
 // exchange buffer: every (rank, block) word of the thread is loaded, then the
@@ -2053,21 +2031,6 @@ __device__ __forceinline__ void ds_chunk(const unsigned char* kt, unsigned char*
   }
 }
 
-// rank hook of the split kernel: candidate c = 4 warp + i of the head goes to
-// CTA c % CL, which prefetches the block's K and V tiles of its head into L2
-struct TilePrefetch {
-  static constexpr bool active = true;
-  const unsigned char* k;
-  const unsigned char* v;
-  int hkv, h, split, cl;
-  __device__ void operator()(int warp, int i, int id) const {
-    if ((warp * 4 + i) % cl != split) return;
-    const size_t off = ((size_t)id * hkv + h) * DS_TILE_BYTES;
-    prefetch_l2_bulk(k + off, DS_TILE_BYTES);
-    prefetch_l2_bulk(v + off, DS_TILE_BYTES);
-  }
-};
-
 template <int CL, bool FUSED>
 __global__ void __launch_bounds__(DS_WARPS * 32, 2) decode_split_kernel(const AttendParams p,
                                                                      const __grid_constant__ DecodeMaps tm) {
@@ -2201,17 +2164,7 @@ __global__ void __launch_bounds__(DS_WARPS * 32, 2) decode_split_kernel(const At
     if (tid == 0) fs_arrive(p);
   } else {
     pdl_wait();  // the scoring grid's scores are complete past this point
-    if (p.rank_prefetch && (p.tma_mask & 1)) {
-      // while the CTAs rank, the tiles of each warp's four best blocks (32
-      // candidates per head, which hold most of the top k) start moving into
-      // L2, two candidates per CTA of the head, so that most selected tiles
-      // are L2 hits by the time they are issued; a prefetch changes no result
-      rank_topk<NW>(p.rank_scores, p.rank_n, p.n_sel, s_sel, s_cand, s_misc, nullptr,
-                    TilePrefetch{static_cast<const unsigned char*>(p.k_store),
-                                 static_cast<const unsigned char*>(p.v_store), p.hkv, h, split, CL});
-    } else {
-      rank_topk<NW>(p.rank_scores, p.rank_n, p.n_sel, s_sel, s_cand, s_misc, nullptr);
-    }
+    rank_topk<NW>(p.rank_scores, p.rank_n, p.n_sel, s_sel, s_cand, s_misc, nullptr);
   }
   if (split == 0 && h == 0 && tid < p.n_sel) {
     p.rank_out[tid] = (long long)key_id(s_sel[tid]);
@@ -2948,7 +2901,6 @@ static int attend_impl(nkv_stream_t stream, const nkv_attend_args* a, const Rank
   p.fs_sync = one_launch ? (unsigned*)((char*)rank->sel_ws + 16) : nullptr;
   p.fs_bpc = 0;
   p.fs_prefetch = env_int("NKV_FS_PREFETCH", 1);
-  p.rank_prefetch = env_int("NKV_RANK_PREFETCH", 1);
   p.xp_P = 0;
   p.xp_scores = nullptr;
   p.xp_sync = nullptr;
