@@ -1124,13 +1124,15 @@ __device__ void rank_topk(const float* __restrict__ scores, int n, int k, u64* s
   topk_threshold<NW>(u, live, n, k, s_sel, s_cand, s_misc, trc);
 }
 // rank_topk over the max across ranks of the tagged scores in this rank's
-// exchange buffer: every (rank, block) word of the thread is loaded, then the
-// ones not yet carrying this step's tag are polled again (bounded, then
+// exchange buffer: every (rank, block) word of the thread is loaded in one
+// pass (all ranks' loads in flight together, one round trip), then only the
+// words not yet carrying this step's tag are polled again (bounded, then
 // ERR_WAIT_TIMEOUT and the stale value).
 template <int NW>
 __device__ void rank_topk_peer(const AttendParams& p, uint32_t ep, u64* s_sel, u64* s_cand, unsigned* s_misc,
                                int* trc) {
   constexpr int NT = NW * 32;
+  static_assert(NKV_MAX_PEERS * FS_MAXE <= 64, "one pending bit per (rank, key) word");
   const int tid = threadIdx.x;
   const uint32_t tag = step_tag(ep);
   const u64* xs = p.xp_scores + (long long)(ep & 1u) * p.xp_P * p.xp_cap;
@@ -1141,23 +1143,34 @@ __device__ void rank_topk_peer(const AttendParams& p, uint32_t ep, u64* s_sel, u
     v[e] = -INFINITY;
     if (tid + e * NT < p.rank_n) live |= 1u << e;
   }
+  u64 pending = 0ull;  // bit r * FS_MAXE + e: word (rank r, key e) still without the tag
   for (int r = 0; r < p.xp_P; ++r) {
-    unsigned pending = live;
-    const long long t0 = clock64();
-    while (pending) {
 #pragma unroll
-      for (int e = 0; e < FS_MAXE; ++e) {
-        if (!((pending >> e) & 1u)) continue;
-        const u64 w = ld_peer_u64(xs + (long long)r * p.xp_cap + tid + e * NT);
-        if ((uint32_t)(w >> 32) == tag) {
-          v[e] = fmaxf(v[e], f32_unorder((uint32_t)w));
-          pending &= ~(1u << e);
-        }
+    for (int e = 0; e < FS_MAXE; ++e) {
+      if (!((live >> e) & 1u)) continue;
+      const u64 w = ld_peer_u64(xs + (long long)r * p.xp_cap + tid + e * NT);
+      if ((uint32_t)(w >> 32) == tag) v[e] = fmaxf(v[e], f32_unorder((uint32_t)w));
+      else pending |= 1ull << (r * FS_MAXE + e);
+    }
+  }
+  const long long t0 = clock64();
+  while (pending) {
+    u64 left = pending;
+    while (left) {
+      const int b = __ffsll((long long)left) - 1;
+      left &= left - 1ull;
+      const int r = b / FS_MAXE, e = b % FS_MAXE;
+      const u64 w = ld_peer_u64(xs + (long long)r * p.xp_cap + tid + e * NT);
+      if ((uint32_t)(w >> 32) == tag) {
+#pragma unroll
+        for (int x = 0; x < FS_MAXE; ++x)  // v[e] with e known only at run time: keep v in registers
+          if (x == e) v[x] = fmaxf(v[x], f32_unorder((uint32_t)w));
+        pending &= ~(1ull << b);
       }
-      if (pending && clock64() - t0 > PEER_WAIT_CYCLES) {
-        if (p.err) atomicExch(p.err, ERR_WAIT_TIMEOUT);
-        break;
-      }
+    }
+    if (pending && clock64() - t0 > PEER_WAIT_CYCLES) {
+      if (p.err) atomicExch(p.err, ERR_WAIT_TIMEOUT);
+      break;
     }
   }
   uint32_t u[FS_MAXE];
