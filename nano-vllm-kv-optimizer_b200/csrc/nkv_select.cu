@@ -644,7 +644,13 @@ __global__ void __launch_bounds__(SC_THREADS) score_kernel_tc(SelectParams p) {
 using namespace nkv;
 
 static int launch_score(cudaStream_t st, SelectParams& p, int G) {
-  const int sms = sm_count();
+  // the blocks are spread over up to 2 CTAs per SM (NKV_SCORE_CPS): at 32K that
+  // still rounds to 4 blocks per CTA (128 CTAs, which sit beside the attention
+  // CTAs); at 128K it halves the rows per CTA to one 32-row unit per warp (one
+  // round trip instead of two): 2.65 -> 2.57 ms per token of the 131072-token
+  // model decode, although the attention CTAs then start after the scoring
+  const int cps = knob("NKV_SCORE_CPS", 2);
+  const int sms = sm_count() * (cps > 1 ? cps : 1);
   const int per = (p.nblocks + sms - 1) / sms;
   p.bpc = (per + SC_UPW - 1) / SC_UPW * SC_UPW;
   const int grid = (p.nblocks + p.bpc - 1) / p.bpc;
