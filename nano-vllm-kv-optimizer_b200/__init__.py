@@ -21,6 +21,7 @@ from .qwen3_harness import DecodeLoop, Qwen3Arch, Qwen3SparseModel
 from .proposers import DraftArch, DraftModelProposer, NgramProposer, StaticDraftModel
 from .segmented_prefill import SegmentedPrefillAdapter
 from .sharded import KVHeadShardedLayer
+from . import torch_ops  # registers torch.ops.nanokv.*
 
 __all__ = [
     "DecodeGraph",
