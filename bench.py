@@ -406,6 +406,43 @@ def store_measure(nkv, dev, iters=16):
                          "frac": round(gbs / peak, 4), "peak_kind": kind}}
 
 
+def verify6_measure(nkv, dev, iters=50):
+    """BASELINE config 4's multi-token variant as an operator: one layer state
+    of 28672 tokens (7 stored 4096-token chunks), then verify_tokens over 6
+    queries (the current token and 5 drafts) followed by rollback_verified, per
+    call (eager, inputs rotating over 8 sets); per-query (lossless: union of
+    the queries' Top-32 and a per-query mask) and shared selection."""
+    g = torch.Generator(device=dev).manual_seed(606)
+    rt = nkv.M12LayerRuntime(0, nkv.M12Config(max_model_len=PF_HIST + 4096, device=dev,
+                                              verify_union_blocks=6 * TOPK))
+    for c in range(PF_HIST // 4096):
+        k = torch.randn(4096, HKV, D, generator=g, device=dev).bfloat16()
+        v = torch.randn(4096, HKV, D, generator=g, device=dev).bfloat16()
+        (rt.prefill_first(None, k, v) if c == 0 else rt._store_kv(k, v))
+    sets = [tuple(torch.randn(6, h, D, generator=g, device=dev).bfloat16() for h in (HQ, HKV, HKV))
+            for _ in range(NSETS)]
+    rec = {"workload": "verify_tokens over 6 queries (current + 5 drafts) after a 28672-token history "
+                       "(Top-32 per query, sink 64, recent 512), then rollback; eager calls"}
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for lossless in (True, False):
+        rt.verify_lossless = lossless
+        for i in range(5):
+            rt.verify_tokens(*sets[i % NSETS], dev)
+            rt.rollback_verified()
+        torch.cuda.synchronize()
+        e0.record()
+        for i in range(iters):
+            rt.verify_tokens(*sets[i % NSETS], dev)
+            rt.rollback_verified()
+        e1.record()
+        e1.synchronize()
+        rec["per_query_us" if lossless else "shared_us"] = round(e0.elapsed_time(e1) * 1000.0 / iters, 2)
+        if lossless:
+            rec["union_blocks_last_call"] = int(rt.last_verify_block_ids.numel())
+    del rt
+    return rec
+
+
 # BASELINE config 2: the full model decoding after a 32K prompt
 MODEL_PROMPT, MODEL_CHUNK = 32768, 4096
 C5_PROMPT, C5_STEPS = 131072, 256  # BASELINE config 5 (long context)
@@ -905,6 +942,7 @@ def main():
     if rank == 0 and not args.no_offload:
         offload = offload_measure(nkv, dev)
     store = store_measure(nkv, dev) if rank == 0 else None
+    verify6 = verify6_measure(nkv, dev) if rank == 0 else None
     model = model_c3 = model_c5 = None
     if not args.no_model:
         del graph, g_att, dg
@@ -977,6 +1015,7 @@ def main():
             "prefill": prefill,
             "offload": offload,
             "store": store,
+            "verify6": verify6,
             "kv_head_sharded": sharded,
             "model": model,
             "model_c3": model_c3,

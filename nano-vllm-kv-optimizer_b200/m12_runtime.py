@@ -219,6 +219,12 @@ def _ptr(t) -> int:
     return 0 if t is None else t.data_ptr()
 
 
+def _trimmed(ids_dev: torch.Tensor, count_dev) -> torch.Tensor:
+    """Host copy of device ids, cut to a device-held count when there is one."""
+    ids = ids_dev.cpu()
+    return ids if count_dev is None else ids[:int(count_dev.cpu()[0])]
+
+
 class M12LayerRuntime:
     """Per-layer block-sparse attention runtime (reference m12_runtime.py:169)."""
 
@@ -351,7 +357,8 @@ class M12LayerRuntime:
         self.q_history: list[torch.Tensor] = []
         self._pending_k = None
         self._pending_v = None
-        self._last_verify_dev = self._last_verify_host = None
+        self._last_verify_dev = self._last_verify_host = self._last_verify_count = None
+        self._last_ids_count = None
         self.last_verify_timings: dict = {}
         self.verify_mode = False
         self.verify_lossless = False
@@ -397,16 +404,16 @@ class M12LayerRuntime:
     @property
     def last_block_ids(self):
         if self._last_ids_host is None and self._last_ids_dev is not None:
-            self._last_ids_host = self._last_ids_dev.cpu()
+            self._last_ids_host = _trimmed(self._last_ids_dev, self._last_ids_count)
         return self._last_ids_host
 
     @last_block_ids.setter
     def last_block_ids(self, value):
-        self._last_ids_dev = None
+        self._last_ids_dev = self._last_ids_count = None
         self._last_ids_host = value
 
-    def _set_last_ids(self, ids_dev):
-        self._last_ids_dev = ids_dev
+    def _set_last_ids(self, ids_dev, count_dev=None):
+        self._last_ids_dev, self._last_ids_count = ids_dev, count_dev
         self._last_ids_host = None
 
     @property
@@ -415,12 +422,12 @@ class M12LayerRuntime:
         the device when first read, so that a verify pass does not wait for
         the device."""
         if self._last_verify_host is None and self._last_verify_dev is not None:
-            self._last_verify_host = self._last_verify_dev.cpu()
+            self._last_verify_host = _trimmed(self._last_verify_dev, self._last_verify_count)
         return self._last_verify_host
 
     @last_verify_block_ids.setter
     def last_verify_block_ids(self, value):
-        self._last_verify_dev = None
+        self._last_verify_dev = self._last_verify_count = None
         self._last_verify_host = value
 
     # ------------------------------------------------------------------
@@ -696,7 +703,25 @@ class M12LayerRuntime:
         union_cpu, allowed, _ = self._select_per_query_dev(q, k)
         return union_cpu, allowed
 
+    def _select_per_query_padded(self, q: torch.Tensor, k: int):
+        """The per-query selection without a device wait: the sorted union's
+        ids and allowed mask padded to Tq * k entries (past the union count,
+        block 0 allowed for no query: keys that contribute nothing), and the
+        device-held union count."""
+        written = self._select_per_query_launch(q, k)
+        E = written.shape[1]
+        live = torch.arange(E, device=self.device) < self._union_count  # device-side compare
+        ids = torch.where(live, self._ids[:E], 0)
+        allowed = written.bool() & live
+        return ids, allowed, self._union_count
+
     def _select_per_query_dev(self, q: torch.Tensor, k: int):
+        written = self._select_per_query_launch(q, k)
+        U = int(self._union_count.item())
+        union = self._ids[:U].clone()
+        return union.cpu(), written[:, :U].bool(), union
+
+    def _select_per_query_launch(self, q: torch.Tensor, k: int):
         cfg = self.cfg
         if q.ndim == 2:
             q = q.unsqueeze(0)
@@ -718,9 +743,7 @@ class M12LayerRuntime:
              cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, self.reps_gpu.data_ptr(), cfg.r,
              self.max_blocks, nblocks, prot.data_ptr(), nprot, kk, self._ids.data_ptr(),
              self._union_count.data_ptr(), allowed.data_ptr(), 0, ws.data_ptr(), ws.numel())
-        U = int(self._union_count.item())
-        union = self._ids[:U].clone()
-        return union.cpu(), allowed[:, :U].bool(), union
+        return allowed  # [Tq, Tq * k] dense: the tensor the kernel wrote
 
     # ------------------------------------------------------------------
     # attention launches
@@ -850,8 +873,9 @@ class M12LayerRuntime:
             "quant_history is incompatible with the segmented prefill adapter"
         t0 = perf_counter()
         allowed = None
+        count = None
         if self.verify_lossless:
-            _, allowed, ids = self._select_per_query_dev(q, cfg.top_k_blocks)
+            ids, allowed, count = self._select_per_query_padded(q, cfg.top_k_blocks)
             n_sel = ids.numel()
         else:
             n_sel = self._budget(cfg.top_k_blocks)
@@ -866,8 +890,10 @@ class M12LayerRuntime:
                                     "tokens": int(Tq), "blocks": int(n_sel)}
         self._pending_k = k
         self._pending_v = v
-        self._set_last_ids(ids)
+        count = None if count is None else count.clone()  # the union count of this call
+        self._set_last_ids(ids, count)
         self._last_verify_dev, self._last_verify_host = ids.clone(), None
+        self._last_verify_count = count
         return o
 
     def commit_verified(self, n: int) -> None:
